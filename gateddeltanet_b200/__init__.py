@@ -1,0 +1,262 @@
+"""gateddeltanet_b200 -- B200-native GatedDeltaNet-1.3B decode engine.
+
+The product is libgdn_b200.so (built in-tree by gateddeltanet_b200.build): a
+C-ABI library exporting the reference's decode interface (c_impl/gdn_model.h:
+gdn_model_load, gdn_run_state_init, gdn_decode_step_host, gdn_compute_logits,
+...) over hand-written sm_100a CUDA. This module is a thin ctypes host layer
+over that ABI for Python callers (tests, bench.py); it performs no
+computation of its own and raises if the native library is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Sequence
+
+import numpy as np
+
+__all__ = [
+    "GDNWeightHeader", "GDNLayerWeights", "GDNModel", "GDNRunState", "lib", "make_header",
+    "Model", "RunState", "GDN_WS_OFF_X", "GDN_WS_OFF_X_NORM", "GDN_WS_OFF_LOGITS", "GDN_WS_FLOATS",
+]
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgdn_b200.so")
+
+# Workspace float offsets, c_impl/gdn_model.h:54-75 (same values as include/gdn_model.h).
+GDN_WSF_HID, GDN_WSF_HEAD, GDN_WSF_MLP = 2048, 16, 5632
+GDN_WSF_STATE, GDN_WSF_HEADBUF, GDN_WSF_LOGITS = 12582912, 442368, 32000
+GDN_WS_OFF_X = 0
+GDN_WS_OFF_X_NORM = GDN_WS_OFF_X + GDN_WSF_HID
+GDN_WS_OFF_Q = GDN_WS_OFF_X_NORM + GDN_WSF_HID
+GDN_WS_OFF_K = GDN_WS_OFF_Q + GDN_WSF_HID
+GDN_WS_OFF_V = GDN_WS_OFF_K + GDN_WSF_HID
+GDN_WS_OFF_A = GDN_WS_OFF_V + GDN_WSF_HID
+GDN_WS_OFF_B = GDN_WS_OFF_A + GDN_WSF_HEAD
+GDN_WS_OFF_GATE = GDN_WS_OFF_B + GDN_WSF_HEAD
+GDN_WS_OFF_ATTN = GDN_WS_OFF_GATE + GDN_WSF_HID
+GDN_WS_OFF_TMP_HIDDEN = GDN_WS_OFF_ATTN + GDN_WSF_HID
+GDN_WS_OFF_MLP_GATE = GDN_WS_OFF_TMP_HIDDEN + GDN_WSF_HID
+GDN_WS_OFF_MLP_UP = GDN_WS_OFF_MLP_GATE + GDN_WSF_MLP
+GDN_WS_OFF_REC_STATE = GDN_WS_OFF_MLP_UP + GDN_WSF_MLP
+GDN_WS_OFF_HEAD_BUF = GDN_WS_OFF_REC_STATE + GDN_WSF_STATE
+GDN_WS_OFF_LOGITS = GDN_WS_OFF_HEAD_BUF + GDN_WSF_HEADBUF
+GDN_WS_FLOATS = GDN_WS_OFF_LOGITS + GDN_WSF_LOGITS
+
+
+class GDNWeightHeader(ctypes.Structure):
+    """c_impl/gdn_model.h:30-45 (60 bytes)."""
+    _fields_ = [
+        ("magic", ctypes.c_char * 8), ("version", ctypes.c_uint32), ("vocab_size", ctypes.c_uint32),
+        ("hidden_size", ctypes.c_uint32), ("num_layers", ctypes.c_uint32), ("num_heads", ctypes.c_uint32),
+        ("num_v_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32), ("intermediate_size", ctypes.c_uint32),
+        ("conv_size", ctypes.c_uint32), ("max_seq_len", ctypes.c_uint32), ("bos_token_id", ctypes.c_int32),
+        ("eos_token_id", ctypes.c_int32), ("norm_eps", ctypes.c_float),
+    ]
+
+
+_FP = ctypes.POINTER(ctypes.c_float)
+
+
+class GDNLayerWeights(ctypes.Structure):
+    """c_impl/gdn_model.h:123-142."""
+    _fields_ = [(n, _FP) for n in (
+        "attn_norm", "a_log", "dt_bias", "q_proj", "k_proj", "v_proj", "a_proj", "b_proj", "q_conv", "k_conv",
+        "v_conv", "g_proj", "o_norm", "o_proj", "mlp_norm", "mlp_gate_proj", "mlp_up_proj", "mlp_down_proj")]
+
+
+class GDNModel(ctypes.Structure):
+    """c_impl/gdn_model.h:144-151."""
+    _fields_ = [("config", GDNWeightHeader), ("weight_data", _FP), ("layers", ctypes.POINTER(GDNLayerWeights)),
+                ("embeddings", _FP), ("final_norm", _FP), ("lm_head", _FP)]
+
+
+class GDNRunState(ctypes.Structure):
+    """c_impl/gdn_model.h:153-160."""
+    _fields_ = [("workspace", ctypes.c_void_p), ("x", _FP), ("recurrent_state", _FP), ("head_buffer", _FP),
+                ("weight_shards", ctypes.c_void_p * 32), ("aux_weights", ctypes.c_void_p)]
+
+
+assert ctypes.sizeof(GDNWeightHeader) == 60
+
+_LIB: Optional[ctypes.CDLL] = None
+
+# (name, restype, argtypes) of every entry point declared in include/gdn_model.h and include/gdn_b200.h
+EXPORTS = [
+    ("gdn_model_load", ctypes.c_int, [ctypes.POINTER(GDNModel), ctypes.c_char_p]),
+    ("gdn_model_free", None, [ctypes.POINTER(GDNModel)]),
+    ("gdn_run_state_init", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.POINTER(GDNModel), ctypes.c_uint32]),
+    ("gdn_run_state_free", None, [ctypes.POINTER(GDNRunState)]),
+    ("gdn_decode_step_host", ctypes.c_int,
+     [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32)]),
+    ("gdn_compute_logits", None, [ctypes.POINTER(GDNModel), _FP, _FP]),
+    ("gdn_native_bf16_mul_to_fp32", ctypes.c_float, [ctypes.c_uint16, ctypes.c_uint16]),
+    ("gdn_set_native_debug_buffers", None, [_FP, _FP]),
+    ("gdn_reset_mixed_mul_stats", None, []),
+    ("gdn_get_mixed_mul_stats", None, None),  # returns a struct; argtypes set below
+    ("gdn_b200_set_device", ctypes.c_int, [ctypes.c_int]),
+    ("gdn_b200_last_error", ctypes.c_char_p, []),
+    ("gdn_b200_model_synth", ctypes.c_int, [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNWeightHeader), ctypes.c_uint64]),
+    ("gdn_b200_model_save", ctypes.c_int, [ctypes.POINTER(GDNModel), ctypes.c_char_p]),
+    ("gdn_b200_set_boundary", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int]),
+    ("gdn_b200_state_upload", ctypes.c_int, [ctypes.POINTER(GDNRunState), _FP, ctypes.c_size_t, _FP, ctypes.c_size_t]),
+    ("gdn_b200_state_download", ctypes.c_int, [ctypes.POINTER(GDNRunState), _FP, ctypes.c_size_t, _FP, ctypes.c_size_t]),
+    ("gdn_b200_state_load_file", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32)]),
+    ("gdn_b200_state_save_file", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_char_p, ctypes.c_int32]),
+    ("gdn_b200_fetch_outputs", ctypes.c_int, [ctypes.POINTER(GDNRunState), _FP, _FP]),
+    ("gdn_b200_decode_tokens", ctypes.c_int,
+     [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32,
+      ctypes.c_int, ctypes.POINTER(ctypes.c_int32), _FP]),
+    ("gdn_b200_grid_size", ctypes.c_int, []),
+]
+
+
+class GDNMixedMulStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in ("calls", "special_inputs", "flushed_inputs", "flushed_outputs", "overflows")]
+
+
+def lib(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load libgdn_b200.so; raises if it has not been built (no fallback)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise RuntimeError(f"libgdn_b200.so not found at {path}: run `python -m gateddeltanet_b200.build`")
+    L = ctypes.CDLL(path)
+    for name, res, args in EXPORTS:
+        fn = getattr(L, name)
+        if name == "gdn_get_mixed_mul_stats":
+            fn.restype, fn.argtypes = GDNMixedMulStats, []
+            continue
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = L
+    return L
+
+
+def last_error() -> str:
+    return lib().gdn_b200_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what} failed: {last_error()}")
+
+
+def make_header(vocab=32000, hidden=2048, layers=24, heads=8, head_dim=256, inter=5632, conv=4,
+                max_seq_len=2048, eps=1e-6, bos=1, eos=2) -> GDNWeightHeader:
+    """A .gdnw header (the 1.3B shape by default, c_impl/artifacts/gdn-1.3b-bf16w.json)."""
+    return GDNWeightHeader(b"GDNWv1\0\0", 1, vocab, hidden, layers, heads, heads, head_dim, inter, conv,
+                           max_seq_len, bos, eos, eps)
+
+
+def _fptr(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_FP)
+
+
+class Model:
+    """A loaded (or seeded synthetic) model: GDNModel plus its device image."""
+
+    def __init__(self, path: Optional[str] = None, header: Optional[GDNWeightHeader] = None, seed: int = 1234):
+        self.lib = lib()
+        self.m = GDNModel()
+        if path is not None:
+            check(self.lib.gdn_model_load(ctypes.byref(self.m), path.encode()), "gdn_model_load")
+        else:
+            hdr = header if header is not None else make_header()
+            check(self.lib.gdn_b200_model_synth(ctypes.byref(self.m), ctypes.byref(hdr), seed), "gdn_b200_model_synth")
+
+    @property
+    def config(self) -> GDNWeightHeader:
+        return self.m.config
+
+    def save(self, path: str) -> None:
+        check(self.lib.gdn_b200_model_save(ctypes.byref(self.m), path.encode()), "gdn_b200_model_save")
+
+    def compute_logits(self, hidden: np.ndarray) -> np.ndarray:
+        out = np.empty(self.config.vocab_size, dtype=np.float32)
+        h = np.ascontiguousarray(hidden, dtype=np.float32)
+        self.lib.gdn_compute_logits(ctypes.byref(self.m), _fptr(h), _fptr(out))
+        return out
+
+    def free(self) -> None:
+        if self.m.weight_data:
+            self.lib.gdn_model_free(ctypes.byref(self.m))
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class RunState:
+    """One decode stream (GDNRunState) of a Model."""
+
+    def __init__(self, model: Model, max_tokens: Optional[int] = None):
+        self.model = model
+        self.lib = model.lib
+        self.s = GDNRunState()
+        mt = model.config.max_seq_len if max_tokens is None else max_tokens
+        check(self.lib.gdn_run_state_init(ctypes.byref(self.s), ctypes.byref(model.m), mt), "gdn_run_state_init")
+        c = model.config
+        self.rec_floats = c.num_layers * c.num_heads * c.head_dim * c.head_dim
+        self.conv_floats = c.num_layers * 3 * (c.conv_size - 1) * c.hidden_size
+
+    def workspace(self, offset: int, count: int) -> np.ndarray:
+        ptr = ctypes.cast(self.s.workspace, _FP)
+        return np.ctypeslib.as_array(ptr, shape=(GDN_WS_FLOATS,))[offset:offset + count]
+
+    def step(self, token: int) -> int:
+        """gdn_decode_step_host; returns the kernel's greedy token (workspace[X_NORM] lane 0)."""
+        t = ctypes.c_int32(int(token))
+        check(self.lib.gdn_decode_step_host(ctypes.byref(self.model.m), ctypes.byref(self.s), ctypes.byref(t)),
+              "gdn_decode_step_host")
+        return int(self.workspace(GDN_WS_OFF_X_NORM, 1)[0])
+
+    def decode(self, tokens: Sequence[int], greedy: bool = False):
+        """Device-resident loop; returns (argmax per step, device ms for all steps)."""
+        tok = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        n = len(tok)
+        out = np.empty(n, dtype=np.int32)
+        ms = ctypes.c_float(0.0)
+        check(self.lib.gdn_b200_decode_tokens(ctypes.byref(self.model.m), ctypes.byref(self.s),
+                                              tok.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n, int(greedy),
+                                              out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ctypes.byref(ms)),
+              "gdn_b200_decode_tokens")
+        return out, float(ms.value)
+
+    def outputs(self):
+        c = self.model.config
+        logits = np.empty(c.vocab_size, dtype=np.float32)
+        hidden = np.empty(c.hidden_size, dtype=np.float32)
+        check(self.lib.gdn_b200_fetch_outputs(ctypes.byref(self.s), _fptr(logits), _fptr(hidden)),
+              "gdn_b200_fetch_outputs")
+        return logits, hidden
+
+    def set_boundary(self, bf16: bool) -> None:
+        check(self.lib.gdn_b200_set_boundary(ctypes.byref(self.s), int(bool(bf16))), "gdn_b200_set_boundary")
+
+    def load_state(self, rec: np.ndarray, conv: np.ndarray) -> None:
+        rec = np.ascontiguousarray(rec, dtype=np.float32)
+        conv = np.ascontiguousarray(conv, dtype=np.float32)
+        check(self.lib.gdn_b200_state_upload(ctypes.byref(self.s), _fptr(rec), rec.size, _fptr(conv), conv.size),
+              "gdn_b200_state_upload")
+
+    def read_state(self):
+        rec = np.empty(self.rec_floats, dtype=np.float32)
+        conv = np.empty(self.conv_floats, dtype=np.float32)
+        check(self.lib.gdn_b200_state_download(ctypes.byref(self.s), _fptr(rec), rec.size, _fptr(conv), conv.size),
+              "gdn_b200_state_download")
+        return rec, conv
+
+    def free(self) -> None:
+        if self.s.workspace:
+            self.lib.gdn_run_state_free(ctypes.byref(self.s))
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

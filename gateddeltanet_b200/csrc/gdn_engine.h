@@ -1,0 +1,98 @@
+/* Internal interface between the C-ABI host layer (gdn_host.cu) and the
+ * decode kernel (gdn_decode.cu). Not installed; callers use include/gdn_model.h
+ * and include/gdn_b200.h.
+ *
+ * Device image of one model (all pointers device memory, built once per
+ * GDNModel and shared by every run state):
+ *   per layer l, at wimg + l * layer_stride bytes, BF16 row-major [out][in]:
+ *     QKVGAB  [4H + 2nh][H]   rows q | k | v | g | a_proj | b_proj
+ *     O       [H][H]          at + off_o
+ *     GU      [2I][H]         at + off_gu, gate row i at 2i, up row i at 2i+1
+ *     DOWN    [H][I]          at + off_down
+ *   LM head  [V][H] BF16 at w_lm;   embeddings [V][H] BF16 at emb.
+ *   aux FP32 per layer at aux + l * aux_stride floats:
+ *     attn_norm[H] | o_norm[256] | mlp_norm[H] | conv_w[3][H][4] | a_log[nh] | dt_bias[nh]
+ *   final_norm[H] FP32 at aux + L * aux_stride.
+ * Per decode stream (run state):
+ *   S      FP32 [L][nh][256 (v)][256 (k)]  -- column v of a head's S[k][v]
+ *          is 1 KB contiguous, so a CTA's share of columns is one range
+ *   tails  FP32 [L][3 (q,k,v)][H][4]       -- rows 0..2 of the conv window
+ *          (row 2 newest) plus one pad lane, one 16-byte vector per channel
+ */
+#ifndef GDN_ENGINE_H
+#define GDN_ENGINE_H
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace gdn {
+
+constexpr int kHeadDim = 256;
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;      /* + one producer warp */
+constexpr int kSlotBytes = 16384;
+constexpr int kSlots = 12;
+constexpr int kMaxRowsPerChunk = 4;
+constexpr int kColsPerChunk = 2;
+constexpr int kPhasesPerLayer = 5;
+
+/* error codes written to DecodeStatus.err */
+enum {
+    kErrNone = 0,
+    kErrBarrierTimeout = 1,
+    kErrChunkTimeout = 2,
+    kErrSlotTimeout = 3,
+    kErrAborted = 4,
+    kErrBadToken = 5,
+};
+
+/* Small device-side status block; its first 64 bytes mirror the ABI's
+ * workspace[X_NORM] line (lane 0 = token id as a float). */
+struct DecodeStatus {
+    float token_line[16];
+    int32_t token;
+    int32_t err;
+    uint32_t err_cta;
+    uint32_t err_where;
+    uint32_t bar;         /* grid barrier counter (monotonic) */
+    uint32_t done;        /* LM-head ticket counter, reset by the last CTA */
+    uint32_t pad[10];
+};
+
+struct DecodeParams {
+    /* shape */
+    int H, I, V, L, nh;
+    float eps;
+    int bf16_boundary;   /* 1: round activations to BF16 at operator boundaries */
+    /* weights */
+    const uint8_t *wimg;
+    size_t layer_stride, off_o, off_gu, off_down;
+    const uint8_t *w_lm;
+    const uint16_t *emb;
+    const float *aux;
+    size_t aux_stride;
+    /* stream state */
+    float *S;
+    float *tails;
+    /* activations */
+    float *x_in, *x_mid, *y_o, *y_down, *qkv, *gate, *ab, *attn, *m, *logits, *hidden_out;
+    const float *x_embed;      /* FP32 embedding row, used when token_src == nullptr */
+    const int32_t *token_src;  /* device token id: gather the embedding row on device */
+    float *cand_val;
+    int32_t *cand_idx;
+    int32_t *token_out;        /* optional: receives the step's argmax token */
+    DecodeStatus *status;
+    uint32_t bar_base;         /* status->bar at launch */
+};
+
+/* Number of grid barriers one launch performs. */
+inline uint32_t barriers_per_launch(int L) { return (uint32_t)(L * kPhasesPerLayer); }
+
+size_t decode_smem_bytes(int H, int I);
+cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t stream);
+
+}  // namespace gdn
+
+#endif

@@ -1,0 +1,895 @@
+/* gdn_host.cu -- the C ABI of libgdn_b200.so (include/gdn_model.h,
+ * include/gdn_b200.h): model loading, the shared device weight image, decode
+ * streams (run states) and the host-side checks.
+ *
+ * Reference behaviour kept (c_impl/gdn_model.cpp unless noted):
+ *   gdn_model_load          header checks :1082-1100, BF16-exact words :1190-1216
+ *   gdn_run_state_init      max_tokens range :1247-1252
+ *   gdn_decode_step_host    token range :3900-3905, embedding row -> workspace[X]
+ *   token line              workspace[X_NORM] lane 0 = argmax as float :3873-3877
+ *   gdn_compute_logits      scalar LM head with BF16 product rounding :3930-3975
+ *   .gdnstate               c_impl/gdn_eval.cpp:202-267, c_impl/host.cpp:675-735
+ */
+#include "gdn_engine.h"
+#include "gdn_synth.h"
+
+#include "../../include/gdn_b200.h"
+#include "../../include/gdn_model.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local int g_device = 0;
+
+int fail(const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    fprintf(stderr, "%s\n", buf);
+    return -1;
+}
+
+#define CUDA_OK(call)                                                                        \
+    do {                                                                                     \
+        cudaError_t e_ = (call);                                                             \
+        if (e_ != cudaSuccess) return fail("gdn_b200: %s failed: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+constexpr size_t kHeaderBytes = 60;
+
+static_assert(sizeof(GDNWeightHeader) == kHeaderBytes, "GDNWeightHeader must be 60 bytes");
+
+inline uint32_t f2u(float v) { uint32_t b; memcpy(&b, &v, 4); return b; }
+inline float u2f(uint32_t b) { float v; memcpy(&v, &b, 4); return v; }
+
+int hw_threads() {
+    unsigned n = std::thread::hardware_concurrency();
+    if (n == 0) n = 4;
+    return (int)std::min(n, 64u);
+}
+
+template <typename F>
+void parallel_for(size_t n, F fn) {
+    const int t = (int)std::min<size_t>((size_t)hw_threads(), n ? n : 1);
+    if (t <= 1) { fn((size_t)0, n); return; }
+    std::vector<std::thread> th;
+    for (int i = 0; i < t; ++i) {
+        const size_t b = n * (size_t)i / (size_t)t, e = n * (size_t)(i + 1) / (size_t)t;
+        th.emplace_back([=] { fn(b, e); });
+    }
+    for (auto &x : th) x.join();
+}
+
+/* ------------------------------------------------------- blob geometry */
+
+size_t layer_floats(const GDNWeightHeader &c) {
+    const size_t H = c.hidden_size, nh = c.num_heads, hd = c.head_dim, I = c.intermediate_size, cs = c.conv_size;
+    return H + 2 * nh + 3 * H * H + 2 * nh * H + 3 * H * cs + H * H + hd + H * H + H + 2 * I * H + H * I;
+}
+size_t total_floats(const GDNWeightHeader &c) {
+    return (size_t)c.vocab_size * c.hidden_size + (size_t)c.num_layers * layer_floats(c) + c.hidden_size +
+           (size_t)c.vocab_size * c.hidden_size;
+}
+
+/* gdn_validate_config, c_impl/gdn_model.cpp:1082-1100 */
+int validate_config(const GDNWeightHeader &c) {
+    if (memcmp(c.magic, "GDNWv1", 6) != 0 || c.version != 1) return fail("unsupported weight file");
+    if (c.num_heads != c.num_v_heads) return fail("expected num_heads == num_v_heads");
+    if (c.hidden_size != c.num_heads * c.head_dim) return fail("expected hidden_size == num_heads * head_dim");
+    return 0;
+}
+
+/* gdn_assign_weight_views, c_impl/gdn_model.cpp:1102-1159 (same blob order) */
+void assign_views(GDNModel *m) {
+    const GDNWeightHeader &c = m->config;
+    const size_t H = c.hidden_size, nh = c.num_heads, hd = c.head_dim, I = c.intermediate_size, cs = c.conv_size;
+    float *p = m->weight_data;
+    m->embeddings = p;
+    p += (size_t)c.vocab_size * H;
+    for (uint32_t l = 0; l < c.num_layers; ++l) {
+        GDNLayerWeights *w = &m->layers[l];
+        w->attn_norm = p; p += H;
+        w->a_log = p; p += nh;
+        w->dt_bias = p; p += nh;
+        w->q_proj = p; p += H * H;
+        w->k_proj = p; p += H * H;
+        w->v_proj = p; p += H * H;
+        w->a_proj = p; p += nh * H;
+        w->b_proj = p; p += nh * H;
+        w->q_conv = p; p += H * cs;
+        w->k_conv = p; p += H * cs;
+        w->v_conv = p; p += H * cs;
+        w->g_proj = p; p += H * H;
+        w->o_norm = p; p += hd;
+        w->o_proj = p; p += H * H;
+        w->mlp_norm = p; p += H;
+        w->mlp_gate_proj = p; p += I * H;
+        w->mlp_up_proj = p; p += I * H;
+        w->mlp_down_proj = p; p += H * I;
+    }
+    m->final_norm = p;
+    p += H;
+    m->lm_head = p;
+}
+
+/* Shape limits of this engine (beyond the reference's own header checks). */
+int engine_supports(const GDNWeightHeader &c) {
+    const uint32_t H = c.hidden_size, I = c.intermediate_size;
+    if (c.head_dim != 256) return fail("gdn_b200: head_dim must be 256 (got %u)", c.head_dim);
+    if (c.conv_size != 4) return fail("gdn_b200: conv_size must be 4 (got %u)", c.conv_size);
+    if (H % 256 || I % 256 || H == 0 || I == 0) return fail("gdn_b200: hidden and intermediate must be multiples of 256");
+    if (c.num_heads > 8 || H > GDN_WSF_HID) return fail("gdn_b200: at most 8 heads (hidden <= 2048)");
+    if (I > GDN_WSF_MLP || c.vocab_size > GDN_WSF_LOGITS || c.vocab_size == 0)
+        return fail("gdn_b200: intermediate/vocab exceed the workspace ABI");
+    if ((size_t)c.num_layers * c.num_heads * 256 * 256 > GDN_WSF_STATE ||
+        (size_t)c.num_layers * 3 * 3 * H > GDN_WSF_HEADBUF || c.num_layers == 0)
+        return fail("gdn_b200: layer count exceeds the workspace ABI");
+    return 0;
+}
+
+/* ------------------------------------------------- device weight image */
+
+struct DeviceModel {
+    int device = 0;
+    int refs = 0;
+    GDNWeightHeader cfg;
+    uint8_t *wimg = nullptr;
+    size_t layer_stride = 0, off_o = 0, off_gu = 0, off_down = 0;
+    uint8_t *w_lm = nullptr;
+    uint16_t *emb = nullptr;
+    float *aux = nullptr;
+    size_t aux_stride = 0;
+    bool model_alive = true;
+};
+
+std::mutex g_mu;
+std::map<const float *, DeviceModel *> g_models;  /* keyed by GDNModel.weight_data */
+
+inline uint16_t hi16(float v) { return (uint16_t)(f2u(v) >> 16); }
+
+void free_device_model(DeviceModel *dm) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(dm->device);
+    cudaFree(dm->wimg);
+    cudaFree(dm->w_lm);
+    cudaFree(dm->emb);
+    cudaFree(dm->aux);
+    cudaSetDevice(prev);
+    delete dm;
+}
+
+/* Upload n BF16 values produced by fill(dst, begin, end) through a pinned
+ * staging buffer. */
+template <typename F>
+int upload_bf16(uint16_t *dst, size_t n, F fill) {
+    const size_t chunk = (size_t)64 << 20;  /* values per staging pass */
+    uint16_t *stage = nullptr;
+    CUDA_OK(cudaMallocHost(&stage, std::min(n, chunk) * 2));
+    for (size_t b = 0; b < n; b += chunk) {
+        const size_t e = std::min(n, b + chunk);
+        parallel_for(e - b, [&](size_t lo, size_t hi) { fill(stage, b + lo, b + hi, lo); });
+        const cudaError_t err = cudaMemcpy(dst + b, stage, (e - b) * 2, cudaMemcpyHostToDevice);
+        if (err != cudaSuccess) {
+            cudaFreeHost(stage);
+            return fail("gdn_b200: weight upload failed: %s", cudaGetErrorString(err));
+        }
+    }
+    cudaFreeHost(stage);
+    return 0;
+}
+
+DeviceModel *build_device_model(const GDNModel *model) {
+    const GDNWeightHeader &c = model->config;
+    const size_t H = c.hidden_size, nh = c.num_heads, I = c.intermediate_size, V = c.vocab_size, L = c.num_layers;
+    DeviceModel *dm = new DeviceModel();
+    dm->cfg = c;
+    dm->device = g_device;
+    const size_t rows_a = 4 * H + 2 * nh;
+    dm->off_o = rows_a * H * 2;
+    dm->off_gu = dm->off_o + H * H * 2;
+    dm->off_down = dm->off_gu + 2 * I * H * 2;
+    dm->layer_stride = ((dm->off_down + H * I * 2) + 255) & ~(size_t)255;
+    dm->aux_stride = (14 * H + 256 + 2 * nh + 3) & ~(size_t)3;
+    if (cudaMalloc(&dm->wimg, dm->layer_stride * L) != cudaSuccess || cudaMalloc(&dm->w_lm, V * H * 2) != cudaSuccess ||
+        cudaMalloc(&dm->emb, V * H * 2) != cudaSuccess ||
+        cudaMalloc(&dm->aux, (dm->aux_stride * L + H) * sizeof(float)) != cudaSuccess) {
+        fail("gdn_b200: device weight image allocation failed (%.2f GB)",
+             (double)(dm->layer_stride * L + 2 * V * H * 2) / 1e9);
+        free_device_model(dm);
+        return nullptr;
+    }
+    /* per layer: QKVGAB, O, GU (interleaved), DOWN, as one contiguous range */
+    for (size_t l = 0; l < L; ++l) {
+        const GDNLayerWeights &w = model->layers[l];
+        uint16_t *base = reinterpret_cast<uint16_t *>(dm->wimg + l * dm->layer_stride);
+        const size_t n = dm->off_down / 2 + H * I;
+        const int rc = upload_bf16(base, n, [&](uint16_t *st, size_t b, size_t e, size_t so) {
+            for (size_t i = b; i < e; ++i) {
+                float v;
+                if (i < rows_a * H) {
+                    const size_t r = i / H, col = i % H;
+                    const float *src;
+                    if (r < H) src = w.q_proj + r * H;
+                    else if (r < 2 * H) src = w.k_proj + (r - H) * H;
+                    else if (r < 3 * H) src = w.v_proj + (r - 2 * H) * H;
+                    else if (r < 4 * H) src = w.g_proj + (r - 3 * H) * H;
+                    else if (r < 4 * H + nh) src = w.a_proj + (r - 4 * H) * H;
+                    else src = w.b_proj + (r - 4 * H - nh) * H;
+                    v = src[col];
+                } else if (i < dm->off_gu / 2) {
+                    v = w.o_proj[i - dm->off_o / 2];
+                } else if (i < dm->off_down / 2) {
+                    const size_t j = i - dm->off_gu / 2, r = j / H, col = j % H;
+                    v = ((r & 1) ? w.mlp_up_proj : w.mlp_gate_proj)[(r >> 1) * H + col];
+                } else {
+                    v = w.mlp_down_proj[i - dm->off_down / 2];
+                }
+                st[so + (i - b)] = hi16(v);
+            }
+        });
+        if (rc != 0) { free_device_model(dm); return nullptr; }
+    }
+    if (upload_bf16(reinterpret_cast<uint16_t *>(dm->w_lm), V * H,
+                    [&](uint16_t *st, size_t b, size_t e, size_t so) {
+                        for (size_t i = b; i < e; ++i) st[so + (i - b)] = hi16(model->lm_head[i]);
+                    }) != 0 ||
+        upload_bf16(dm->emb, V * H, [&](uint16_t *st, size_t b, size_t e, size_t so) {
+            for (size_t i = b; i < e; ++i) st[so + (i - b)] = hi16(model->embeddings[i]);
+        }) != 0) {
+        free_device_model(dm);
+        return nullptr;
+    }
+    /* aux (FP32): attn_norm | o_norm | mlp_norm | conv_w[3][H][4] | a_log | dt_bias, then final_norm */
+    std::vector<float> aux(dm->aux_stride * L + H, 0.0f);
+    for (size_t l = 0; l < L; ++l) {
+        const GDNLayerWeights &w = model->layers[l];
+        float *a = aux.data() + l * dm->aux_stride;
+        memcpy(a, w.attn_norm, H * 4);
+        memcpy(a + H, w.o_norm, 256 * 4);
+        memcpy(a + H + 256, w.mlp_norm, H * 4);
+        memcpy(a + 2 * H + 256, w.q_conv, H * 4 * 4);
+        memcpy(a + 6 * H + 256, w.k_conv, H * 4 * 4);
+        memcpy(a + 10 * H + 256, w.v_conv, H * 4 * 4);
+        memcpy(a + 14 * H + 256, w.a_log, nh * 4);
+        memcpy(a + 14 * H + 256 + nh, w.dt_bias, nh * 4);
+    }
+    memcpy(aux.data() + dm->aux_stride * L, model->final_norm, H * 4);
+    if (cudaMemcpy(dm->aux, aux.data(), aux.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        fail("gdn_b200: aux upload failed");
+        free_device_model(dm);
+        return nullptr;
+    }
+    return dm;
+}
+
+/* ------------------------------------------------------- decode streams */
+
+struct Stream {
+    DeviceModel *dm = nullptr;
+    int device = 0;
+    int grid = 0;
+    int bf16_boundary = 1;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float *S = nullptr, *tails = nullptr, *acts = nullptr;
+    float *x_in, *x_mid, *y_o, *y_down, *qkv, *gate, *ab, *attn, *m, *logits, *hidden, *x_embed, *cand_val;
+    int32_t *cand_idx = nullptr;
+    gdn::DecodeStatus *status = nullptr;
+    gdn::DecodeStatus *status_host = nullptr;
+    int32_t *tokens = nullptr, *argmax = nullptr;
+    size_t tokens_cap = 0;
+    uint32_t bar = 0;
+    float *ws = nullptr;  /* pinned ABI workspace (host) */
+};
+
+std::map<const void *, Stream *> g_streams;  /* keyed by GDNRunState.workspace */
+
+float *g_debug_hidden = nullptr;
+float *g_debug_logits = nullptr;
+
+Stream *find_stream(GDNRunState *state) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    auto it = g_streams.find(state ? (const void *)state->workspace : nullptr);
+    return it == g_streams.end() ? nullptr : it->second;
+}
+
+gdn::DecodeParams make_params(const Stream &s) {
+    const DeviceModel &dm = *s.dm;
+    gdn::DecodeParams p;
+    memset(&p, 0, sizeof(p));
+    p.H = (int)dm.cfg.hidden_size;
+    p.I = (int)dm.cfg.intermediate_size;
+    p.V = (int)dm.cfg.vocab_size;
+    p.L = (int)dm.cfg.num_layers;
+    p.nh = (int)dm.cfg.num_heads;
+    p.eps = dm.cfg.norm_eps;
+    p.bf16_boundary = s.bf16_boundary;
+    p.wimg = dm.wimg;
+    p.layer_stride = dm.layer_stride;
+    p.off_o = dm.off_o;
+    p.off_gu = dm.off_gu;
+    p.off_down = dm.off_down;
+    p.w_lm = dm.w_lm;
+    p.emb = dm.emb;
+    p.aux = dm.aux;
+    p.aux_stride = dm.aux_stride;
+    p.S = s.S;
+    p.tails = s.tails;
+    p.x_in = s.x_in;
+    p.x_mid = s.x_mid;
+    p.y_o = s.y_o;
+    p.y_down = s.y_down;
+    p.qkv = s.qkv;
+    p.gate = s.gate;
+    p.ab = s.ab;
+    p.attn = s.attn;
+    p.m = s.m;
+    p.logits = s.logits;
+    p.hidden_out = s.hidden;
+    p.x_embed = s.x_embed;
+    p.token_src = nullptr;
+    p.cand_val = s.cand_val;
+    p.cand_idx = s.cand_idx;
+    p.token_out = nullptr;
+    p.status = s.status;
+    p.bar_base = s.bar;
+    return p;
+}
+
+int launch(Stream &s, gdn::DecodeParams &p) {
+    p.bar_base = s.bar;
+    const cudaError_t e = gdn::launch_decode(p, s.grid, s.stream);
+    if (e != cudaSuccess) return fail("gdn_b200: decode launch failed: %s", cudaGetErrorString(e));
+    s.bar += gdn::barriers_per_launch(p.L) * (uint32_t)s.grid;
+    return 0;
+}
+
+/* After a synchronised step: read the status block and recover from a
+ * kernel-reported error (the counters are reset so the stream stays usable). */
+int check_status(Stream &s) {
+    if (s.status_host->err == gdn::kErrNone) return 0;
+    const int err = s.status_host->err;
+    const unsigned cta = s.status_host->err_cta, where = s.status_host->err_where;
+    cudaMemsetAsync(s.status, 0, sizeof(gdn::DecodeStatus), s.stream);
+    cudaStreamSynchronize(s.stream);
+    s.bar = 0;
+    static const char *names[] = {"none", "grid barrier timeout", "chunk wait timeout", "ring slot timeout",
+                                  "aborted", "token id out of range"};
+    return fail("gdn_b200: decode kernel reported %s (cta %u, at %u)", names[err >= 0 && err <= 5 ? err : 4], cta,
+                where);
+}
+
+int sync_and_check(Stream &s) {
+    cudaError_t e = cudaMemcpyAsync(s.status_host, s.status, sizeof(gdn::DecodeStatus), cudaMemcpyDeviceToHost,
+                                    s.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s.stream);
+    if (e != cudaSuccess) return fail("gdn_b200: decode step failed: %s", cudaGetErrorString(e));
+    return check_status(s);
+}
+
+/* BF16 x BF16 -> BF16 product with DAZ/FTZ, the reference's GEMV product
+ * contract (c_impl/gdn_model.cpp:392-462), as FP32 bits. */
+uint32_t native_product_bits(uint16_t lhs, uint16_t rhs) {
+    const uint32_t le = (lhs >> 7) & 0xffu, re = (rhs >> 7) & 0xffu;
+    const bool lnan = le == 0xffu && (lhs & 0x7fu), rnan = re == 0xffu && (rhs & 0x7fu);
+    const bool linf = le == 0xffu && !(lhs & 0x7fu), rinf = re == 0xffu && !(rhs & 0x7fu);
+    const bool lz = le == 0, rz = re == 0;
+    const uint32_t sign = (uint32_t)((lhs ^ rhs) & 0x8000u);
+    if (lnan || rnan || (linf && rz) || (rinf && lz)) return 0x7fc00000u;
+    if (linf || rinf) return (sign | 0x7f80u) << 16;
+    if (lz || rz) return sign << 16;
+    volatile float prod = u2f((uint32_t)lhs << 16) * u2f((uint32_t)rhs << 16);
+    const uint32_t pb = f2u(prod), mag = pb & 0x7fffffffu;
+    if (mag == 0x7f800000u) return pb & 0xffff0000u;
+    if (mag < 0x007fc000u) return pb & 0x80000000u;
+    const uint32_t res = ((pb + 0x7fffu + ((pb >> 16) & 1u)) >> 16) & 0xffffu;
+    if ((res & 0x7f80u) == 0) return (res & 0x8000u) << 16;
+    return res << 16;
+}
+
+uint16_t bf16_rne_bits(float v) {
+    const uint32_t b = f2u(v), mag = b & 0x7fffffffu;
+    if (mag >= 0x7f800000u) {
+        if (mag == 0x7f800000u) return (uint16_t)(b >> 16);
+        return (uint16_t)((b & 0x80000000u) ? 0xffc0u : 0x7fc0u);
+    }
+    return (uint16_t)((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+}
+
+}  // namespace
+
+/* ================================================================ C ABI */
+
+extern "C" {
+
+int gdn_b200_set_device(int device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n)
+        return fail("gdn_b200: no CUDA device %d", device);
+    g_device = device;
+    CUDA_OK(cudaSetDevice(device));
+    return 0;
+}
+
+const char *gdn_b200_last_error(void) { return g_last_error.c_str(); }
+
+int gdn_b200_grid_size(void) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, g_device) != cudaSuccess) return -1;
+    return sms;
+}
+
+int gdn_model_load(GDNModel *model, const char *path) {
+    memset(model, 0, sizeof(*model));
+    FILE *f = fopen(path, "rb");
+    if (f == nullptr) return fail("fopen weights: %s", path);
+    if (fread(&model->config, 1, kHeaderBytes, f) != kHeaderBytes) {
+        fclose(f);
+        return fail("failed to read weight header");
+    }
+    if (validate_config(model->config) != 0) { fclose(f); return -1; }
+    const size_t n = total_floats(model->config);
+    model->weight_data = (float *)malloc(n * sizeof(float));
+    model->layers = (GDNLayerWeights *)calloc(model->config.num_layers, sizeof(GDNLayerWeights));
+    if (model->weight_data == nullptr || model->layers == nullptr) {
+        fclose(f);
+        gdn_model_free(model);
+        return fail("malloc failed");
+    }
+    /* Read in chunks and validate each chunk's BF16-exactness while reading
+     * (c_impl/gdn_model.cpp:1190-1216), so a non-BF16 blob fails early. */
+    const size_t chunk = (size_t)64 << 20;
+    for (size_t b = 0; b < n; b += chunk) {
+        const size_t req = std::min(chunk, n - b);
+        if (fread(model->weight_data + b, sizeof(float), req, f) != req) {
+            fclose(f);
+            gdn_model_free(model);
+            return fail("failed to read weight payload");
+        }
+        std::atomic<size_t> bad{(size_t)-1};
+        const float *w = model->weight_data + b;
+        parallel_for(req, [&](size_t lo, size_t hi) {
+            for (size_t i = lo; i < hi; ++i)
+                if (f2u(w[i]) & 0xffffu) {
+                    size_t cur = bad.load();
+                    while (i < cur && !bad.compare_exchange_weak(cur, i)) {
+                    }
+                    return;
+                }
+        });
+        if (bad.load() != (size_t)-1) {
+            const size_t i = b + bad.load();
+            fclose(f);
+            fail("gdn: weight %zu is not BF16-exact (bits=0x%08x)", i, f2u(model->weight_data[i]));
+            gdn_model_free(model);
+            return fail("dense packing requires a BF16-exact FP32-word checkpoint");
+        }
+    }
+    fclose(f);
+    assign_views(model);
+    return 0;
+}
+
+int gdn_b200_model_synth(GDNModel *model, const GDNWeightHeader *config, uint64_t seed) {
+    memset(model, 0, sizeof(*model));
+    model->config = *config;
+    if (validate_config(model->config) != 0) return -1;
+    const GDNWeightHeader &c = model->config;
+    const size_t n = total_floats(c);
+    model->weight_data = (float *)malloc(n * sizeof(float));
+    model->layers = (GDNLayerWeights *)calloc(c.num_layers, sizeof(GDNLayerWeights));
+    if (model->weight_data == nullptr || model->layers == nullptr) {
+        gdn_model_free(model);
+        return fail("malloc failed");
+    }
+    /* tensor table in blob order */
+    struct T { size_t off, size; uint32_t id; };
+    std::vector<T> tensors;
+    const size_t H = c.hidden_size, nh = c.num_heads, hd = c.head_dim, I = c.intermediate_size, cs = c.conv_size;
+    const size_t sizes[GDN_SYNTH_TENSORS_PER_LAYER] = {H, nh, nh, H * H, H * H, H * H, nh * H, nh * H, H * cs,
+                                                       H * cs, H * cs, H * H, hd, H * H, H, I * H, I * H, H * I};
+    size_t off = 0;
+    uint32_t id = 0;
+    tensors.push_back({off, (size_t)c.vocab_size * H, id++});
+    off += (size_t)c.vocab_size * H;
+    for (uint32_t l = 0; l < c.num_layers; ++l)
+        for (int j = 0; j < GDN_SYNTH_TENSORS_PER_LAYER; ++j) {
+            tensors.push_back({off, sizes[j], id++});
+            off += sizes[j];
+        }
+    tensors.push_back({off, H, id++});
+    off += H;
+    tensors.push_back({off, (size_t)c.vocab_size * H, id++});
+    const size_t piece = (size_t)1 << 20;
+    const size_t pieces = (n + piece - 1) / piece;
+    parallel_for(pieces, [&](size_t pb, size_t pe) {
+        size_t ti = 0;
+        for (size_t pc = pb; pc < pe; ++pc) {
+            const size_t lo = pc * piece, hi = std::min(n, lo + piece);
+            while (ti < tensors.size() && tensors[ti].off + tensors[ti].size <= lo) ++ti;
+            for (size_t k = ti; k < tensors.size() && tensors[k].off < hi; ++k) {
+                const size_t b0 = std::max(lo, tensors[k].off), e0 = std::min(hi, tensors[k].off + tensors[k].size);
+                gdn_synth_fill(model->weight_data + b0, seed, tensors[k].id,
+                               gdn_synth_tensor_dist(tensors[k].id, c.num_layers), b0 - tensors[k].off,
+                               e0 - tensors[k].off);
+            }
+        }
+    });
+    assign_views(model);
+    return 0;
+}
+
+int gdn_b200_model_save(const GDNModel *model, const char *path) {
+    FILE *f = fopen(path, "wb");
+    if (f == nullptr) return fail("cannot create %s", path);
+    const size_t n = total_floats(model->config);
+    const bool ok = fwrite(&model->config, 1, kHeaderBytes, f) == kHeaderBytes &&
+                    fwrite(model->weight_data, sizeof(float), n, f) == n;
+    fclose(f);
+    return ok ? 0 : fail("write failed: %s", path);
+}
+
+void gdn_model_free(GDNModel *model) {
+    if (model == nullptr) return;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        auto it = g_models.find(model->weight_data);
+        if (it != g_models.end()) {
+            DeviceModel *dm = it->second;
+            g_models.erase(it);
+            dm->model_alive = false;
+            if (dm->refs == 0) free_device_model(dm);
+        }
+    }
+    free(model->weight_data);
+    free(model->layers);
+    memset(model, 0, sizeof(*model));
+}
+
+int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_tokens) {
+    memset(state, 0, sizeof(*state));
+    if (max_tokens == 0 || max_tokens > model->config.max_seq_len) return fail("invalid max_tokens for run state");
+    if (engine_supports(model->config) != 0) return -1;
+    CUDA_OK(cudaSetDevice(g_device));
+    DeviceModel *dm = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        auto it = g_models.find(model->weight_data);
+        if (it != g_models.end()) dm = it->second;
+    }
+    if (dm == nullptr) {
+        dm = build_device_model(model);
+        if (dm == nullptr) return -1;
+        std::lock_guard<std::mutex> lock(g_mu);
+        g_models[model->weight_data] = dm;
+    }
+    if (dm->device != g_device) return fail("gdn_b200: model image lives on device %d, run state on %d", dm->device, g_device);
+
+    Stream *s = new Stream();
+    s->dm = dm;
+    s->device = g_device;
+    s->grid = gdn_b200_grid_size();
+    const GDNWeightHeader &c = model->config;
+    const size_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size, nh = c.num_heads, L = c.num_layers;
+    auto cleanup = [&](int rc) {
+        if (s->stream) cudaStreamDestroy(s->stream);
+        if (s->ev0) cudaEventDestroy(s->ev0);
+        if (s->ev1) cudaEventDestroy(s->ev1);
+        cudaFree(s->S);
+        cudaFree(s->tails);
+        cudaFree(s->acts);
+        cudaFree(s->status);
+        cudaFreeHost(s->status_host);
+        cudaFreeHost(s->ws);
+        delete s;
+        return rc;
+    };
+    if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreate(&s->ev0) != cudaSuccess || cudaEventCreate(&s->ev1) != cudaSuccess)
+        return cleanup(fail("gdn_b200: stream creation failed"));
+    const size_t s_bytes = L * nh * 256 * 256 * sizeof(float);
+    const size_t t_bytes = L * 3 * H * 4 * sizeof(float);
+    const size_t act_floats = 4 * H + 3 * H + H + 64 + H + I + V + H + H + 2 * (size_t)s->grid + 64;
+    if (cudaMalloc(&s->S, s_bytes) != cudaSuccess || cudaMalloc(&s->tails, t_bytes) != cudaSuccess ||
+        cudaMalloc(&s->acts, act_floats * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&s->status, sizeof(gdn::DecodeStatus)) != cudaSuccess ||
+        cudaMallocHost(&s->status_host, sizeof(gdn::DecodeStatus)) != cudaSuccess ||
+        cudaHostAlloc(&s->ws, GDN_WS_FLOATS * sizeof(float), cudaHostAllocDefault) != cudaSuccess)
+        return cleanup(fail("gdn_b200: run state allocation failed"));
+    float *a = s->acts;
+    s->x_in = a; a += H;
+    s->x_mid = a; a += H;
+    s->y_o = a; a += H;
+    s->y_down = a; a += H;
+    s->qkv = a; a += 3 * H;
+    s->gate = a; a += H;
+    s->ab = a; a += 64;
+    s->attn = a; a += H;
+    s->m = a; a += I;
+    s->logits = a; a += V;
+    s->hidden = a; a += H;
+    s->x_embed = a; a += H;
+    s->cand_val = a; a += s->grid;
+    s->cand_idx = reinterpret_cast<int32_t *>(a);
+    if (cudaMemsetAsync(s->S, 0, s_bytes, s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->tails, 0, t_bytes, s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->acts, 0, act_floats * sizeof(float), s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->status, 0, sizeof(gdn::DecodeStatus), s->stream) != cudaSuccess ||
+        cudaStreamSynchronize(s->stream) != cudaSuccess)
+        return cleanup(fail("gdn_b200: run state initialisation failed"));
+    memset(s->ws, 0, GDN_WS_FLOATS * sizeof(float));
+    state->workspace = reinterpret_cast<Beat512 *>(s->ws);
+    state->x = s->ws + GDN_WS_OFF_X;
+    state->recurrent_state = s->ws + GDN_WS_OFF_REC_STATE;
+    state->head_buffer = s->ws + GDN_WS_OFF_HEAD_BUF;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        dm->refs++;
+        g_streams[state->workspace] = s;
+    }
+    return 0;
+}
+
+void gdn_run_state_free(GDNRunState *state) {
+    if (state == nullptr || state->workspace == nullptr) return;
+    Stream *s = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        auto it = g_streams.find(state->workspace);
+        if (it != g_streams.end()) {
+            s = it->second;
+            g_streams.erase(it);
+        }
+    }
+    if (s != nullptr) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(s->device);
+        cudaStreamSynchronize(s->stream);
+        cudaStreamDestroy(s->stream);
+        cudaEventDestroy(s->ev0);
+        cudaEventDestroy(s->ev1);
+        cudaFree(s->S);
+        cudaFree(s->tails);
+        cudaFree(s->acts);
+        cudaFree(s->status);
+        cudaFree(s->tokens);
+        cudaFree(s->argmax);
+        cudaFreeHost(s->status_host);
+        cudaFreeHost(s->ws);
+        cudaSetDevice(prev);
+        std::lock_guard<std::mutex> lock(g_mu);
+        DeviceModel *dm = s->dm;
+        if (--dm->refs == 0 && !dm->model_alive) free_device_model(dm);
+        delete s;
+    }
+    memset(state, 0, sizeof(*state));
+}
+
+int gdn_b200_set_boundary(GDNRunState *state, int bf16_boundary) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    s->bf16_boundary = bf16_boundary ? 1 : 0;
+    return 0;
+}
+
+int gdn_decode_step_host(const GDNModel *model, GDNRunState *state, const int32_t *token) {
+    if (*token < 0 || (uint32_t)*token >= model->config.vocab_size) return fail("token id out of range");
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    const size_t H = model->config.hidden_size;
+    /* the host writes the FP32 embedding row into workspace[X]
+     * (c_impl/gdn_model.cpp:3906-3908; c_impl/host.cpp:955-960) */
+    memcpy(state->x, model->embeddings + (size_t)*token * H, H * sizeof(float));
+    CUDA_OK(cudaSetDevice(s->device));
+    CUDA_OK(cudaMemcpyAsync(s->x_embed, state->x, H * sizeof(float), cudaMemcpyHostToDevice, s->stream));
+    gdn::DecodeParams p = make_params(*s);
+    if (launch(*s, p) != 0) return -1;
+    /* token line -> workspace[X_NORM] (64 bytes, c_impl/host.cpp:1011-1017) */
+    CUDA_OK(cudaMemcpyAsync(s->ws + GDN_WS_OFF_X_NORM, s->status->token_line, 64, cudaMemcpyDeviceToHost, s->stream));
+    if (g_debug_hidden != nullptr)
+        CUDA_OK(cudaMemcpyAsync(g_debug_hidden, s->hidden, H * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    if (g_debug_logits != nullptr)
+        CUDA_OK(cudaMemcpyAsync(g_debug_logits, s->logits, model->config.vocab_size * sizeof(float),
+                                cudaMemcpyDeviceToHost, s->stream));
+    return sync_and_check(*s);
+}
+
+int gdn_b200_decode_tokens(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n, int greedy,
+                           int32_t *argmax_out, float *kernel_ms) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    if (n == 0) return 0;
+    const uint32_t V = model->config.vocab_size;
+    for (uint32_t i = 0; i < (greedy ? 1u : n); ++i)
+        if (tokens[i] < 0 || (uint32_t)tokens[i] >= V) return fail("token id out of range");
+    CUDA_OK(cudaSetDevice(s->device));
+    if (s->tokens_cap < n) {
+        cudaFree(s->tokens);
+        cudaFree(s->argmax);
+        s->tokens = nullptr;
+        s->argmax = nullptr;
+        s->tokens_cap = 0;
+        CUDA_OK(cudaMalloc(&s->tokens, n * sizeof(int32_t)));
+        CUDA_OK(cudaMalloc(&s->argmax, n * sizeof(int32_t)));
+        s->tokens_cap = n;
+    }
+    CUDA_OK(cudaMemcpyAsync(s->tokens, tokens, (greedy ? 1u : n) * sizeof(int32_t), cudaMemcpyHostToDevice, s->stream));
+    gdn::DecodeParams p = make_params(*s);
+    CUDA_OK(cudaEventRecord(s->ev0, s->stream));
+    for (uint32_t i = 0; i < n; ++i) {
+        p.token_src = (greedy && i > 0) ? s->argmax + (i - 1) : s->tokens + i;
+        p.token_out = s->argmax + i;
+        if (launch(*s, p) != 0) return -1;
+    }
+    CUDA_OK(cudaEventRecord(s->ev1, s->stream));
+    if (argmax_out != nullptr)
+        CUDA_OK(cudaMemcpyAsync(argmax_out, s->argmax, n * sizeof(int32_t), cudaMemcpyDeviceToHost, s->stream));
+    CUDA_OK(cudaMemcpyAsync(s->ws + GDN_WS_OFF_X_NORM, s->status->token_line, 64, cudaMemcpyDeviceToHost, s->stream));
+    const int rc = sync_and_check(*s);
+    if (rc != 0) return rc;
+    if (kernel_ms != nullptr) CUDA_OK(cudaEventElapsedTime(kernel_ms, s->ev0, s->ev1));
+    return 0;
+}
+
+int gdn_b200_fetch_outputs(GDNRunState *state, float *logits, float *final_hidden) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    CUDA_OK(cudaSetDevice(s->device));
+    if (logits != nullptr)
+        CUDA_OK(cudaMemcpyAsync(logits, s->logits, s->dm->cfg.vocab_size * sizeof(float), cudaMemcpyDeviceToHost,
+                                s->stream));
+    if (final_hidden != nullptr)
+        CUDA_OK(cudaMemcpyAsync(final_hidden, s->hidden, s->dm->cfg.hidden_size * sizeof(float),
+                                cudaMemcpyDeviceToHost, s->stream));
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    return 0;
+}
+
+int gdn_b200_state_upload(GDNRunState *state, const float *rec, size_t rec_floats, const float *conv,
+                          size_t conv_floats) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    const GDNWeightHeader &c = s->dm->cfg;
+    const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
+    if (rec_floats != L * nh * 256 * 256 || conv_floats != L * 3 * 3 * H)
+        return fail("gdn_b200: state sizes do not match the model (rec %zu, conv %zu)", rec_floats, conv_floats);
+    /* [L][h][k][v] -> [L][h][v][k];  [L][kind][row][H] -> [L][kind][H][4] */
+    std::vector<float> S(rec_floats), T(L * 3 * H * 4, 0.0f);
+    parallel_for(L * nh, [&](size_t b, size_t e) {
+        for (size_t lh = b; lh < e; ++lh)
+            for (size_t k = 0; k < 256; ++k)
+                for (size_t v = 0; v < 256; ++v) S[(lh * 256 + v) * 256 + k] = rec[(lh * 256 + k) * 256 + v];
+    });
+    for (size_t lk = 0; lk < L * 3; ++lk)
+        for (size_t d = 0; d < H; ++d)
+            for (size_t r = 0; r < 3; ++r) T[(lk * H + d) * 4 + r] = conv[(lk * 3 + r) * H + d];
+    CUDA_OK(cudaSetDevice(s->device));
+    CUDA_OK(cudaMemcpyAsync(s->S, S.data(), S.size() * 4, cudaMemcpyHostToDevice, s->stream));
+    CUDA_OK(cudaMemcpyAsync(s->tails, T.data(), T.size() * 4, cudaMemcpyHostToDevice, s->stream));
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    return 0;
+}
+
+int gdn_b200_state_download(GDNRunState *state, float *rec, size_t rec_floats, float *conv, size_t conv_floats) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    const GDNWeightHeader &c = s->dm->cfg;
+    const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
+    if (rec_floats != L * nh * 256 * 256 || conv_floats != L * 3 * 3 * H)
+        return fail("gdn_b200: state sizes do not match the model");
+    std::vector<float> S(rec_floats), T(L * 3 * H * 4);
+    CUDA_OK(cudaSetDevice(s->device));
+    CUDA_OK(cudaMemcpyAsync(S.data(), s->S, S.size() * 4, cudaMemcpyDeviceToHost, s->stream));
+    CUDA_OK(cudaMemcpyAsync(T.data(), s->tails, T.size() * 4, cudaMemcpyDeviceToHost, s->stream));
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    parallel_for(L * nh, [&](size_t b, size_t e) {
+        for (size_t lh = b; lh < e; ++lh)
+            for (size_t k = 0; k < 256; ++k)
+                for (size_t v = 0; v < 256; ++v) rec[(lh * 256 + k) * 256 + v] = S[(lh * 256 + v) * 256 + k];
+    });
+    for (size_t lk = 0; lk < L * 3; ++lk)
+        for (size_t d = 0; d < H; ++d)
+            for (size_t r = 0; r < 3; ++r) conv[(lk * 3 + r) * H + d] = T[(lk * H + d) * 4 + r];
+    return 0;
+}
+
+int gdn_b200_state_load_file(GDNRunState *state, const char *path, int32_t *seed_token) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    FILE *f = fopen(path, "rb");
+    if (f == nullptr) return fail("cannot open .gdnstate file");
+    char magic[8];
+    uint32_t v[9];
+    if (fread(magic, 1, 8, f) != 8 || memcmp(magic, "GDNSTAT1", 8) != 0) {
+        fclose(f);
+        return fail(".gdnstate: bad magic (expected GDNSTAT1)");
+    }
+    if (fread(v, sizeof(uint32_t), 9, f) != 9) { fclose(f); return fail(".gdnstate: truncated header"); }
+    const GDNWeightHeader &c = s->dm->cfg;
+    if (v[0] != 1 || v[1] != c.num_layers || v[2] != c.num_heads || v[3] != c.head_dim || v[4] != c.head_dim ||
+        v[5] != c.hidden_size || v[6] != c.conv_size) {
+        fclose(f);
+        return fail(".gdnstate: dims do not match the loaded model");
+    }
+    if (fseek(f, (long)v[7] * 4, SEEK_CUR) != 0) { fclose(f); return fail(".gdnstate: cannot skip prompt ids"); }
+    const size_t nrec = (size_t)v[1] * v[2] * v[3] * v[4], nconv = (size_t)v[1] * 3 * (v[6] - 1) * v[5];
+    std::vector<float> rec(nrec), conv(nconv);
+    if (fread(rec.data(), 4, nrec, f) != nrec) { fclose(f); return fail(".gdnstate: truncated recurrent section"); }
+    if (fread(conv.data(), 4, nconv, f) != nconv) { fclose(f); return fail(".gdnstate: truncated conv section"); }
+    char extra;
+    const bool trailing = fread(&extra, 1, 1, f) == 1;
+    fclose(f);
+    if (trailing) return fail(".gdnstate: unexpected trailing bytes");
+    if (seed_token != nullptr) *seed_token = (int32_t)v[8];
+    return gdn_b200_state_upload(state, rec.data(), nrec, conv.data(), nconv);
+}
+
+int gdn_b200_state_save_file(GDNRunState *state, const char *path, int32_t seed_token) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    const GDNWeightHeader &c = s->dm->cfg;
+    const size_t nrec = (size_t)c.num_layers * c.num_heads * 256 * 256, nconv = (size_t)c.num_layers * 3 * 3 * c.hidden_size;
+    std::vector<float> rec(nrec), conv(nconv);
+    if (gdn_b200_state_download(state, rec.data(), nrec, conv.data(), nconv) != 0) return -1;
+    FILE *f = fopen(path, "wb");
+    if (f == nullptr) return fail("cannot create %s", path);
+    const uint32_t v[9] = {1, c.num_layers, c.num_heads, c.head_dim, c.head_dim, c.hidden_size, c.conv_size, 0,
+                           (uint32_t)seed_token};
+    bool ok = fwrite("GDNSTAT1", 1, 8, f) == 8 && fwrite(v, 4, 9, f) == 9 && fwrite(rec.data(), 4, nrec, f) == nrec &&
+              fwrite(conv.data(), 4, nconv, f) == nconv;
+    fclose(f);
+    return ok ? 0 : fail("write failed: %s", path);
+}
+
+void gdn_compute_logits(const GDNModel *model, const float *hidden, float *logits_out) {
+    const uint32_t V = model->config.vocab_size, H = model->config.hidden_size;
+    std::vector<uint16_t> act(H);
+    for (uint32_t i = 0; i < H; ++i) act[i] = bf16_rne_bits(hidden[i]);
+    parallel_for(V, [&](size_t b, size_t e) {
+        for (size_t v = b; v < e; ++v) {
+            const float *row = model->lm_head + v * H;
+            float sum = 0.0f;
+            for (uint32_t i = 0; i < H; ++i) sum += u2f(native_product_bits(hi16(row[i]), act[i]));
+            logits_out[v] = sum;
+        }
+    });
+}
+
+float gdn_native_bf16_mul_to_fp32(uint16_t weight, uint16_t activation) {
+    return u2f(native_product_bits(weight, activation));
+}
+
+void gdn_set_native_debug_buffers(float *final_hidden, float *logits) {
+    g_debug_hidden = final_hidden;
+    g_debug_logits = logits;
+}
+
+void gdn_reset_mixed_mul_stats(void) {}
+
+GDNMixedMulStats gdn_get_mixed_mul_stats(void) {
+    GDNMixedMulStats s;
+    memset(&s, 0, sizeof(s));
+    return s;
+}
+
+}  // extern "C"

@@ -1,0 +1,77 @@
+/* gdn_b200.h -- entry points of libgdn_b200.so beyond the reference's
+ * c_impl/gdn_model.h. All return 0 on success and -1 on failure, with the
+ * reason available from gdn_b200_last_error() (and printed to stderr, as the
+ * reference's gdn_print_error does).
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "gdn_model.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* CUDA device used by models and run states created afterwards on this
+ * thread (default: device 0). One process per GPU is the intended layout.
+ * No reference counterpart (the FPGA host selects its card through XRT,
+ * c_impl/host.cpp:214-417). */
+int gdn_b200_set_device(int device);
+
+/* Message of the most recent failure on this thread ("" if none). */
+const char *gdn_b200_last_error(void);
+
+/* Fill `model` with seeded synthetic weights in the .gdnw blob order
+ * (BF16-exact FP32 words; distributions in gateddeltanet_b200/csrc/gdn_synth.h)
+ * instead of reading a file; afterwards the model behaves exactly as one
+ * returned by gdn_model_load. Counterpart of the reference's weight writer
+ * scripts/export_gdn_c.py:177-210 for a checkpoint that does not exist here. */
+int gdn_b200_model_synth(GDNModel *model, const GDNWeightHeader *config, uint64_t seed);
+
+/* Write `model` as a .gdnw file (60-byte header + FP32 words), the format
+ * gdn_model_load reads (scripts/export_gdn_c.py:177-210). */
+int gdn_b200_model_save(const GDNModel *model, const char *path);
+
+/* Operator-boundary precision of a stream: 1 (default) rounds every
+ * activation to BF16 where the reference does; 0 keeps FP32 (the "FP32
+ * control" of the parity gates). */
+int gdn_b200_set_boundary(GDNRunState *state, int bf16_boundary);
+
+/* Replace / read the decode state in the .gdnstate section layouts:
+ * rec [layers][heads][K=256][V=256] FP32 and conv tails
+ * [layers][q,k,v][conv_size-1][hidden] FP32, last row newest
+ * (scripts/export_gdn_state.py:13-19, 340-362; c_impl/gdn_eval.cpp:202-267). */
+int gdn_b200_state_upload(GDNRunState *state, const float *rec, size_t rec_floats, const float *conv,
+                          size_t conv_floats);
+int gdn_b200_state_download(GDNRunState *state, float *rec, size_t rec_floats, float *conv, size_t conv_floats);
+
+/* .gdnstate files ("GDNSTAT1", c_impl/gdn_eval.cpp:202-267 and
+ * c_impl/host.cpp:675-735: dims must match the model, no trailing bytes). */
+int gdn_b200_state_load_file(GDNRunState *state, const char *path, int32_t *seed_token);
+int gdn_b200_state_save_file(GDNRunState *state, const char *path, int32_t seed_token);
+
+/* FP32 logits (vocab floats) and final normalised hidden vector (hidden
+ * floats) of the most recent step; either pointer may be NULL. */
+int gdn_b200_fetch_outputs(GDNRunState *state, float *logits, float *final_hidden);
+
+/* Decode n tokens back to back without returning to the host between
+ * steps. greedy = 0: teacher-forced, step i consumes tokens[i]; greedy = 1:
+ * step 0 consumes tokens[0] and step i > 0 consumes step i-1's argmax
+ * (the loop of c_impl/gdn_eval.cpp:336-440). argmax_out[i] receives step
+ * i's token. If kernel_ms is not NULL it receives the device time of the n
+ * steps (CUDA events on the stream). Embedding rows are gathered on the
+ * device; the token ids cross PCIe once. */
+int gdn_b200_decode_tokens(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n,
+                           int greedy, int32_t *argmax_out, float *kernel_ms);
+
+/* Number of SMs (CTAs) the decode kernel uses on the current device. */
+int gdn_b200_grid_size(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -317,6 +317,45 @@ void gdn_oracle_synth_weights(const GdnOracleDims *d, uint64_t seed, float *blob
     parallel_for((total + piece - 1) / piece, threads, synth_range, &c);
 }
 
+void gdn_oracle_bf16_rne_batch(const uint32_t *in, size_t n, uint16_t *out) {
+    for (size_t i = 0; i < n; ++i) out[i] = gdn_oracle_bf16_rne_bits(in[i]);
+}
+
+void gdn_oracle_native_product_grid(const uint16_t *w, size_t n_w, const uint16_t *a, size_t n_a, uint32_t *out) {
+    for (size_t j = 0; j < n_a; ++j)
+        for (size_t i = 0; i < n_w; ++i) out[j * n_w + i] = gdn_oracle_native_product_bits(w[i], a[j]);
+}
+
+typedef struct {
+    const float *lm;
+    const uint16_t *act;
+    float *out;
+    uint32_t H;
+} logits_ctx;
+
+static void logits_range(void *c, size_t b, size_t e) {
+    logits_ctx *g = (logits_ctx *)c;
+    for (size_t v = b; v < e; ++v) {
+        const float *row = g->lm + v * g->H;
+        float sum = 0.0f;
+        for (uint32_t i = 0; i < g->H; ++i)
+            sum += u2f(gdn_oracle_native_product_bits((uint16_t)(f2u(row[i]) >> 16), g->act[i]));
+        g->out[v] = sum;
+    }
+}
+
+void gdn_oracle_compute_logits(const GdnOracleDims *d, const float *blob, const float *hidden, float *logits,
+                               int threads) {
+    const float *final_norm, *lm_head;
+    views(d, blob, 0, NULL, &final_norm, &lm_head);
+    uint16_t *act = (uint16_t *)malloc(sizeof(uint16_t) * d->hidden);
+    if (act == NULL) return;
+    for (uint32_t i = 0; i < d->hidden; ++i) act[i] = gdn_oracle_bf16_rne_bits(f2u(hidden[i]));
+    logits_ctx c = {lm_head, act, logits, d->hidden};
+    parallel_for(d->vocab, threads, logits_range, &c);
+    free(act);
+}
+
 int32_t gdn_oracle_synth_token(uint64_t seed, uint32_t stream, uint64_t i, uint32_t vocab) {
     return gdn_synth_token(seed, stream, i, vocab);
 }

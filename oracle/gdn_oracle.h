@@ -70,6 +70,17 @@ uint16_t gdn_oracle_bf16_rne_bits(uint32_t fp32_bits);
 uint32_t gdn_oracle_native_product_bits(uint16_t weight, uint16_t activation);
 float gdn_oracle_row_dot(const float *w_row, const float *x, uint32_t k, int native_product);
 
+/* Batch forms for the known-answer tests: out[i] = RNE bits of in[i];
+ * out[j * n_w + i] = product bits of (w[i], a[j]). */
+void gdn_oracle_bf16_rne_batch(const uint32_t *in, size_t n, uint16_t *out);
+void gdn_oracle_native_product_grid(const uint16_t *w, size_t n_w, const uint16_t *a, size_t n_a, uint32_t *out);
+
+/* gdn_compute_logits (c_impl/gdn_model.cpp:3930-3975): logits[v] =
+ * sequential sum over i of the BF16-rounded product of lm_head[v][i] and
+ * RNE(hidden[i]). blob is the .gdnw payload. */
+void gdn_oracle_compute_logits(const GdnOracleDims *d, const float *blob, const float *hidden, float *logits,
+                               int threads);
+
 /* The gated delta rule for one head from the read pass on
  * (c_impl/gdn_model.cpp:2119-2300): S [K][V] updated in place from already
  * L2-normalised q/k, the decay and beta; o [V] receives the unrounded output. */

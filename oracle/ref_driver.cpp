@@ -61,7 +61,46 @@ static float bf16_to_f(uint16_t b) {
     return f;
 }
 
+/* Known-answer grids over the reference's own primitives, written raw:
+ *   RNE set A: x = i * 65521 (mod 2^32), i < 65536
+ *   RNE set B: x = (h << 16) | l, h < 65536, l in {0, 0x7fff, 0x8000, 0x8001, 0xffff}
+ *   product grid: every BF16 weight pattern (65536) x the 32 activations below
+ * through gdn_test_fp32_to_bf16_rne_bits and gdn_native_bf16_mul_to_fp32
+ * (c_impl/gdn_model.cpp:314-325, 392-466). tests/test_oracle_golden.py
+ * rebuilds the same grids. */
+static const uint16_t kGridActivations[32] = {
+    0x0000, 0x8000, 0x0001, 0x807f, 0x0080, 0x8080, 0x3f80, 0xbf80, 0x7f80, 0xff80, 0x7fc0,
+    0x7f81, 0x7f7f, 0xff7f, 0x3f81, 0x4000, 0x00ff, 0x3e4c, 0xc2f7, 0x1f00, 0x2000, 0x2080,
+    0x5f00, 0x6000, 0x0100, 0x3c00, 0x3b80, 0x1c3f, 0x23a1, 0x9e77, 0x4b19, 0xd0e3};
+
+static int dump_primitives(const char *path) {
+    FILE *f = std::fopen(path, "wb");
+    if (f == nullptr) die("cannot open primitives output");
+    std::vector<uint16_t> rne;
+    for (uint32_t i = 0; i < 65536u; ++i) rne.push_back(gdn_test_fp32_to_bf16_rne_bits(i * 65521u));
+    const uint32_t lows[5] = {0x0000u, 0x7fffu, 0x8000u, 0x8001u, 0xffffu};
+    for (uint32_t h = 0; h < 65536u; ++h)
+        for (uint32_t k = 0; k < 5; ++k) rne.push_back(gdn_test_fp32_to_bf16_rne_bits((h << 16) | lows[k]));
+    std::vector<uint32_t> prod;
+    prod.reserve(65536u * 32u);
+    for (uint32_t j = 0; j < 32; ++j)
+        for (uint32_t w = 0; w < 65536u; ++w) {
+            const float v = gdn_native_bf16_mul_to_fp32(Bf16Bits(w), Bf16Bits(kGridActivations[j]));
+            uint32_t b;
+            std::memcpy(&b, &v, 4);
+            prod.push_back(b);
+        }
+    std::fwrite("GDNPRIM1", 1, 8, f);
+    const uint32_t n[2] = {(uint32_t)rne.size(), (uint32_t)prod.size()};
+    std::fwrite(n, 4, 2, f);
+    std::fwrite(rne.data(), 2, rne.size(), f);
+    std::fwrite(prod.data(), 4, prod.size(), f);
+    std::fclose(f);
+    return 0;
+}
+
 int main(int argc, char **argv) {
+    if (argc == 3 && std::string(argv[1]) == "--primitives") return dump_primitives(argv[2]);
     uint64_t seed = 1234;
     uint64_t stream_seed = 99;
     uint32_t stream_id = 0;

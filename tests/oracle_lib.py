@@ -108,6 +108,13 @@ class Oracle:
         if state_seed:
             self.lib.gdn_oracle_synth_state(ctypes.byref(self.dims), state_seed, ptr(self.rec), ptr(self.conv))
 
+    def reset_state(self, state_seed: int = 0) -> None:
+        """Zero state, or the seeded BF16-exact initial state."""
+        self.rec[:] = 0.0
+        self.conv[:] = 0.0
+        if state_seed:
+            self.lib.gdn_oracle_synth_state(ctypes.byref(self.dims), state_seed, ptr(self.rec), ptr(self.conv))
+
     def token(self, stream_seed: int, stream: int, i: int) -> int:
         return int(self.lib.gdn_oracle_synth_token(stream_seed, stream, i, self.dims.vocab))
 
