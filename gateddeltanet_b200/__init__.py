@@ -98,7 +98,7 @@ EXPORTS = [
     ("gdn_b200_last_error", ctypes.c_char_p, []),
     ("gdn_b200_model_synth", ctypes.c_int, [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNWeightHeader), ctypes.c_uint64]),
     ("gdn_b200_model_save", ctypes.c_int, [ctypes.POINTER(GDNModel), ctypes.c_char_p]),
-    ("gdn_b200_set_boundary", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int]),
+    ("gdn_b200_set_numerics", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     ("gdn_b200_state_upload", ctypes.c_int, [ctypes.POINTER(GDNRunState), _FP, ctypes.c_size_t, _FP, ctypes.c_size_t]),
     ("gdn_b200_state_download", ctypes.c_int, [ctypes.POINTER(GDNRunState), _FP, ctypes.c_size_t, _FP, ctypes.c_size_t]),
     ("gdn_b200_state_load_file", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32)]),
@@ -107,6 +107,9 @@ EXPORTS = [
     ("gdn_b200_decode_tokens", ctypes.c_int,
      [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32,
       ctypes.c_int, ctypes.POINTER(ctypes.c_int32), _FP]),
+    ("gdn_b200_trace_step", ctypes.c_int,
+     [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64),
+      ctypes.c_size_t]),
     ("gdn_b200_grid_size", ctypes.c_int, []),
 ]
 
@@ -227,6 +230,19 @@ class RunState:
               "gdn_b200_decode_tokens")
         return out, float(ms.value)
 
+    def trace(self, token: int) -> np.ndarray:
+        """One traced step: array [cta, phase, 8] of %globaltimer ns stamps
+        (see gdn_b200_trace_step in include/gdn_b200.h)."""
+        c = self.model.config
+        grid = self.lib.gdn_b200_grid_size()
+        phases = c.num_layers * 5 + 1
+        buf = np.zeros(grid * phases * 8, dtype=np.uint64)
+        n = self.lib.gdn_b200_trace_step(ctypes.byref(self.model.m), ctypes.byref(self.s), int(token),
+                                         buf.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), buf.size)
+        if n < 0:
+            raise RuntimeError(f"gdn_b200_trace_step failed: {last_error()}")
+        return buf.reshape(grid, phases, 8)
+
     def outputs(self):
         c = self.model.config
         logits = np.empty(c.vocab_size, dtype=np.float32)
@@ -235,8 +251,11 @@ class RunState:
               "gdn_b200_fetch_outputs")
         return logits, hidden
 
-    def set_boundary(self, bf16: bool) -> None:
-        check(self.lib.gdn_b200_set_boundary(ctypes.byref(self.s), int(bool(bf16))), "gdn_b200_set_boundary")
+    def set_numerics(self, bf16_boundary: bool = True, bf16_products: bool = False, bf16_state: bool = False) -> None:
+        """Engine default (True, False, False); the c_impl's own arithmetic is
+        (True, True, True); the FP32 control is (False, False, False)."""
+        check(self.lib.gdn_b200_set_numerics(ctypes.byref(self.s), int(bool(bf16_boundary)), int(bool(bf16_products)),
+                                             int(bool(bf16_state))), "gdn_b200_set_numerics")
 
     def load_state(self, rec: np.ndarray, conv: np.ndarray) -> None:
         rec = np.ascontiguousarray(rec, dtype=np.float32)

@@ -11,33 +11,38 @@
  *   - grid = one CTA per SM, launched cooperatively; each CTA owns a fixed
  *     slice of every phase's rows (and of the recurrent state's columns);
  *   - warp 8 of every CTA is a producer: one lane walks the CTA's whole
- *     token schedule of weight / state chunks and streams each chunk into a
- *     12-slot shared-memory ring with cp.async.bulk (TMA bulk copies,
+ *     token schedule of weight / state chunks and streams each chunk into an
+ *     11-slot shared-memory ring with cp.async.bulk (TMA bulk copies,
  *     mbarrier completion, evict-first L2 policy for weights). Weights do
  *     not depend on activations, so the producer runs ahead across phase
- *     boundaries while the consumers wait at grid barriers;
- *   - warps 0..7 are consumers: per phase they pass a grid barrier, build the
- *     phase's input vector in shared memory (residual add + RMSNorm, output
- *     norm x swish gate, ...), then each warp takes every 8th chunk: 16-byte
- *     vector reads of BF16 weights, FP32 FMA, butterfly warp reductions, and
- *     the phase's epilogue fused per row (short conv + SiLU + conv-window
- *     update, SwiGLU, LM-head logits + argmax).
+ *     boundaries while the consumers wait for inputs;
+ *   - warps 0..7 are consumers: per phase they build the phase's input vector
+ *     in shared memory from the previous phase's outputs (residual add +
+ *     RMSNorm, output norm x swish gate, ...), then each warp takes every 8th
+ *     chunk: tree16 dot products in the reference's reduction order, and the
+ *     phase's epilogue fused per row (short conv + SiLU + conv-window update,
+ *     SwiGLU, LM-head logits + argmax).
  *
  * Phases per layer l: A QKVG+a/b rows, B state columns (gated delta rule),
  * C O rows, D gate/up row pairs, E down rows; after the last layer F LM head.
- * Five grid barriers per layer (none before layer 0's A).
+ * There is no grid barrier: a phase's outputs travel as 64-bit words that
+ * carry the phase's tag next to the value, and each consumer CTA polls the
+ * words it needs (gdn_engine.h). A CTA cannot run more than one phase ahead
+ * of any CTA it reads from, so exchange buffers are reused every layer
+ * without write-after-read hazards; the residual stream lives in each CTA's
+ * shared memory (every CTA computes it identically).
  *
- * Every wait (mbarrier, grid barrier) is bounded by %globaltimer; on expiry
+ * Every wait (mbarrier, exchange word) is bounded by %globaltimer; on expiry
  * the kernel records an error in DecodeStatus, stops issuing copies, waits
  * for the copies already in flight and returns. The host reports -1.
  */
 #include "gdn_engine.h"
+#include "gdn_math.h"
 
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace gdn {
-
 constexpr uint64_t kWaitNs = 2000000000ull;  /* 2 s: normal waits are microseconds */
 
 /* ------------------------------------------------------------ PTX helpers */
@@ -116,26 +121,34 @@ __device__ __forceinline__ float bf16_round(float v) {
     b = (b + 0x7fffu + ((b >> 16) & 1u)) & 0xffff0000u;
     return __uint_as_float(b);
 }
-template <bool BF16B>
+template <int MODE>
 __device__ __forceinline__ float bnd(float v) {
-    return BF16B ? bf16_round(v) : v;
+    return (MODE & 1) ? bf16_round(v) : v;
 }
 
-/* gdn_sigmoid / gdn_softplus with IEEE single-rounding operations
- * (c_impl/gdn_model.cpp:1307-1330). */
-__device__ __forceinline__ float sigmoid_ref(float x) {
-    if (x >= 0.0f) {
-        const float z = expf(-x);
-        return __fdiv_rn(1.0f, __fadd_rn(1.0f, z));
-    }
-    const float z = expf(x);
-    return __fdiv_rn(z, __fadd_rn(1.0f, z));
-}
+/* exp table (2^(j/64) as hi | lo) staged in shared memory at kernel start */
+__device__ __forceinline__ const float *exp_table();
+
+/* exp / sigmoid / silu / softplus of the reference (c_impl/gdn_model.cpp:
+ * 1307-1330) on the primitives of gdn_math.h. */
+__device__ __forceinline__ float exp_ref(float x) { return gdn_expf(x, exp_table()); }
+__device__ __forceinline__ float sigmoid_ref(float x) { return gdn_sigmoidf(x, exp_table()); }
 __device__ __forceinline__ float silu_ref(float x) { return __fmul_rn(x, sigmoid_ref(x)); }
 __device__ __forceinline__ float softplus_ref(float x) {
     if (x > 20.0f) return x;
-    if (x < -20.0f) return expf(x);
-    return log1pf(expf(x));
+    if (x < -20.0f) return exp_ref(x);
+    return log1pf(exp_ref(x));
+}
+
+/* The c_impl GEMV product (c_impl/gdn_model.cpp:392-462) for finite normal
+ * BF16 operands: the exact product, flushed to a signed zero below
+ * 0x007fc000, else rounded to BF16 (RNE). Subnormal operands, which the
+ * reference flushes first, do not occur in BF16 weights/activations of
+ * normal magnitude and are not special-cased. */
+__device__ __forceinline__ float native_round(float p) {
+    const uint32_t b = __float_as_uint(p);
+    if ((b & 0x7fffffffu) < 0x007fc000u) return __uint_as_float(b & 0x80000000u);
+    return __uint_as_float((b + 0x7fffu + ((b >> 16) & 1u)) & 0xffff0000u);
 }
 
 /* Butterfly sum: lane offsets 1, 2, 4, 8, 16 give the balanced pairwise tree
@@ -149,11 +162,13 @@ __device__ __forceinline__ float warp_sum(float v) {
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-/* Shared-memory position of input column c: lane l of a 256-column step
- * reads its 8 columns as two float4 that are contiguous across lanes. */
+/* Shared-memory position of input column c. Columns come in groups of 512
+ * = 32 halves of 16; lane l owns half l of a group and reads its 16 inputs as
+ * four float4 (quads q = 0..3) at group*512 + q*128 + 4*l, contiguous across
+ * lanes. */
 __device__ __forceinline__ int xs_pos(int c) {
-    const int s = c >> 8, w = c & 255, l = w >> 3, j = w & 7;
-    return (s << 8) + (j < 4 ? (l << 2) + j : 128 + (l << 2) + (j - 4));
+    const int g = c >> 9, w = c & 511, half = w >> 4, i = w & 15;
+    return (g << 9) + ((i >> 2) << 7) + (half << 2) + (i & 3);
 }
 
 /* ------------------------------------------------------------ schedule */
@@ -217,14 +232,70 @@ __device__ __forceinline__ Geom geom(const DecodeParams &p, int l, int ph, uint3
     return g;
 }
 
+/* ------------------------------------------------------ exchange words */
+
+__device__ __forceinline__ void xput(xword *p, float v, uint32_t tag) {
+    const xword w = ((xword)tag << 32) | (xword)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ xword xget(const xword *p) {
+    xword w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ uint32_t xtag(xword w) { return (uint32_t)(w >> 32); }
+__device__ __forceinline__ float xval(xword w) { return __uint_as_float((uint32_t)w); }
+
+/* A position in a CTA's chunk schedule: layers' phases A..E, then the LM
+ * head. The producer walks one cursor to fill the ring and a second one,
+ * kPrefetchBytes ahead of it, to pull the same chunks from HBM into L2. */
+struct Cursor {
+    int l, pi;
+    uint32_t u;
+    Geom g;
+};
+
+__device__ __forceinline__ bool cursor_valid(const DecodeParams &p, const Cursor &c) {
+    return c.l < p.L || (c.l == p.L && c.pi == 0);
+}
+
+__device__ __forceinline__ void cursor_settle(const DecodeParams &p, Cursor &c, uint32_t cta, uint32_t ncta) {
+    while (cursor_valid(p, c) && c.u >= c.g.u1) {
+        if (c.l == p.L) {
+            c.pi = 1;  /* past the LM head */
+            return;
+        }
+        if (++c.pi == kPhasesPerLayer) {
+            c.pi = 0;
+            ++c.l;
+        }
+        c.g = geom(p, c.l < p.L ? c.l : 0, c.l < p.L ? c.pi : PH_LM, cta, ncta);
+        c.u = c.g.u0;
+    }
+}
+
+__device__ __forceinline__ void cursor_init(const DecodeParams &p, Cursor &c, uint32_t cta, uint32_t ncta) {
+    c.l = 0;
+    c.pi = 0;
+    c.g = geom(p, 0, PH_QKVG, cta, ncta);
+    c.u = c.g.u0;
+    cursor_settle(p, c, cta, ncta);
+}
+
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 /* ------------------------------------------------------- shared memory */
 
 struct Smem {
     uint8_t *ring;
-    float *xs;        /* permuted phase input, max(H, I) floats */
+    float *xs;        /* permuted phase input, max(H, I) floats; phase B: qn | kn */
     float *qn, *kn;   /* [2][256] normalised q/k of the CTA's (at most two) heads */
-    float *red;       /* [8 warps][8 values] reduction scratch */
-    float *hscal;     /* [2][4]: alpha, beta, decay per local head */
+    float *xres;      /* residual stream, H floats (the same in every CTA) */
+    float *red;       /* 160 floats: half sums [0,128), block partials [0,64), scalars [128,160) */
+    float *chain;     /* [8 warps][512] per-warp GEMV bank partials */
+    float *hscal;     /* [2][4] alpha, beta, decay per local head; [8, 16) per-head norm scales */
     float *wbest;     /* [8] */
     int32_t *wbest_i; /* [8] */
     uint64_t *full, *empty;
@@ -232,47 +303,59 @@ struct Smem {
     volatile int32_t *decision;    /* thread 0's CTA-uniform go/stop, read after a barrier */
 };
 
+/* Shared-memory layout: every region sits at a compile-time offset (so the
+ * region pointers fold into immediate addresses instead of occupying
+ * registers); only the size of the last region, xs, depends on the shape. */
+constexpr size_t kOffRing = 0;
+constexpr size_t kOffChain = kOffRing + (size_t)kSlots * kSlotBytes;
+constexpr size_t kOffRed = kOffChain + (size_t)kConsumerWarps * 512 * 4;
+constexpr size_t kOffHscal = kOffRed + 160 * 4;
+constexpr size_t kOffWbest = kOffHscal + 16 * 4;
+constexpr size_t kOffWbestI = kOffWbest + 8 * 4;
+constexpr size_t kOffBars = kOffWbestI + 8 * 4;
+constexpr size_t kOffFlags = kOffBars + 2 * kSlots * 8;
+constexpr size_t kOffExpTab = (kOffFlags + 16 + 15) & ~(size_t)15;
+constexpr size_t kOffXres = kOffExpTab + 128 * 4;
+constexpr size_t kMaxHidden = 2048;
+constexpr size_t kOffXs = kOffXres + kMaxHidden * 4;
+
 __device__ __forceinline__ Smem carve(uint8_t *base, int H, int I) {
+    (void)H;
+    (void)I;
     Smem s;
-    size_t off = 0;
-    s.ring = base;
-    off += (size_t)kSlots * kSlotBytes;
-    s.xs = reinterpret_cast<float *>(base + off);
-    off += (size_t)4 * (H > I ? H : I);
-    s.qn = reinterpret_cast<float *>(base + off);
-    off += 2 * kHeadDim * 4;
-    s.kn = reinterpret_cast<float *>(base + off);
-    off += 2 * kHeadDim * 4;
-    s.red = reinterpret_cast<float *>(base + off);
-    off += 64 * 4;
-    s.hscal = reinterpret_cast<float *>(base + off);
-    off += 8 * 4;
-    s.wbest = reinterpret_cast<float *>(base + off);
-    off += 8 * 4;
-    s.wbest_i = reinterpret_cast<int32_t *>(base + off);
-    off += 8 * 4;
-    off = (off + 7) & ~(size_t)7;
-    s.full = reinterpret_cast<uint64_t *>(base + off);
-    off += kSlots * 8;
-    s.empty = reinterpret_cast<uint64_t *>(base + off);
-    off += kSlots * 8;
-    s.abort_flag = reinterpret_cast<volatile int32_t *>(base + off);
-    s.decision = reinterpret_cast<volatile int32_t *>(base + off + 4);
+    s.ring = base + kOffRing;
+    s.xs = reinterpret_cast<float *>(base + kOffXs);
+    s.qn = s.xs;
+    s.kn = s.xs + 2 * kHeadDim;
+    s.xres = reinterpret_cast<float *>(base + kOffXres);
+    s.red = reinterpret_cast<float *>(base + kOffRed);
+    s.chain = reinterpret_cast<float *>(base + kOffChain);
+    s.hscal = reinterpret_cast<float *>(base + kOffHscal);
+    s.wbest = reinterpret_cast<float *>(base + kOffWbest);
+    s.wbest_i = reinterpret_cast<int32_t *>(base + kOffWbestI);
+    s.full = reinterpret_cast<uint64_t *>(base + kOffBars);
+    s.empty = reinterpret_cast<uint64_t *>(base + kOffBars + kSlots * 8);
+    s.abort_flag = reinterpret_cast<volatile int32_t *>(base + kOffFlags);
+    s.decision = reinterpret_cast<volatile int32_t *>(base + kOffFlags + 4);
     return s;
 }
 
 size_t decode_smem_bytes(int H, int I) {
-    size_t off = (size_t)kSlots * kSlotBytes + (size_t)4 * (H > I ? H : I) + 4 * kHeadDim * 4 + 64 * 4 +
-                 8 * 4 * 3;
-    off = (off + 7) & ~(size_t)7;
-    off += 2 * kSlots * 8 + 16;
-    return off;
+    return kOffXs + (size_t)4 * (H > I ? H : I);
+}
+
+extern __shared__ __align__(128) uint8_t smem_raw[];
+
+__device__ __forceinline__ const float *exp_table() {
+    return reinterpret_cast<const float *>(smem_raw + kOffExpTab);
 }
 
 /* --------------------------------------------------- block-level helpers */
 
 /* Deterministic sum over the 256 consumer threads of N values each: warp
- * butterfly, then a fixed pairwise tree over the 8 warps. */
+ * butterfly, then a fixed pairwise tree over the 8 warps. Over 256 inputs
+ * held one per thread this is exactly the balanced tree of
+ * gdn_tree_reduce_256 (c_impl/gdn_model.cpp:1336-1375). */
 template <int N>
 __device__ __forceinline__ void block_sum(float (&v)[N], float *red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -294,44 +377,108 @@ __device__ __forceinline__ void block_sum(float (&v)[N], float *red) {
     named_sync(1, kConsumerThreads);
 }
 
-/* Grid barrier among the consumer warps of all CTAs. Returns false when the
- * kernel is aborting (timeout here or an error raised by another CTA). The
- * answer is decided by thread 0 and published through s.decision before the
- * closing barrier, so every consumer thread sees the same value even if the
- * producer raises the abort flag meanwhile. */
-__device__ bool grid_sync(const DecodeParams &p, uint32_t index, const Smem &s) {
-    named_sync(1, kConsumerThreads);
-    if (threadIdx.x == 0 && *s.abort_flag == 0) {
-        const uint32_t target = p.bar_base + (index + 1u) * gridDim.x;
-        __threadfence();
-        atomicAdd(&p.status->bar, 1u);
-        uint64_t t0 = 0;
-        uint32_t spins = 0;
-        while (true) {
-            const uint32_t v = ld_acquire(&p.status->bar);
-            if ((int32_t)(v - target) >= 0) break;
-            if ((++spins & 255u) == 0) {
-                if (ld_volatile_i32(&p.status->err) != 0) {
-                    *s.abort_flag = 1;
-                    break;
-                }
-                const uint64_t now = gtimer();
-                if (t0 == 0) t0 = now;
-                else if (now - t0 > kWaitNs) {
-                    if (atomicCAS(&p.status->err, 0, kErrBarrierTimeout) == 0) {
-                        p.status->err_cta = blockIdx.x;
-                        p.status->err_where = index;
-                    }
-                    *s.abort_flag = 1;
-                    break;
-                }
+__device__ __forceinline__ void trace_put(const DecodeParams &p, int phase, int slot) {
+    if (p.trace != nullptr)
+        p.trace[((size_t)blockIdx.x * (p.L * kPhasesPerLayer + 1) + phase) * kTraceSlots + slot] = gtimer();
+}
+
+__device__ __forceinline__ void raise_error(const DecodeParams &p, const Smem &s, int code, uint32_t where) {
+    if (atomicCAS(&p.status->err, 0, code) == 0) {
+        p.status->err_cta = blockIdx.x;
+        p.status->err_where = where;
+    }
+    *s.abort_flag = 1;
+}
+
+/* Spin (with a short back-off) on one exchange word until it carries `tag`;
+ * returns the last word read, whose tag differs from `tag` on abort/timeout. */
+__device__ __noinline__ xword xwait(const DecodeParams &p, const Smem &s, const xword *a, uint32_t tag) {
+    const uint64_t t0 = gtimer();
+    uint32_t spins = 0;
+    while (true) {
+        const xword w = xget(a);
+        if (xtag(w) == tag) return w;
+        if (*s.abort_flag) return w;
+        if ((++spins & 63u) == 0) {
+            if (ld_volatile_i32(&p.status->err) != 0) {
+                *s.abort_flag = 1;
+                return w;
+            }
+            if (gtimer() - t0 > kWaitNs) {
+                raise_error(p, s, kErrExchangeTimeout, tag);
+                return w;
             }
         }
-        __threadfence();
     }
-    if (threadIdx.x == 0) *s.decision = (*s.abort_flag == 0) ? 1 : 0;
-    named_sync(1, kConsumerThreads);
-    return *s.decision != 0;
+}
+
+/* Warp-wide read of exchange words: lane i reads n (<= N) words at
+ * src_i + j * stride. While the producers are still busy only lane 0 polls,
+ * on the warp's last word (its likely latest); then every lane issues all its
+ * loads at once and re-issues the ones still carrying an old tag, round by
+ * round, so a late phase costs one round trip per round rather than one per
+ * word. All 32 lanes must call. */
+template <int N>
+__device__ __forceinline__ bool xread(const DecodeParams &p, const Smem &s, const xword *src, int stride, int n,
+                                      uint32_t tag, float (&v)[N]) {
+    const int lane = threadIdx.x & 31;
+    const xword *hint = reinterpret_cast<const xword *>(
+        __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(src + (size_t)(n - 1) * stride), 31));
+    int okw = 1;
+    if (lane == 0 && xtag(xget(hint)) != tag) okw = xtag(xwait(p, s, hint, tag)) == tag;
+    if (!__shfl_sync(0xffffffffu, okw, 0)) return false;
+    xword w[N];
+    uint32_t missing = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        if (i < n) w[i] = xget(src + (size_t)i * stride);
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        if (i < n && xtag(w[i]) != tag) missing |= 1u << i;
+    const uint64_t t0 = missing ? gtimer() : 0;
+    while (missing) {
+        if (*s.abort_flag) return false;
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+            if ((missing >> i) & 1u) w[i] = xget(src + (size_t)i * stride);
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+            if (((missing >> i) & 1u) && xtag(w[i]) == tag) missing &= ~(1u << i);
+        if (missing && gtimer() - t0 > kWaitNs) {
+            raise_error(p, s, kErrExchangeTimeout, tag);
+            return false;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        if (i < n) v[i] = xval(w[i]);
+    return true;
+}
+
+/* Read n exchange words (n/256 <= 32 per thread, element t + 256 j) into the
+ * permuted shared input, with xread's protocol. All consumer threads call. */
+__device__ __noinline__ bool xread_to_xs(const DecodeParams &p, const Smem &s, const xword *src, int n, uint32_t tag) {
+    const int t = threadIdx.x;
+    const int per = n >> 8;
+    bool ok = true;
+    for (int j0 = 0; j0 < per; j0 += 16) {
+        float v[16];
+        const int cnt = (per - j0) < 16 ? (per - j0) : 16;
+        ok = xread<16>(p, s, src + t + (j0 << 8), 256, cnt, tag, v) && ok;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (j < cnt) s.xs[xs_pos(t + ((j0 + j) << 8))] = v[j];
+    }
+    return ok;
+}
+
+/* Single-lane read of one exchange word (poll with back-off). */
+__device__ __forceinline__ bool xread1(const DecodeParams &p, const Smem &s, const xword *src, uint32_t tag,
+                                       float &v) {
+    xword w = xget(src);
+    if (xtag(w) != tag) w = xwait(p, s, src, tag);
+    v = xval(w);
+    return xtag(w) == tag;
 }
 
 /* Wait for a ring slot to be filled; false on abort. */
@@ -343,165 +490,303 @@ __device__ __forceinline__ bool wait_full(const DecodeParams &p, const Smem &s, 
         if (mbar_try(bar, parity)) return true;
         if (*s.abort_flag) return false;
         if (gtimer() - t0 > kWaitNs) {
-            if (atomicCAS(&p.status->err, 0, kErrChunkTimeout) == 0) {
-                p.status->err_cta = blockIdx.x;
-                p.status->err_where = slot;
-            }
-            *s.abort_flag = 1;
+            raise_error(p, s, kErrChunkTimeout, slot);
             return false;
         }
     }
 }
 
-/* Dot products of up to 4 BF16 rows (contiguous in a ring slot) with the
- * permuted input vector; every lane returns all sums. */
-__device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, const float *xs, float (&out)[4]) {
+/* Products of one BF16 weight with one input in the selected contract. */
+template <int MODE>
+__device__ __forceinline__ float prod(float w, float x) {
+    const float p = __fmul_rn(w, x);
+    return (MODE & 2) ? native_round(p) : p;
+}
+
+/* tree16 of one 16-column half (gemv32_tree16, c_impl/gdn_model.cpp:4004-4035):
+ * ((p0+p1)+(p2+p3)) + ((p4+p5)+(p6+p7)) ... over the 16 products. With BF16
+ * inputs and exact products a pair sum p0 + p1 equals fma(w1, x1, p0). */
+template <int MODE>
+__device__ __forceinline__ float tree16_half(const uint4 &w0, const uint4 &w1, const float4 &x0, const float4 &x1,
+                                             const float4 &x2, const float4 &x3) {
+    float s0, s1, s2, s3, s4, s5, s6, s7;
+    if (MODE == 1) {
+        s0 = fmaf(bf_hi(w0.x), x0.y, __fmul_rn(bf_lo(w0.x), x0.x));
+        s1 = fmaf(bf_hi(w0.y), x0.w, __fmul_rn(bf_lo(w0.y), x0.z));
+        s2 = fmaf(bf_hi(w0.z), x1.y, __fmul_rn(bf_lo(w0.z), x1.x));
+        s3 = fmaf(bf_hi(w0.w), x1.w, __fmul_rn(bf_lo(w0.w), x1.z));
+        s4 = fmaf(bf_hi(w1.x), x2.y, __fmul_rn(bf_lo(w1.x), x2.x));
+        s5 = fmaf(bf_hi(w1.y), x2.w, __fmul_rn(bf_lo(w1.y), x2.z));
+        s6 = fmaf(bf_hi(w1.z), x3.y, __fmul_rn(bf_lo(w1.z), x3.x));
+        s7 = fmaf(bf_hi(w1.w), x3.w, __fmul_rn(bf_lo(w1.w), x3.z));
+    } else {
+        s0 = __fadd_rn(prod<MODE>(bf_lo(w0.x), x0.x), prod<MODE>(bf_hi(w0.x), x0.y));
+        s1 = __fadd_rn(prod<MODE>(bf_lo(w0.y), x0.z), prod<MODE>(bf_hi(w0.y), x0.w));
+        s2 = __fadd_rn(prod<MODE>(bf_lo(w0.z), x1.x), prod<MODE>(bf_hi(w0.z), x1.y));
+        s3 = __fadd_rn(prod<MODE>(bf_lo(w0.w), x1.z), prod<MODE>(bf_hi(w0.w), x1.w));
+        s4 = __fadd_rn(prod<MODE>(bf_lo(w1.x), x2.x), prod<MODE>(bf_hi(w1.x), x2.y));
+        s5 = __fadd_rn(prod<MODE>(bf_lo(w1.y), x2.z), prod<MODE>(bf_hi(w1.y), x2.w));
+        s6 = __fadd_rn(prod<MODE>(bf_lo(w1.z), x3.x), prod<MODE>(bf_hi(w1.z), x3.y));
+        s7 = __fadd_rn(prod<MODE>(bf_lo(w1.w), x3.z), prod<MODE>(bf_hi(w1.w), x3.w));
+    }
+    const float a0 = __fadd_rn(s0, s1), a1 = __fadd_rn(s2, s3), a2 = __fadd_rn(s4, s5), a3 = __fadd_rn(s6, s7);
+    return __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+}
+
+/* Dot products of up to 4 BF16 rows (contiguous in a ring slot, columns
+ * permuted per 512-column group) with the shared input, summed in the
+ * reference's order (c_impl/gdn_model.cpp:4444-4586):
+ *   stage 1: lane l computes tree16 of half l of every group and parks it in
+ *            the warp's chain scratch at bank (half & 3) -- lo/hi half x
+ *            even/odd 32-column beat -- position half >> 2;
+ *   stage 2: lane 4r + b accumulates bank b of row r sequentially from 0;
+ *            row = (bank0 + bank1) + (bank2 + bank3).
+ * Rows flagged in `tiny` (the a/b projections, c_impl/gdn_model.cpp:1501-1535)
+ * instead take one sequential chain over all halves in column order.
+ * Every lane returns all row sums. */
+template <int MODE>
+__device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, unsigned tiny, const float *xs,
+                                         float *chain, uint32_t empty_bar, float (&out)[4]) {
     const int lane = threadIdx.x & 31;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    const int steps = K >> 8;
-    for (int st = 0; st < steps; ++st) {
-        const float4 xa = *reinterpret_cast<const float4 *>(xs + (st << 8) + (lane << 2));
-        const float4 xb = *reinterpret_cast<const float4 *>(xs + (st << 8) + 128 + (lane << 2));
-        const int col = (st << 8) + (lane << 3);
+    const int G = K >> 9;           /* 512-column groups */
+    const int C = K >> 6;           /* halves per bank of one row */
+    const int wpos = ((lane & 3) * C) + (lane >> 2);
+    const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+    for (int g = 0; g < G; ++g) {
+        const float4 x0 = xs4[(g << 7) + lane];
+        const float4 x1 = xs4[(g << 7) + 32 + lane];
+        const float4 x2 = xs4[(g << 7) + 64 + lane];
+        const float4 x3 = xs4[(g << 7) + 96 + lane];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             if (r < nrows) {
-                const uint4 w = *reinterpret_cast<const uint4 *>(slot + ((size_t)r * K + col) * 2);
-                float a = acc[r];
-                a = fmaf(bf_lo(w.x), xa.x, a);
-                a = fmaf(bf_hi(w.x), xa.y, a);
-                a = fmaf(bf_lo(w.y), xa.z, a);
-                a = fmaf(bf_hi(w.y), xa.w, a);
-                a = fmaf(bf_lo(w.z), xb.x, a);
-                a = fmaf(bf_hi(w.z), xb.y, a);
-                a = fmaf(bf_lo(w.w), xb.z, a);
-                a = fmaf(bf_hi(w.w), xb.w, a);
-                acc[r] = a;
+                const uint4 *wr = reinterpret_cast<const uint4 *>(slot + (size_t)r * K * 2) + (g << 6);
+                /* the a/b projections multiply exactly even in the c_impl
+                 * contract (c_impl/gdn_model.cpp:1517-1520) */
+                const float d = ((MODE & 2) && ((tiny >> r) & 1u))
+                                    ? tree16_half<MODE & 1>(wr[lane], wr[32 + lane], x0, x1, x2, x3)
+                                    : tree16_half<MODE>(wr[lane], wr[32 + lane], x0, x1, x2, x3);
+                chain[r * 4 * C + wpos + (g << 3)] = d;
             }
         }
     }
+    /* the weights have been read: hand the ring slot back before the bank
+     * chains and the epilogue, so it can be refilled sooner */
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);
+    const int r = lane >> 2, b = lane & 3;
+    float acc = 0.0f;
+    const bool is_tiny = r < nrows && ((tiny >> r) & 1u);
+    if (r < nrows) {
+        if (!is_tiny) {
+            const float *c = chain + (r * 4 + b) * C;
+            for (int k = 0; k < C; k += 4) {
+                const float4 v = *reinterpret_cast<const float4 *>(c + k);
+                acc = __fadd_rn(acc, v.x);
+                acc = __fadd_rn(acc, v.y);
+                acc = __fadd_rn(acc, v.z);
+                acc = __fadd_rn(acc, v.w);
+            }
+        } else if (b == 0) {
+            const float *c = chain + r * 4 * C;
+            for (int k = 0; k < C; ++k) {
+                acc = __fadd_rn(acc, c[k]);
+                acc = __fadd_rn(acc, c[C + k]);
+                acc = __fadd_rn(acc, c[2 * C + k]);
+                acc = __fadd_rn(acc, c[3 * C + k]);
+            }
+        }
+    }
+    const float t = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));  /* b=0: bank0+bank1, b=2: bank2+bank3 */
+    const float t2 = __shfl_down_sync(0xffffffffu, t, 2);
+    const float total = is_tiny ? acc : __fadd_rn(t, t2);
 #pragma unroll
-    for (int r = 0; r < 4; ++r) out[r] = warp_sum(acc[r]);
+    for (int q = 0; q < 4; ++q) out[q] = __shfl_sync(0xffffffffu, total, q << 2);
+    __syncwarp();
 }
 
 /* ---------------------------------------------------------- prologues */
 
-/* x = round(a + b) (or the embedding for layer 0), optional store of x,
- * then RMSNorm with weight w into the permuted shared input
- * (c_impl/gdn_model.cpp:3351-3452, 1394-1476). */
-template <bool BF16B>
-__device__ void prologue_residual_norm(const DecodeParams &p, const Smem &s, const float *a, const float *b,
-                                       const float *w, float *x_store, bool embed) {
+/* Residual add + RMSNorm into the permuted shared input, in the reference's
+ * order (c_impl/gdn_model.cpp:1394-1476, 3351-3452): thread t < H/16 owns the
+ * 16-column half t (beat t/2, half t%2): x = round(xres + y) (or the embedding
+ * for layer 0), s_t = its squares summed sequentially; then thread 0 sums the
+ * s_t sequentially; scale = 1/sqrtf(sum/H + eps); out = round((x*scale)*w). */
+template <int MODE>
+__device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s, const xword *y, uint32_t tag, const float *w,
+                              bool embed, float *hidden, int pidx) {
     const int t = threadIdx.x;
-    const int H = p.H;
-    const int per = H >> 8;
-    float xv[8];
-    float sq[1] = {0.0f};
-    int32_t tok = -1;
-    if (embed && p.token_src != nullptr) tok = *p.token_src;
-    for (int j = 0; j < per; ++j) {
-        const int i = t + (j << 8);
-        float x;
+    const int halves = p.H >> 4;
+    bool ok = true;
+    float wv[16];
+    if (t < halves) {
+        float x[16];
+        const float4 *w4 = reinterpret_cast<const float4 *>(w + 16 * t);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 v = __ldg(w4 + q);
+            wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
+        }
         if (embed) {
             if (p.token_src != nullptr) {
-                const uint16_t e = p.emb[(size_t)tok * H + i];
-                x = __uint_as_float((uint32_t)e << 16);
+                const int32_t tok = *p.token_src;
+                const uint16_t *e = p.emb + (size_t)tok * p.H + 16 * t;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) x[i] = bnd<MODE>(__uint_as_float((uint32_t)e[i] << 16));
             } else {
-                x = p.x_embed[i];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) x[i] = bnd<MODE>(p.x_embed[16 * t + i]);
             }
-            x = bnd<BF16B>(x);
         } else {
-            x = bnd<BF16B>(__fadd_rn(__ldcg(a + i), __ldcg(b + i)));
+            float yv[16];
+            ok = xread<16>(p, s, y + 16 * t, 1, 16, tag, yv);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) x[i] = bnd<MODE>(__fadd_rn(s.xres[16 * t + i], yv[i]));
         }
-        xv[j] = x;
-        sq[0] = fmaf(x, x, sq[0]);
-        if (x_store != nullptr) x_store[i] = x;
+        if (t == 0) trace_put(p, pidx, 1);
+        float hs = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            hs = __fadd_rn(hs, __fmul_rn(x[i], x[i]));
+            s.xres[16 * t + i] = x[i];
+        }
+        s.red[t] = hs;
     }
-    block_sum<1>(sq, s.red);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq[0], (float)H), p.eps)));
-    for (int j = 0; j < per; ++j) {
-        const int i = t + (j << 8);
-        s.xs[xs_pos(i)] = bnd<BF16B>(__fmul_rn(__fmul_rn(xv[j], scale), __ldg(w + i)));
+    named_sync(1, kConsumerThreads);
+    if (t == 0) {
+        float sum = 0.0f;
+        for (int j = 0; j < halves; j += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(s.red + j);
+            sum = __fadd_rn(sum, v.x);
+            sum = __fadd_rn(sum, v.y);
+            sum = __fadd_rn(sum, v.z);
+            sum = __fadd_rn(sum, v.w);
+        }
+        s.red[128] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)p.H), p.eps)));
+        trace_put(p, pidx, 6);
     }
+    named_sync(1, kConsumerThreads);
+    const float scale = s.red[128];
+    if (t < halves) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float o = bnd<MODE>(__fmul_rn(__fmul_rn(s.xres[16 * t + i], scale), wv[i]));
+            s.xs[xs_pos(16 * t + i)] = o;
+            if (hidden != nullptr) hidden[16 * t + i] = o;
+        }
+    }
+    return ok;
 }
 
-/* Per-head RMSNorm of the attention output times swish(gate), into the
- * permuted shared input (c_impl/gdn_model.cpp:3226-3349). Element i = t +
- * 256 j belongs to head j. */
-template <bool BF16B>
-__device__ void prologue_norm_gate(const DecodeParams &p, const Smem &s, const float *o_norm) {
+/* Per-head RMSNorm of the attention output times swish(gate) in the
+ * reference's order (c_impl/gdn_model.cpp:3226-3349): per head, 16 half sums
+ * of 16 sequential squares, summed sequentially; scale = 1/sqrtf(sum/256 +
+ * eps); out = round(((a*scale)*w) * g * sigmoid(g)). */
+template <int MODE>
+__device__ __noinline__ bool prologue_norm_gate(const DecodeParams &p, const Smem &s, const float *o_norm, uint32_t tag_a,
+                                   uint32_t tag_b, int pidx) {
     const int t = threadIdx.x;
-    float av[8], sq[8];
+    const int halves = p.H >> 4;
+    bool ok = true;
+    float wv[16];
+    float *a_sh = s.chain, *g_sh = s.chain + p.H;   /* H <= 2048: both fit the 16 KB scratch */
+    if (t < halves) {
+        float a[16], g[16];
+        const float4 *w4 = reinterpret_cast<const float4 *>(o_norm + 16 * (t & 15));
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        sq[j] = 0.0f;
-        av[j] = 0.0f;
-        if (j < p.nh) {
-            av[j] = __ldcg(p.attn + t + (j << 8));
-            sq[j] = __fmul_rn(av[j], av[j]);
+        for (int q = 0; q < 4; ++q) {
+            const float4 v = __ldg(w4 + q);
+            wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
+        }
+        ok = xread<16>(p, s, p.attn + 16 * t, 1, 16, tag_b, a);
+        ok = xread<16>(p, s, p.gate + 16 * t, 1, 16, tag_a, g) && ok;
+        if (t == 0) trace_put(p, pidx, 1);
+        float hs = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            hs = __fadd_rn(hs, __fmul_rn(a[i], a[i]));
+            a_sh[16 * t + i] = a[i];
+            g_sh[16 * t + i] = g[i];
+        }
+        s.red[t] = hs;
+    }
+    named_sync(1, kConsumerThreads);
+    if (t < p.nh) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum = __fadd_rn(sum, s.red[16 * t + j]);
+        s.hscal[8 + t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 256.0f), p.eps)));
+        if (t == 0) trace_put(p, pidx, 6);
+    }
+    named_sync(1, kConsumerThreads);
+    if (t < halves) {
+        const float scale = s.hscal[8 + (t >> 4)];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float gi = g_sh[16 * t + i];
+            const float normalized = __fmul_rn(__fmul_rn(a_sh[16 * t + i], scale), wv[i]);
+            s.xs[xs_pos(16 * t + i)] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gi), sigmoid_ref(gi)));
         }
     }
-    block_sum<8>(sq, s.red);
-    const float w = __ldg(o_norm + t);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        if (j < p.nh) {
-            const int i = t + (j << 8);
-            const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq[j], 256.0f), p.eps)));
-            const float g = __ldcg(p.gate + i);
-            const float normalized = __fmul_rn(__fmul_rn(av[j], scale), w);
-            s.xs[xs_pos(i)] = bnd<BF16B>(__fmul_rn(__fmul_rn(normalized, g), sigmoid_ref(g)));
-        }
-    }
+    return ok;
 }
 
 /* q/k L2 norms (balanced tree order of gdn_tree_reduce_256), alpha, beta
  * and decay for the CTA's heads (c_impl/gdn_model.cpp:2059-2124). */
-__device__ void prologue_state(const DecodeParams &p, const Smem &s, int l, int h0, int h1) {
+__device__ __noinline__ bool prologue_state(const DecodeParams &p, const Smem &s, int l, int h0, int h1, uint32_t tag) {
     const int t = threadIdx.x;
     const float *aux = p.aux + (size_t)l * p.aux_stride;
     const float *a_log = aux + 14 * p.H + kHeadDim;
     const float *dt_bias = a_log + p.nh;
+    bool ok = true;
     for (int hs = 0; hs <= h1 - h0; ++hs) {
         const int h = h0 + hs;
-        const float q = __ldcg(p.qkv + h * kHeadDim + t);
-        const float k = __ldcg(p.qkv + p.H + h * kHeadDim + t);
-        float v2[2] = {__fmul_rn(q, q), __fmul_rn(k, k)};
-        block_sum<2>(v2, s.red);
-        const float q_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(v2[0], 1e-6f)));
-        const float k_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(v2[1], 1e-6f)));
-        const float qn = __fmul_rn(q, q_inv), kn = __fmul_rn(k, k_inv);
+        float qk[2];
+        float qv[1], kv[1];
+        ok = xread<1>(p, s, p.qkv + h * kHeadDim + t, 1, 1, tag, qv) && ok;
+        ok = xread<1>(p, s, p.qkv + p.H + h * kHeadDim + t, 1, 1, tag, kv) && ok;  /* all 256 threads */
+        qk[0] = __fmul_rn(qv[0], qv[0]);
+        qk[1] = __fmul_rn(kv[0], kv[0]);
+        block_sum<2>(qk, s.red);
+        const float q_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(qk[0], 1e-6f)));
+        const float k_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(qk[1], 1e-6f)));
+        const float qn = __fmul_rn(qv[0], q_inv), kn = __fmul_rn(kv[0], k_inv);
         s.qn[hs * kHeadDim + t] = qn;
         s.kn[hs * kHeadDim + t] = kn;
         float al[1] = {__fmul_rn(qn, kn)};
         block_sum<1>(al, s.red);
         if (t == 0) {
-            const float beta = sigmoid_ref(__ldcg(p.ab + p.nh + h));
-            const float decay_in = __fadd_rn(__ldcg(p.ab + h), __ldg(dt_bias + h));
-            const float decay_val = __fmul_rn(-expf(__ldg(a_log + h)), softplus_ref(decay_in));
+            float av, bv;
+            ok = xread1(p, s, p.ab + h, tag, av) && ok;
+            ok = xread1(p, s, p.ab + p.nh + h, tag, bv) && ok;
+            const float beta = sigmoid_ref(bv);
+            const float decay_in = __fadd_rn(av, __ldg(dt_bias + h));
+            const float decay_val = __fmul_rn(-exp_ref(__ldg(a_log + h)), softplus_ref(decay_in));
             s.hscal[hs * 4 + 0] = al[0];
             s.hscal[hs * 4 + 1] = beta;
-            s.hscal[hs * 4 + 2] = expf(decay_val);
+            s.hscal[hs * 4 + 2] = exp_ref(decay_val);
         }
     }
-    named_sync(1, kConsumerThreads);
+    return ok;
 }
 
 /* ------------------------------------------------------------ the kernel */
 
-template <bool BF16B>
+template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodeParams p) {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem s = carve(smem_raw, p.H, p.I);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t cta = blockIdx.x, ncta = gridDim.x;
 
+    if (threadIdx.x < 128)
+        reinterpret_cast<float *>(smem_raw + kOffExpTab)[threadIdx.x] = __ldg(p.exp_table + threadIdx.x);
     if (threadIdx.x == 0) {
         for (int i = 0; i < kSlots; ++i) {
             mbar_init(smem_u32(&s.full[i]), 1);
             mbar_init(smem_u32(&s.empty[i]), 1);
         }
         *s.abort_flag = 0;
+        *s.decision = 1;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -513,6 +798,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
             const uint64_t pol_s = policy_evict_last();
             uint32_t seq = 0;
             bool ok = true;
+            Cursor pf;
+            cursor_init(p, pf, cta, ncta);
+            uint32_t pf_ahead = 0;  /* bytes prefetched into L2 but not yet copied to the ring */
             for (int l = 0; l <= p.L && ok; ++l) {
                 const int nph = (l < p.L) ? kPhasesPerLayer : 1;
                 for (int pi = 0; pi < nph && ok; ++pi) {
@@ -529,11 +817,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                                 while (!mbar_try(bar, par)) {
                                     if (*s.abort_flag) { ok = false; break; }
                                     if (gtimer() - t0 > kWaitNs) {
-                                        if (atomicCAS(&p.status->err, 0, kErrSlotTimeout) == 0) {
-                                            p.status->err_cta = cta;
-                                            p.status->err_where = seq;
-                                        }
-                                        *s.abort_flag = 1;
+                                        raise_error(p, s, kErrSlotTimeout, seq);
                                         ok = false;
                                         break;
                                     }
@@ -543,7 +827,21 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                         }
                         if (*s.abort_flag) { ok = false; break; }
                         const uint32_t bytes = n * g.unit_bytes;
+                        while (pf_ahead < (uint32_t)kPrefetchBytes && cursor_valid(p, pf)) {
+                            const uint32_t pn = (pf.g.u1 - pf.u) < pf.g.upc ? (pf.g.u1 - pf.u) : pf.g.upc;
+                            const uint32_t pbytes = pn * pf.g.unit_bytes;
+                            bulk_prefetch_l2(pf.g.src + (size_t)pf.u * pf.g.unit_bytes, pbytes);
+                            pf_ahead += pbytes;
+                            pf.u += pf.g.upc;
+                            cursor_settle(p, pf, cta, ncta);
+                        }
+                        pf_ahead -= bytes;
                         const uint32_t fb = smem_u32(&s.full[slot]);
+                        if (p.trace != nullptr) {
+                            const int pidx = l * kPhasesPerLayer + pi;
+                            if (u == g.u0) trace_put(p, pidx, 4);
+                            trace_put(p, pidx, 5);
+                        }
                         mbar_expect_tx(fb, bytes);
                         bulk_g2s(smem_u32(s.ring + (size_t)slot * kSlotBytes), g.src + (size_t)u * g.unit_bytes,
                                  bytes, fb, ph == PH_STATE ? pol_s : pol_w);
@@ -566,21 +864,23 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
     } else {
         /* ---------------------------------------------- consumer warps */
         uint32_t seq = 0;
-        uint32_t bar_index = 0;
         float best = -3.402823466e38f;
         int32_t best_i = 0;
         bool ok = true;
         for (int l = 0; l <= p.L && ok; ++l) {
             const int nph = (l < p.L) ? kPhasesPerLayer : 1;
             const float *aux = p.aux + (size_t)(l < p.L ? l : 0) * p.aux_stride;
+            const uint32_t tag_base = p.epoch + (uint32_t)(l * kPhasesPerLayer);
             for (int pi = 0; pi < nph && ok; ++pi) {
                 const int ph = (l < p.L) ? pi : PH_LM;
+                const int pidx = l * kPhasesPerLayer + pi;
                 const Geom g = geom(p, l < p.L ? l : 0, ph, cta, ncta);
-                if (!(l == 0 && ph == PH_QKVG)) {
-                    if (!grid_sync(p, bar_index++, s)) { ok = false; break; }
-                }
+                /* every consumer warp is done with the previous phase's chunks
+                 * (shared inputs may be overwritten) */
+                named_sync(1, kConsumerThreads);
+                if (threadIdx.x == 0) trace_put(p, pidx, 0);
                 int h0 = 0, h1 = 0;
-                /* phase input */
+                bool in_ok = true;
                 switch (ph) {
                 case PH_QKVG:
                     if (l == 0) {
@@ -588,54 +888,55 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                             const int32_t tok = *p.token_src;
                             if (tok < 0 || tok >= p.V) {
                                 /* every consumer thread reads the same token: uniform exit */
-                                if (threadIdx.x == 0) {
-                                    atomicCAS(&p.status->err, 0, kErrBadToken);
-                                    *s.abort_flag = 1;
-                                }
+                                if (threadIdx.x == 0) raise_error(p, s, kErrBadToken, (uint32_t)tok);
                                 ok = false;
                                 break;
                             }
                         }
-                        prologue_residual_norm<BF16B>(p, s, nullptr, nullptr, aux, cta == 0 ? p.x_in : nullptr, true);
+                        in_ok = prologue_norm<MODE>(p, s, nullptr, 0, aux, true, nullptr, pidx);
                     } else {
-                        prologue_residual_norm<BF16B>(p, s, p.x_mid, p.y_down, aux, cta == 0 ? p.x_in : nullptr,
-                                                      false);
+                        in_ok = prologue_norm<MODE>(p, s, p.y_down, tag_base - kPhasesPerLayer + PH_DOWN, aux,
+                                                    false, nullptr, pidx);
                     }
                     break;
                 case PH_STATE:
                     if (g.u1 > g.u0) {
                         h0 = (int)(g.u0 >> 8);
                         h1 = (int)((g.u1 - 1) >> 8);
-                        prologue_state(p, s, l, h0, h1);
+                        in_ok = prologue_state(p, s, l, h0, h1, tag_base + PH_QKVG);
+                        if (threadIdx.x == 0) trace_put(p, pidx, 1);
                     }
                     break;
                 case PH_O:
-                    prologue_norm_gate<BF16B>(p, s, aux + p.H);
+                    in_ok = prologue_norm_gate<MODE>(p, s, aux + p.H, tag_base + PH_QKVG, tag_base + PH_STATE, pidx);
                     break;
                 case PH_GU:
-                    prologue_residual_norm<BF16B>(p, s, p.x_in, p.y_o, aux + p.H + kHeadDim,
-                                                  cta == 0 ? p.x_mid : nullptr, false);
+                    in_ok = prologue_norm<MODE>(p, s, p.y_o, tag_base + PH_O, aux + p.H + kHeadDim, false, nullptr, pidx);
                     break;
                 case PH_DOWN:
-                    for (int i = threadIdx.x; i < p.I; i += kConsumerThreads) s.xs[xs_pos(i)] = __ldcg(p.m + i);
+                    in_ok = xread_to_xs(p, s, p.m, p.I, tag_base + PH_GU);
+                    if (threadIdx.x == 0) trace_put(p, pidx, 1);
                     break;
                 default: {
                     const float *final_norm = p.aux + (size_t)p.L * p.aux_stride;
-                    prologue_residual_norm<BF16B>(p, s, p.x_mid, p.y_down, final_norm, nullptr, false);
+                    in_ok = prologue_norm<MODE>(p, s, p.y_down,
+                                                p.epoch + (uint32_t)((p.L - 1) * kPhasesPerLayer + PH_DOWN),
+                                                final_norm, false, cta == 0 ? p.hidden_out : nullptr, pidx);
                     break;
                 }
                 }
                 if (!ok) break;
+                (void)in_ok;  /* a failed read has raised the abort flag */
+                if (threadIdx.x == 0) *s.decision = (*s.abort_flag == 0) ? 1 : 0;
                 named_sync(1, kConsumerThreads);
-                if (ph == PH_LM && cta == 0 && p.hidden_out != nullptr) {
-                    for (int i = threadIdx.x; i < p.H; i += kConsumerThreads) p.hidden_out[i] = s.xs[xs_pos(i)];
-                }
+                if (*s.decision == 0) { ok = false; break; }
+                if (threadIdx.x == 0) trace_put(p, pidx, 2);
 
-                /* chunks of this phase: warp w takes every 8th */
-                /* A warp that gives up (abort) skips its remaining chunks but
-                 * keeps walking the schedule, so that all consumer warps meet
-                 * the same named barriers; the stop is taken uniformly at the
-                 * next grid_sync. */
+                const uint32_t tag_out = tag_base + (uint32_t)ph;
+                /* chunks of this phase: warp w takes every 8th. A warp that
+                 * gives up (abort) skips its remaining chunks but keeps walking
+                 * the schedule, so all consumer warps meet the same named
+                 * barriers; the stop is taken uniformly at the next phase. */
                 for (uint32_t u = g.u0; u < g.u1; u += g.upc, ++seq) {
                     if ((int)(seq % kConsumerWarps) != warp) continue;
                     if (*s.abort_flag) continue;
@@ -657,41 +958,54 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                                 aux + 2 * p.H + kHeadDim + ((size_t)row_kind * p.H + d) * 4));
                         }
                     }
+                    float vv = 0.0f;
+                    if (ph == PH_STATE && lane < (int)n) xread1(p, s, p.qkv + 2 * p.H + u + lane, tag_base + PH_QKVG, vv);
 
                     if (!wait_full(p, s, slot, (seq / kSlots) & 1u)) continue;
 
                     if (ph == PH_STATE) {
+                        /* read pass, sequential over k for each column (lane j owns
+                         * column u + j), c_impl/gdn_model.cpp:2184-2210 */
+                        float r = 0.0f, pp = 0.0f;
+                        if (lane < (int)n) {
+                            const int hs = (int)((u + lane) >> 8) - h0;
+                            const float4 *col = reinterpret_cast<const float4 *>(buf) + lane * (kHeadDim / 4);
+                            const float4 *kn4 = reinterpret_cast<const float4 *>(s.kn + hs * kHeadDim);
+                            const float4 *qn4 = reinterpret_cast<const float4 *>(s.qn + hs * kHeadDim);
+#pragma unroll 4
+                            for (int k = 0; k < kHeadDim / 4; ++k) {
+                                const float4 sv = col[k], kv = kn4[k], qv = qn4[k];
+                                r = __fadd_rn(r, __fmul_rn(sv.x, kv.x));
+                                pp = __fadd_rn(pp, __fmul_rn(sv.x, qv.x));
+                                r = __fadd_rn(r, __fmul_rn(sv.y, kv.y));
+                                pp = __fadd_rn(pp, __fmul_rn(sv.y, qv.y));
+                                r = __fadd_rn(r, __fmul_rn(sv.z, kv.z));
+                                pp = __fadd_rn(pp, __fmul_rn(sv.z, qv.z));
+                                r = __fadd_rn(r, __fmul_rn(sv.w, kv.w));
+                                pp = __fadd_rn(pp, __fmul_rn(sv.w, qv.w));
+                            }
+                        }
                         for (uint32_t j = 0; j < n; ++j) {
                             const uint32_t c = u + j;
                             const int hs = (int)(c >> 8) - h0;
-                            const float *col = reinterpret_cast<const float *>(buf) + j * kHeadDim + lane * 8;
-                            const float4 s0 = *reinterpret_cast<const float4 *>(col);
-                            const float4 s1 = *reinterpret_cast<const float4 *>(col + 4);
-                            const float *qn = s.qn + hs * kHeadDim + lane * 8;
-                            const float *kn = s.kn + hs * kHeadDim + lane * 8;
-                            const float4 q0 = *reinterpret_cast<const float4 *>(qn);
-                            const float4 q1 = *reinterpret_cast<const float4 *>(qn + 4);
-                            const float4 k0 = *reinterpret_cast<const float4 *>(kn);
-                            const float4 k1 = *reinterpret_cast<const float4 *>(kn + 4);
-                            float r = 0.0f, pp = 0.0f;
-                            r = fmaf(s0.x, k0.x, r); pp = fmaf(s0.x, q0.x, pp);
-                            r = fmaf(s0.y, k0.y, r); pp = fmaf(s0.y, q0.y, pp);
-                            r = fmaf(s0.z, k0.z, r); pp = fmaf(s0.z, q0.z, pp);
-                            r = fmaf(s0.w, k0.w, r); pp = fmaf(s0.w, q0.w, pp);
-                            r = fmaf(s1.x, k1.x, r); pp = fmaf(s1.x, q1.x, pp);
-                            r = fmaf(s1.y, k1.y, r); pp = fmaf(s1.y, q1.y, pp);
-                            r = fmaf(s1.z, k1.z, r); pp = fmaf(s1.z, q1.z, pp);
-                            r = fmaf(s1.w, k1.w, r); pp = fmaf(s1.w, q1.w, pp);
-                            r = warp_sum(r);
-                            pp = warp_sum(pp);
+                            const float rj = __shfl_sync(0xffffffffu, r, j);
+                            const float pj = __shfl_sync(0xffffffffu, pp, j);
+                            const float vj = __shfl_sync(0xffffffffu, vv, j);
                             const float alpha = s.hscal[hs * 4 + 0];
                             const float beta = s.hscal[hs * 4 + 1];
                             const float decay = s.hscal[hs * 4 + 2];
-                            const float vv = __ldcg(p.qkv + 2 * p.H + c);
-                            /* c_impl/gdn_model.cpp:2214-2243, 2268-2300 */
-                            const float delta = __fmul_rn(beta, __fsub_rn(vv, __fmul_rn(decay, r)));
-                            const float o = __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pp), __fmul_rn(alpha, delta)));
-                            if (lane == 0) p.attn[c] = bnd<BF16B>(o);
+                            /* c_impl/gdn_model.cpp:2214-2243 */
+                            const float delta = __fmul_rn(beta, __fsub_rn(vj, __fmul_rn(decay, rj)));
+                            const float o =
+                                __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pj), __fmul_rn(alpha, delta)));
+                            if (lane == 0) xput(p.attn + c, bnd<MODE>(o), tag_out);
+                            /* update, c_impl/gdn_model.cpp:2268-2300 */
+                            const float *colp = reinterpret_cast<const float *>(buf) + j * kHeadDim + lane * 8;
+                            const float *knp = s.kn + hs * kHeadDim + lane * 8;
+                            const float4 s0 = *reinterpret_cast<const float4 *>(colp);
+                            const float4 s1 = *reinterpret_cast<const float4 *>(colp + 4);
+                            const float4 k0 = *reinterpret_cast<const float4 *>(knp);
+                            const float4 k1 = *reinterpret_cast<const float4 *>(knp + 4);
                             float4 n0, n1;
                             n0.x = __fadd_rn(__fmul_rn(decay, s0.x), __fmul_rn(k0.x, delta));
                             n0.y = __fadd_rn(__fmul_rn(decay, s0.y), __fmul_rn(k0.y, delta));
@@ -701,6 +1015,12 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                             n1.y = __fadd_rn(__fmul_rn(decay, s1.y), __fmul_rn(k1.y, delta));
                             n1.z = __fadd_rn(__fmul_rn(decay, s1.z), __fmul_rn(k1.z, delta));
                             n1.w = __fadd_rn(__fmul_rn(decay, s1.w), __fmul_rn(k1.w, delta));
+                            if (p.bf16_state) {
+                                n0.x = bf16_round(n0.x); n0.y = bf16_round(n0.y);
+                                n0.z = bf16_round(n0.z); n0.w = bf16_round(n0.w);
+                                n1.x = bf16_round(n1.x); n1.y = bf16_round(n1.y);
+                                n1.z = bf16_round(n1.z); n1.w = bf16_round(n1.w);
+                            }
                             float *dst = p.S + ((size_t)l * p.nh * kHeadDim + c) * kHeadDim + lane * 8;
                             __stcg(reinterpret_cast<float4 *>(dst), n0);
                             __stcg(reinterpret_cast<float4 *>(dst + 4), n1);
@@ -708,16 +1028,22 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                     } else {
                         const int K = (ph == PH_DOWN) ? p.I : p.H;
                         float out[4];
-                        warp_dot(buf, K, (int)((ph == PH_GU) ? 2 * n : n), s.xs, out);
+                        unsigned tiny = 0;
+                        if (ph == PH_QKVG) {
+                            for (uint32_t j = 0; j < n; ++j)
+                                if (u + j >= 4u * p.H) tiny |= 1u << j;
+                        }
+                        warp_dot<MODE>(buf, K, (int)((ph == PH_GU) ? 2 * n : n), tiny, s.xs,
+                                       s.chain + warp * 512, smem_u32(&s.empty[slot]), out);
+                        float y = out[0];
+                        if (lane == 1) y = out[1];
+                        if (lane == 2) y = out[2];
+                        if (lane == 3) y = out[3];
                         switch (ph) {
-                        case PH_QKVG: {
-                            float y = out[0];
-                            if (lane == 1) y = out[1];
-                            if (lane == 2) y = out[2];
-                            if (lane == 3) y = out[3];
+                        case PH_QKVG:
                             if (lane < (int)n) {
                                 const uint32_t r = u + lane;
-                                const float raw = bnd<BF16B>(y);
+                                const float raw = bnd<MODE>(y);
                                 if (row_kind >= 0) {
                                     /* depthwise conv over [t0 t1 t2 new] + SiLU, left to right
                                      * (c_impl/gdn_model.cpp:1630-1650), then the window shift */
@@ -725,40 +1051,32 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                                         __fadd_rn(__fadd_rn(__fmul_rn(tail.x, cw.x), __fmul_rn(tail.y, cw.y)),
                                                   __fmul_rn(tail.z, cw.z)),
                                         __fmul_rn(raw, cw.w));
-                                    p.qkv[r] = bnd<BF16B>(silu_ref(sum));
+                                    xput(p.qkv + r, bnd<MODE>(silu_ref(sum)), tag_out);
                                     const uint32_t d = r - (uint32_t)row_kind * p.H;
                                     __stcg(reinterpret_cast<float4 *>(
                                                p.tails + (((size_t)l * 3 + row_kind) * p.H + d) * 4),
                                            make_float4(tail.y, tail.z, raw, 0.0f));
                                 } else if (r < 4u * p.H) {
-                                    p.gate[r - 3u * p.H] = raw;
+                                    xput(p.gate + (r - 3u * p.H), raw, tag_out);
                                 } else {
-                                    p.ab[r - 4u * p.H] = raw;
+                                    xput(p.ab + (r - 4u * p.H), raw, tag_out);
                                 }
                             }
                             break;
-                        }
                         case PH_O:
-                        case PH_DOWN: {
-                            float y = out[0];
-                            if (lane == 1) y = out[1];
-                            if (lane == 2) y = out[2];
-                            if (lane == 3) y = out[3];
-                            if (lane < (int)n) (ph == PH_O ? p.y_o : p.y_down)[u + lane] = bnd<BF16B>(y);
+                            if (lane < (int)n) xput(p.y_o + u + lane, bnd<MODE>(y), tag_out);
                             break;
-                        }
+                        case PH_DOWN:
+                            if (lane < (int)n) xput(p.y_down + u + lane, bnd<MODE>(y), tag_out);
+                            break;
                         case PH_GU: {
                             /* rows [g_u, u_u, g_u+1, u_u+1]; SwiGLU as c_impl/gdn_model.cpp:4751-4770 */
-                            const float gv = bnd<BF16B>(lane == 0 ? out[0] : out[2]);
-                            const float uv = bnd<BF16B>(lane == 0 ? out[1] : out[3]);
-                            if (lane < (int)n) p.m[u + lane] = bnd<BF16B>(__fmul_rn(silu_ref(gv), uv));
+                            const float gv = bnd<MODE>(lane == 0 ? out[0] : out[2]);
+                            const float uv = bnd<MODE>(lane == 0 ? out[1] : out[3]);
+                            if (lane < (int)n) xput(p.m + u + lane, bnd<MODE>(__fmul_rn(silu_ref(gv), uv)), tag_out);
                             break;
                         }
-                        default: {
-                            float y = out[0];
-                            if (lane == 1) y = out[1];
-                            if (lane == 2) y = out[2];
-                            if (lane == 3) y = out[3];
+                        default:
                             if (lane < (int)n) p.logits[u + lane] = y;
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
@@ -769,21 +1087,19 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                             }
                             break;
                         }
-                        }
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(smem_u32(&s.empty[slot]));
+                    if (ph == PH_STATE && lane == 0) mbar_arrive(smem_u32(&s.empty[slot]));
                 }
+                if (threadIdx.x == 0) trace_put(p, pidx, 3);
             }
         }
 
         /* LM-head argmax: warps -> CTA candidate -> the last CTA picks the token */
-        if (ok) {
-            if (threadIdx.x == 0) *s.decision = (*s.abort_flag == 0) ? 1 : 0;
-            named_sync(1, kConsumerThreads);
-            ok = *s.decision != 0;
-        }
-        if (ok) {
+        named_sync(1, kConsumerThreads);
+        if (threadIdx.x == 0) *s.decision = (ok && *s.abort_flag == 0) ? 1 : 0;
+        named_sync(1, kConsumerThreads);
+        if (*s.decision != 0) {
             if (lane == 0) {
                 s.wbest[warp] = best;
                 s.wbest_i[warp] = best_i;
@@ -822,20 +1138,24 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
     __syncthreads();
 }
 
+template <int MODE>
+static cudaError_t launch_mode(const DecodeParams &p, int grid, cudaStream_t stream, size_t smem) {
+    void *args[] = {const_cast<DecodeParams *>(&p)};
+    const cudaError_t e =
+        cudaFuncSetAttribute(gdn_decode_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return cudaLaunchCooperativeKernel((const void *)gdn_decode_kernel<MODE>, dim3(grid), dim3(kThreads), args, smem,
+                                       stream);
+}
+
+/* MODE bit 0: BF16 boundaries; bit 1: BF16-rounded products (needs bit 0). */
 cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t stream) {
     const size_t smem = decode_smem_bytes(p.H, p.I);
-    void *args[] = {const_cast<DecodeParams *>(&p)};
-    cudaError_t e;
-    if (p.bf16_boundary) {
-        e = cudaFuncSetAttribute(gdn_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        return cudaLaunchCooperativeKernel((const void *)gdn_decode_kernel<true>, dim3(grid), dim3(kThreads), args,
-                                           smem, stream);
+    if (!p.bf16_boundary) {
+        if (p.native_product) return cudaErrorInvalidValue;
+        return launch_mode<0>(p, grid, stream, smem);
     }
-    e = cudaFuncSetAttribute(gdn_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    return cudaLaunchCooperativeKernel((const void *)gdn_decode_kernel<false>, dim3(grid), dim3(kThreads), args,
-                                       smem, stream);
+    return p.native_product ? launch_mode<3>(p, grid, stream, smem) : launch_mode<1>(p, grid, stream, smem);
 }
 
 }  // namespace gdn

@@ -4,7 +4,10 @@
  *
  * Device image of one model (all pointers device memory, built once per
  * GDNModel and shared by every run state):
- *   per layer l, at wimg + l * layer_stride bytes, BF16 row-major [out][in]:
+ *   per layer l, at wimg + l * layer_stride bytes, BF16 rows [out][in] whose
+ *   columns are permuted inside every 512-column group: the group stores the
+ *   first 8 columns of each of its 32 sixteen-column halves, then the last 8
+ *   (so lane l of a warp reads half l with two conflict-free 16-byte loads):
  *     QKVGAB  [4H + 2nh][H]   rows q | k | v | g | a_proj | b_proj
  *     O       [H][H]          at + off_o
  *     GU      [2I][H]         at + off_gu, gate row i at 2i, up row i at 2i+1
@@ -18,6 +21,12 @@
  *          is 1 KB contiguous, so a CTA's share of columns is one range
  *   tails  FP32 [L][3 (q,k,v)][H][4]       -- rows 0..2 of the conv window
  *          (row 2 newest) plus one pad lane, one 16-byte vector per channel
+ *   exchange buffers (qkv, gate, ab, attn, y_o, m, y_down): 64-bit words
+ *          {FP32 bits (low), tag (high)}. A phase's producer CTAs store each
+ *          word once with a single 64-bit store; consumer CTAs poll the words
+ *          until every tag equals the phase's tag (epoch + phase index), so a
+ *          phase boundary costs one round trip instead of a grid barrier plus
+ *          a load.
  */
 #ifndef GDN_ENGINE_H
 #define GDN_ENGINE_H
@@ -33,15 +42,17 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;      /* + one producer warp */
 constexpr int kSlotBytes = 16384;
-constexpr int kSlots = 12;
+constexpr int kSlots = 11;
 constexpr int kMaxRowsPerChunk = 4;
 constexpr int kColsPerChunk = 2;
 constexpr int kPhasesPerLayer = 5;
+constexpr int kTraceSlots = 8;
+constexpr int kPrefetchBytes = 256 * 1024;  /* per-CTA L2 prefetch lookahead of the weight stream */
 
 /* error codes written to DecodeStatus.err */
 enum {
     kErrNone = 0,
-    kErrBarrierTimeout = 1,
+    kErrExchangeTimeout = 1,
     kErrChunkTimeout = 2,
     kErrSlotTimeout = 3,
     kErrAborted = 4,
@@ -56,16 +67,19 @@ struct DecodeStatus {
     int32_t err;
     uint32_t err_cta;
     uint32_t err_where;
-    uint32_t bar;         /* grid barrier counter (monotonic) */
     uint32_t done;        /* LM-head ticket counter, reset by the last CTA */
-    uint32_t pad[10];
+    uint32_t pad[11];
 };
+
+typedef unsigned long long xword;  /* exchange word: {fp32 bits, tag} */
 
 struct DecodeParams {
     /* shape */
     int H, I, V, L, nh;
     float eps;
     int bf16_boundary;   /* 1: round activations to BF16 at operator boundaries */
+    int native_product;  /* 1: round every GEMV product to BF16 (DAZ/FTZ), the c_impl contract */
+    int bf16_state;      /* 1: round the updated recurrent state to BF16 (c_impl storage) */
     /* weights */
     const uint8_t *wimg;
     size_t layer_stride, off_o, off_gu, off_down;
@@ -73,22 +87,31 @@ struct DecodeParams {
     const uint16_t *emb;
     const float *aux;
     size_t aux_stride;
+    const float *exp_table;    /* 2^(j/64), j < 64, as hi[64] | lo[64] (gdn_math.h) */
     /* stream state */
     float *S;
     float *tails;
-    /* activations */
-    float *x_in, *x_mid, *y_o, *y_down, *qkv, *gate, *ab, *attn, *m, *logits, *hidden_out;
+    /* exchange buffers */
+    xword *qkv, *gate, *ab, *attn, *y_o, *m, *y_down;
+    /* outputs */
+    float *logits, *hidden_out;
     const float *x_embed;      /* FP32 embedding row, used when token_src == nullptr */
     const int32_t *token_src;  /* device token id: gather the embedding row on device */
     float *cand_val;
     int32_t *cand_idx;
     int32_t *token_out;        /* optional: receives the step's argmax token */
     DecodeStatus *status;
-    uint32_t bar_base;         /* status->bar at launch */
+    uint32_t epoch;            /* tag of phase q of this launch is epoch + q */
+    /* optional phase trace, %globaltimer ns: [cta][phase][kTraceSlots], phase =
+     * layer * 5 + {A..E}, L * 5 = LM head. Slots: 0 consumers done with the
+     * previous phase, 1 phase inputs arrived, 2 phase input built, 3 consumer
+     * chunks done (warp 0), 4 producer's first copy of the phase issued, 5 its
+     * last copy issued. */
+    unsigned long long *trace;
 };
 
-/* Number of grid barriers one launch performs. */
-inline uint32_t barriers_per_launch(int L) { return (uint32_t)(L * kPhasesPerLayer); }
+/* Tags one launch consumes; the host advances DecodeParams.epoch by this. */
+inline uint32_t epoch_stride(int L) { return (uint32_t)(L * kPhasesPerLayer + 1); }
 
 size_t decode_smem_bytes(int H, int I);
 cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t stream);

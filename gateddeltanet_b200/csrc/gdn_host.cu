@@ -11,6 +11,7 @@
  *   .gdnstate               c_impl/gdn_eval.cpp:202-267, c_impl/host.cpp:675-735
  */
 #include "gdn_engine.h"
+#include "gdn_math.h"
 #include "gdn_synth.h"
 
 #include "../../include/gdn_b200.h"
@@ -135,7 +136,8 @@ int engine_supports(const GDNWeightHeader &c) {
     const uint32_t H = c.hidden_size, I = c.intermediate_size;
     if (c.head_dim != 256) return fail("gdn_b200: head_dim must be 256 (got %u)", c.head_dim);
     if (c.conv_size != 4) return fail("gdn_b200: conv_size must be 4 (got %u)", c.conv_size);
-    if (H % 256 || I % 256 || H == 0 || I == 0) return fail("gdn_b200: hidden and intermediate must be multiples of 256");
+    if (H % 512 || I % 512 || H == 0 || I == 0) return fail("gdn_b200: hidden and intermediate must be multiples of 512");
+    if (2 * I > (uint32_t)gdn::kSlotBytes) return fail("gdn_b200: intermediate must be at most %d", gdn::kSlotBytes / 2);
     if (c.num_heads > 8 || H > GDN_WSF_HID) return fail("gdn_b200: at most 8 heads (hidden <= 2048)");
     if (I > GDN_WSF_MLP || c.vocab_size > GDN_WSF_LOGITS || c.vocab_size == 0)
         return fail("gdn_b200: intermediate/vocab exceed the workspace ABI");
@@ -157,6 +159,7 @@ struct DeviceModel {
     uint16_t *emb = nullptr;
     float *aux = nullptr;
     size_t aux_stride = 0;
+    float *exp_table = nullptr;
     bool model_alive = true;
 };
 
@@ -164,6 +167,15 @@ std::mutex g_mu;
 std::map<const float *, DeviceModel *> g_models;  /* keyed by GDNModel.weight_data */
 
 inline uint16_t hi16(float v) { return (uint16_t)(f2u(v) >> 16); }
+
+/* Device column position p of a GEMV row -> natural column. Inside each
+ * 512-column group the device row holds columns 0..7 of halves 0..31, then
+ * columns 8..15 of halves 0..31 (gdn_engine.h). */
+inline size_t natural_col(size_t p) {
+    const size_t g = p >> 9, w = p & 511;
+    const size_t hi = w >> 8, half = (w & 255) >> 3, e = w & 7;
+    return (g << 9) + half * 16 + hi * 8 + e;
+}
 
 void free_device_model(DeviceModel *dm) {
     int prev = 0;
@@ -173,6 +185,7 @@ void free_device_model(DeviceModel *dm) {
     cudaFree(dm->w_lm);
     cudaFree(dm->emb);
     cudaFree(dm->aux);
+    cudaFree(dm->exp_table);
     cudaSetDevice(prev);
     delete dm;
 }
@@ -226,7 +239,7 @@ DeviceModel *build_device_model(const GDNModel *model) {
             for (size_t i = b; i < e; ++i) {
                 float v;
                 if (i < rows_a * H) {
-                    const size_t r = i / H, col = i % H;
+                    const size_t r = i / H, col = natural_col(i % H);
                     const float *src;
                     if (r < H) src = w.q_proj + r * H;
                     else if (r < 2 * H) src = w.k_proj + (r - H) * H;
@@ -236,12 +249,14 @@ DeviceModel *build_device_model(const GDNModel *model) {
                     else src = w.b_proj + (r - 4 * H - nh) * H;
                     v = src[col];
                 } else if (i < dm->off_gu / 2) {
-                    v = w.o_proj[i - dm->off_o / 2];
+                    const size_t j = i - dm->off_o / 2;
+                    v = w.o_proj[(j / H) * H + natural_col(j % H)];
                 } else if (i < dm->off_down / 2) {
-                    const size_t j = i - dm->off_gu / 2, r = j / H, col = j % H;
+                    const size_t j = i - dm->off_gu / 2, r = j / H, col = natural_col(j % H);
                     v = ((r & 1) ? w.mlp_up_proj : w.mlp_gate_proj)[(r >> 1) * H + col];
                 } else {
-                    v = w.mlp_down_proj[i - dm->off_down / 2];
+                    const size_t j = i - dm->off_down / 2;
+                    v = w.mlp_down_proj[(j / I) * I + natural_col(j % I)];
                 }
                 st[so + (i - b)] = hi16(v);
             }
@@ -250,7 +265,8 @@ DeviceModel *build_device_model(const GDNModel *model) {
     }
     if (upload_bf16(reinterpret_cast<uint16_t *>(dm->w_lm), V * H,
                     [&](uint16_t *st, size_t b, size_t e, size_t so) {
-                        for (size_t i = b; i < e; ++i) st[so + (i - b)] = hi16(model->lm_head[i]);
+                        for (size_t i = b; i < e; ++i)
+                            st[so + (i - b)] = hi16(model->lm_head[(i / H) * H + natural_col(i % H)]);
                     }) != 0 ||
         upload_bf16(dm->emb, V * H, [&](uint16_t *st, size_t b, size_t e, size_t so) {
             for (size_t i = b; i < e; ++i) st[so + (i - b)] = hi16(model->embeddings[i]);
@@ -273,7 +289,11 @@ DeviceModel *build_device_model(const GDNModel *model) {
         memcpy(a + 14 * H + 256 + nh, w.dt_bias, nh * 4);
     }
     memcpy(aux.data() + dm->aux_stride * L, model->final_norm, H * 4);
-    if (cudaMemcpy(dm->aux, aux.data(), aux.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    float table[128];
+    gdn_exp_table_fill(table);
+    if (cudaMemcpy(dm->aux, aux.data(), aux.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMalloc(&dm->exp_table, sizeof(table)) != cudaSuccess ||
+        cudaMemcpy(dm->exp_table, table, sizeof(table), cudaMemcpyHostToDevice) != cudaSuccess) {
         fail("gdn_b200: aux upload failed");
         free_device_model(dm);
         return nullptr;
@@ -288,16 +308,20 @@ struct Stream {
     int device = 0;
     int grid = 0;
     int bf16_boundary = 1;
+    int native_product = 0;
+    int bf16_state = 0;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float *S = nullptr, *tails = nullptr, *acts = nullptr;
-    float *x_in, *x_mid, *y_o, *y_down, *qkv, *gate, *ab, *attn, *m, *logits, *hidden, *x_embed, *cand_val;
+    gdn::xword *xbuf = nullptr;  /* exchange words: qkv | gate | ab | attn | y_o | m | y_down */
+    gdn::xword *qkv, *gate, *ab, *attn, *y_o, *m, *y_down;
+    float *logits, *hidden, *x_embed, *cand_val;
     int32_t *cand_idx = nullptr;
     gdn::DecodeStatus *status = nullptr;
     gdn::DecodeStatus *status_host = nullptr;
     int32_t *tokens = nullptr, *argmax = nullptr;
     size_t tokens_cap = 0;
-    uint32_t bar = 0;
+    uint32_t epoch = 0;   /* exchange tag base of the next launch */
     float *ws = nullptr;  /* pinned ABI workspace (host) */
 };
 
@@ -323,6 +347,8 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.nh = (int)dm.cfg.num_heads;
     p.eps = dm.cfg.norm_eps;
     p.bf16_boundary = s.bf16_boundary;
+    p.native_product = s.native_product;
+    p.bf16_state = s.bf16_state;
     p.wimg = dm.wimg;
     p.layer_stride = dm.layer_stride;
     p.off_o = dm.off_o;
@@ -332,10 +358,9 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.emb = dm.emb;
     p.aux = dm.aux;
     p.aux_stride = dm.aux_stride;
+    p.exp_table = dm.exp_table;
     p.S = s.S;
     p.tails = s.tails;
-    p.x_in = s.x_in;
-    p.x_mid = s.x_mid;
     p.y_o = s.y_o;
     p.y_down = s.y_down;
     p.qkv = s.qkv;
@@ -351,15 +376,15 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.cand_idx = s.cand_idx;
     p.token_out = nullptr;
     p.status = s.status;
-    p.bar_base = s.bar;
+    p.epoch = s.epoch;
     return p;
 }
 
 int launch(Stream &s, gdn::DecodeParams &p) {
-    p.bar_base = s.bar;
+    p.epoch = s.epoch;
     const cudaError_t e = gdn::launch_decode(p, s.grid, s.stream);
     if (e != cudaSuccess) return fail("gdn_b200: decode launch failed: %s", cudaGetErrorString(e));
-    s.bar += gdn::barriers_per_launch(p.L) * (uint32_t)s.grid;
+    s.epoch += gdn::epoch_stride(p.L);
     return 0;
 }
 
@@ -371,8 +396,7 @@ int check_status(Stream &s) {
     const unsigned cta = s.status_host->err_cta, where = s.status_host->err_where;
     cudaMemsetAsync(s.status, 0, sizeof(gdn::DecodeStatus), s.stream);
     cudaStreamSynchronize(s.stream);
-    s.bar = 0;
-    static const char *names[] = {"none", "grid barrier timeout", "chunk wait timeout", "ring slot timeout",
+    static const char *names[] = {"none", "exchange wait timeout", "chunk wait timeout", "ring slot timeout",
                                   "aborted", "token id out of range"};
     return fail("gdn_b200: decode kernel reported %s (cta %u, at %u)", names[err >= 0 && err <= 5 ? err : 4], cta,
                 where);
@@ -587,7 +611,15 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
     Stream *s = new Stream();
     s->dm = dm;
     s->device = g_device;
+    /* one CTA per SM, but never more CTAs than units of the smallest phase:
+     * every CTA owns work in every phase (the exchange ordering relies on it) */
     s->grid = gdn_b200_grid_size();
+    {
+        const int units[] = {(int)(4 * model->config.hidden_size + 2 * model->config.num_heads),
+                             (int)(model->config.num_heads * 256), (int)model->config.hidden_size,
+                             (int)model->config.intermediate_size, (int)model->config.vocab_size};
+        for (int u : units) s->grid = std::min(s->grid, u);
+    }
     const GDNWeightHeader &c = model->config;
     const size_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size, nh = c.num_heads, L = c.num_layers;
     auto cleanup = [&](int rc) {
@@ -597,6 +629,7 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
         cudaFree(s->S);
         cudaFree(s->tails);
         cudaFree(s->acts);
+        cudaFree(s->xbuf);
         cudaFree(s->status);
         cudaFreeHost(s->status_host);
         cudaFreeHost(s->ws);
@@ -608,31 +641,34 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
         return cleanup(fail("gdn_b200: stream creation failed"));
     const size_t s_bytes = L * nh * 256 * 256 * sizeof(float);
     const size_t t_bytes = L * 3 * H * 4 * sizeof(float);
-    const size_t act_floats = 4 * H + 3 * H + H + 64 + H + I + V + H + H + 2 * (size_t)s->grid + 64;
+    const size_t act_floats = V + H + H + 2 * (size_t)s->grid + 64;
+    const size_t xwords = 3 * H + H + 64 + H + H + I + H;
     if (cudaMalloc(&s->S, s_bytes) != cudaSuccess || cudaMalloc(&s->tails, t_bytes) != cudaSuccess ||
         cudaMalloc(&s->acts, act_floats * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&s->xbuf, xwords * sizeof(gdn::xword)) != cudaSuccess ||
         cudaMalloc(&s->status, sizeof(gdn::DecodeStatus)) != cudaSuccess ||
         cudaMallocHost(&s->status_host, sizeof(gdn::DecodeStatus)) != cudaSuccess ||
         cudaHostAlloc(&s->ws, GDN_WS_FLOATS * sizeof(float), cudaHostAllocDefault) != cudaSuccess)
         return cleanup(fail("gdn_b200: run state allocation failed"));
+    gdn::xword *x = s->xbuf;
+    s->qkv = x; x += 3 * H;
+    s->gate = x; x += H;
+    s->ab = x; x += 64;
+    s->attn = x; x += H;
+    s->y_o = x; x += H;
+    s->m = x; x += I;
+    s->y_down = x;
     float *a = s->acts;
-    s->x_in = a; a += H;
-    s->x_mid = a; a += H;
-    s->y_o = a; a += H;
-    s->y_down = a; a += H;
-    s->qkv = a; a += 3 * H;
-    s->gate = a; a += H;
-    s->ab = a; a += 64;
-    s->attn = a; a += H;
-    s->m = a; a += I;
     s->logits = a; a += V;
     s->hidden = a; a += H;
     s->x_embed = a; a += H;
     s->cand_val = a; a += s->grid;
     s->cand_idx = reinterpret_cast<int32_t *>(a);
+    /* exchange words start with tag 0xffffffff, which no launch uses */
     if (cudaMemsetAsync(s->S, 0, s_bytes, s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->tails, 0, t_bytes, s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->acts, 0, act_floats * sizeof(float), s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->xbuf, 0xff, xwords * sizeof(gdn::xword), s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->status, 0, sizeof(gdn::DecodeStatus), s->stream) != cudaSuccess ||
         cudaStreamSynchronize(s->stream) != cudaSuccess)
         return cleanup(fail("gdn_b200: run state initialisation failed"));
@@ -671,6 +707,7 @@ void gdn_run_state_free(GDNRunState *state) {
         cudaFree(s->S);
         cudaFree(s->tails);
         cudaFree(s->acts);
+        cudaFree(s->xbuf);
         cudaFree(s->status);
         cudaFree(s->tokens);
         cudaFree(s->argmax);
@@ -685,10 +722,13 @@ void gdn_run_state_free(GDNRunState *state) {
     memset(state, 0, sizeof(*state));
 }
 
-int gdn_b200_set_boundary(GDNRunState *state, int bf16_boundary) {
+int gdn_b200_set_numerics(GDNRunState *state, int bf16_boundary, int bf16_products, int bf16_state) {
     Stream *s = find_stream(state);
     if (s == nullptr) return fail("gdn_b200: unknown run state");
+    if (bf16_products && !bf16_boundary) return fail("gdn_b200: BF16-rounded products need BF16 boundaries");
     s->bf16_boundary = bf16_boundary ? 1 : 0;
+    s->native_product = bf16_products ? 1 : 0;
+    s->bf16_state = bf16_state ? 1 : 0;
     return 0;
 }
 
@@ -749,6 +789,35 @@ int gdn_b200_decode_tokens(const GDNModel *model, GDNRunState *state, const int3
     if (rc != 0) return rc;
     if (kernel_ms != nullptr) CUDA_OK(cudaEventElapsedTime(kernel_ms, s->ev0, s->ev1));
     return 0;
+}
+
+int gdn_b200_trace_step(const GDNModel *model, GDNRunState *state, int32_t token, uint64_t *trace_out,
+                        size_t capacity) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    if (token < 0 || (uint32_t)token >= model->config.vocab_size) return fail("token id out of range");
+    const size_t n = (size_t)s->grid * (model->config.num_layers * gdn::kPhasesPerLayer + 1) * gdn::kTraceSlots;
+    if (trace_out == nullptr || capacity < n) return fail("gdn_b200: trace buffer needs %zu entries", n);
+    CUDA_OK(cudaSetDevice(s->device));
+    unsigned long long *dtrace = nullptr;
+    int32_t *dtok = nullptr;
+    CUDA_OK(cudaMalloc(&dtrace, n * sizeof(uint64_t)));
+    if (cudaMalloc(&dtok, sizeof(int32_t)) != cudaSuccess) {
+        cudaFree(dtrace);
+        return fail("gdn_b200: trace allocation failed");
+    }
+    cudaMemsetAsync(dtrace, 0, n * sizeof(uint64_t), s->stream);
+    cudaMemcpyAsync(dtok, &token, sizeof(int32_t), cudaMemcpyHostToDevice, s->stream);
+    gdn::DecodeParams p = make_params(*s);
+    p.token_src = dtok;
+    p.trace = dtrace;
+    int rc = launch(*s, p);
+    if (rc == 0) rc = sync_and_check(*s);
+    if (rc == 0 && cudaMemcpy(trace_out, dtrace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = fail("gdn_b200: trace copy failed");
+    cudaFree(dtrace);
+    cudaFree(dtok);
+    return rc == 0 ? (int)(n / gdn::kTraceSlots) : rc;
 }
 
 int gdn_b200_fetch_outputs(GDNRunState *state, float *logits, float *final_hidden) {

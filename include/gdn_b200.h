@@ -35,10 +35,18 @@ int gdn_b200_model_synth(GDNModel *model, const GDNWeightHeader *config, uint64_
  * gdn_model_load reads (scripts/export_gdn_c.py:177-210). */
 int gdn_b200_model_save(const GDNModel *model, const char *path);
 
-/* Operator-boundary precision of a stream: 1 (default) rounds every
- * activation to BF16 where the reference does; 0 keeps FP32 (the "FP32
- * control" of the parity gates). */
-int gdn_b200_set_boundary(GDNRunState *state, int bf16_boundary);
+/* Numerics of a stream (defaults 1, 0, 0):
+ *   bf16_boundary  1: round every activation to BF16 where the reference does
+ *                  (its all-BF16 transient contract); 0: keep FP32 (the "FP32
+ *                  control" of the parity gates).
+ *   bf16_products  1: round each GEMV product to BF16 with DAZ/FTZ before the
+ *                  sum, the c_impl/FPGA product contract
+ *                  (c_impl/gdn_model.cpp:392-466); 0: exact products (the
+ *                  PyTorch/GPU arithmetic). Needs bf16_boundary.
+ *   bf16_state     1: store the recurrent state rounded to BF16 after each
+ *                  update (c_impl/gdn_model.cpp:2268-2300); 0: FP32 state.
+ * GEMV sums always follow the reference's reduction order. */
+int gdn_b200_set_numerics(GDNRunState *state, int bf16_boundary, int bf16_products, int bf16_state);
 
 /* Replace / read the decode state in the .gdnstate section layouts:
  * rec [layers][heads][K=256][V=256] FP32 and conv tails
@@ -66,6 +74,16 @@ int gdn_b200_fetch_outputs(GDNRunState *state, float *logits, float *final_hidde
  * device; the token ids cross PCIe once. */
 int gdn_b200_decode_tokens(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n,
                            int greedy, int32_t *argmax_out, float *kernel_ms);
+
+/* One decode step of `token` with the kernel's phase trace enabled: for every
+ * CTA and phase (layer * 5 + {QKVG, state, O, gate/up, down}, then the LM
+ * head) eight %globaltimer stamps in ns -- consumers done with the previous
+ * phase, past the grid barrier, phase input built, own chunks done, producer's
+ * first and last copy issued, two unused. Layout [cta][phase][8]; returns the
+ * number of (cta, phase) records or -1. The B200 counterpart of the
+ * reference's GDN_CALL_PROBE cycle stamps (c_impl/gdn_model.cpp:18-127). */
+int gdn_b200_trace_step(const GDNModel *model, GDNRunState *state, int32_t token, uint64_t *trace_out,
+                        size_t capacity);
 
 /* Number of SMs (CTAs) the decode kernel uses on the current device. */
 int gdn_b200_grid_size(void);

@@ -56,10 +56,15 @@ def full(lib):
     return model, oracle
 
 
-def run_parity(model, oracle, steps, mode, bf16_boundary, state_seed, tol_logits, tol_state, use_loop=False):
+ENGINE = (True, False, False)      # engine default numerics (gdn_b200_set_numerics)
+CIMPL = (True, True, True)         # the c_impl's own arithmetic
+FP32 = (False, False, False)       # FP32 control
+
+
+def run_parity(model, oracle, steps, mode, numerics, state_seed, tol_logits, tol_state, use_loop=False):
     oracle.reset_state(state_seed)
     rs = gdn.RunState(model)
-    rs.set_boundary(bf16_boundary)
+    rs.set_numerics(*numerics)
     if state_seed:
         rs.load_state(oracle.rec, oracle.conv)
     tokens = [oracle.token(STREAM_SEED, 0, i) for i in range(steps)]
@@ -89,18 +94,18 @@ def run_parity(model, oracle, steps, mode, bf16_boundary, state_seed, tol_logits
 @pytest.mark.parametrize("state_seed", [0, 7])
 def test_small_engine_mode(small, state_seed):
     model, oracle = small
-    run_parity(model, oracle, 8, ol.ENGINE_MODE, True, state_seed, parity.LOGITS_BF16, parity.STATE)
+    run_parity(model, oracle, 8, ol.ENGINE_MODE, ENGINE, state_seed, parity.LOGITS_BF16, parity.STATE)
 
 
 @pytest.mark.parametrize("state_seed", [0, 7])
 def test_small_fp32_control(small, state_seed):
     model, oracle = small
-    run_parity(model, oracle, 6, ol.FP32_CONTROL, False, state_seed, parity.LOGITS_FP32, parity.LOGITS_FP32)
+    run_parity(model, oracle, 6, ol.FP32_CONTROL, FP32, state_seed, parity.LOGITS_FP32, parity.LOGITS_FP32)
 
 
 def test_small_reference_mode(small):
     model, oracle = small
-    run_parity(model, oracle, 6, ol.REFERENCE_MODE, True, 7, parity.LOGITS_BF16, 1e-2)
+    run_parity(model, oracle, 6, ol.REFERENCE_MODE, CIMPL, 7, parity.LOGITS_BF16, parity.STATE)
 
 
 def test_small_device_loop_matches_host_steps(small):
@@ -202,10 +207,10 @@ def test_full_engine_and_reference_modes(full):
     seeded state in the engine mode, then against the reference's own
     arithmetic (BF16 products, BF16 state)."""
     model, oracle = full
-    run_parity(model, oracle, 3, ol.ENGINE_MODE, True, 7, parity.LOGITS_BF16, parity.STATE)
-    run_parity(model, oracle, 2, ol.REFERENCE_MODE, True, 7, parity.LOGITS_BF16, 1e-2, use_loop=True)
+    run_parity(model, oracle, 3, ol.ENGINE_MODE, ENGINE, 7, parity.LOGITS_BF16, parity.STATE)
+    run_parity(model, oracle, 2, ol.REFERENCE_MODE, CIMPL, 7, parity.LOGITS_BF16, parity.STATE, use_loop=True)
 
 
 def test_full_fp32_control(full):
     model, oracle = full
-    run_parity(model, oracle, 2, ol.FP32_CONTROL, False, 0, parity.LOGITS_FP32, parity.LOGITS_FP32)
+    run_parity(model, oracle, 2, ol.FP32_CONTROL, FP32, 0, parity.LOGITS_FP32, parity.LOGITS_FP32)
