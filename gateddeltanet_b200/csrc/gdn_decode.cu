@@ -390,8 +390,8 @@ __device__ __forceinline__ void raise_error(const DecodeParams &p, const Smem &s
     *s.abort_flag = 1;
 }
 
-/* Spin (with a short back-off) on one exchange word until it carries `tag`;
- * returns the last word read, whose tag differs from `tag` on abort/timeout. */
+/* Spin on one exchange word until it carries `tag`; returns the last word
+ * read, whose tag differs from `tag` on abort/timeout. */
 __device__ __noinline__ xword xwait(const DecodeParams &p, const Smem &s, const xword *a, uint32_t tag) {
     const uint64_t t0 = gtimer();
     uint32_t spins = 0;
@@ -412,40 +412,55 @@ __device__ __noinline__ xword xwait(const DecodeParams &p, const Smem &s, const 
     }
 }
 
+__device__ __forceinline__ void xget2(const xword *p, xword &a, xword &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 /* Warp-wide read of exchange words: lane i reads n (<= N) words at
- * src_i + j * stride. While the producers are still busy only lane 0 polls,
- * on the warp's last word (its likely latest); then every lane issues all its
- * loads at once and re-issues the ones still carrying an old tag, round by
- * round, so a late phase costs one round trip per round rather than one per
- * word. All 32 lanes must call. */
+ * src_i + j * stride (stride 1: 16-byte vector loads; src 16-byte aligned,
+ * n even). Every load is issued at once, so data that is already there costs
+ * one round trip. While words are missing, one lane of the warp polls a
+ * missing word (no flood of loads while producers are still busy), then the
+ * warp re-reads everything still missing. All 32 lanes must call; lanes with
+ * n == 0 take part in the protocol only. */
 template <int N>
 __device__ __forceinline__ bool xread(const DecodeParams &p, const Smem &s, const xword *src, int stride, int n,
                                       uint32_t tag, float (&v)[N]) {
     const int lane = threadIdx.x & 31;
-    const xword *hint = reinterpret_cast<const xword *>(
-        __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(src + (size_t)(n - 1) * stride), 31));
-    int okw = 1;
-    if (lane == 0 && xtag(xget(hint)) != tag) okw = xtag(xwait(p, s, hint, tag)) == tag;
-    if (!__shfl_sync(0xffffffffu, okw, 0)) return false;
     xword w[N];
+    if (stride == 1) {
+#pragma unroll
+        for (int i = 0; i < N; i += 2)
+            if (i < n) xget2(src + i, w[i], w[i + 1]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+            if (i < n) w[i] = xget(src + (size_t)i * stride);
+    }
     uint32_t missing = 0;
 #pragma unroll
     for (int i = 0; i < N; ++i)
-        if (i < n) w[i] = xget(src + (size_t)i * stride);
-#pragma unroll
-    for (int i = 0; i < N; ++i)
         if (i < n && xtag(w[i]) != tag) missing |= 1u << i;
-    const uint64_t t0 = missing ? gtimer() : 0;
-    while (missing) {
-        if (*s.abort_flag) return false;
+    uint64_t t0 = 0;
+    while (__any_sync(0xffffffffu, missing != 0)) {
+        /* the lowest lane with a missing word polls it until it lands */
+        const uint32_t ballot = __ballot_sync(0xffffffffu, missing != 0);
+        const int leader = __ffs(ballot) - 1;
+        int ok = 1;
+        if (lane == leader) {
+            const int i = __ffs(missing) - 1;
+            ok = xtag(xwait(p, s, src + (size_t)i * stride, tag)) == tag;
+        }
+        if (!__shfl_sync(0xffffffffu, ok, leader)) return false;
 #pragma unroll
         for (int i = 0; i < N; ++i)
             if ((missing >> i) & 1u) w[i] = xget(src + (size_t)i * stride);
 #pragma unroll
         for (int i = 0; i < N; ++i)
             if (((missing >> i) & 1u) && xtag(w[i]) == tag) missing &= ~(1u << i);
-        if (missing && gtimer() - t0 > kWaitNs) {
-            raise_error(p, s, kErrExchangeTimeout, tag);
+        if (t0 == 0) t0 = gtimer();
+        else if (gtimer() - t0 > kWaitNs) {
+            if (missing) raise_error(p, s, kErrExchangeTimeout, tag);
             return false;
         }
     }
@@ -455,24 +470,19 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Smem &s, cons
     return true;
 }
 
-/* Read n exchange words (n/256 <= 32 per thread, element t + 256 j) into the
+/* Read n exchange words (element t + 256 j, n/256 <= 32 per thread) into the
  * permuted shared input, with xread's protocol. All consumer threads call. */
 __device__ __noinline__ bool xread_to_xs(const DecodeParams &p, const Smem &s, const xword *src, int n, uint32_t tag) {
     const int t = threadIdx.x;
-    const int per = n >> 8;
-    bool ok = true;
-    for (int j0 = 0; j0 < per; j0 += 16) {
-        float v[16];
-        const int cnt = (per - j0) < 16 ? (per - j0) : 16;
-        ok = xread<16>(p, s, src + t + (j0 << 8), 256, cnt, tag, v) && ok;
+    float v[32];
+    const bool ok = xread<32>(p, s, src + t, 256, n >> 8, tag, v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if (j < cnt) s.xs[xs_pos(t + ((j0 + j) << 8))] = v[j];
-    }
+    for (int j = 0; j < 32; ++j)
+        if (j < (n >> 8)) s.xs[xs_pos(t + (j << 8))] = v[j];
     return ok;
 }
 
-/* Single-lane read of one exchange word (poll with back-off). */
+/* Single-lane read of one exchange word. */
 __device__ __forceinline__ bool xread1(const DecodeParams &p, const Smem &s, const xword *src, uint32_t tag,
                                        float &v) {
     xword w = xget(src);
@@ -607,20 +617,36 @@ __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, 
 
 /* ---------------------------------------------------------- prologues */
 
+/* Sequential sum of n (multiple of 4) floats in shared memory, in index
+ * order from 0.0f (one thread). */
+__device__ __forceinline__ float seq_sum(const float *a, int n) {
+    float sum = 0.0f;
+#pragma unroll 8
+    for (int j = 0; j < n; j += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(a + j);
+        sum = __fadd_rn(sum, v.x);
+        sum = __fadd_rn(sum, v.y);
+        sum = __fadd_rn(sum, v.z);
+        sum = __fadd_rn(sum, v.w);
+    }
+    return sum;
+}
+
 /* Residual add + RMSNorm into the permuted shared input, in the reference's
  * order (c_impl/gdn_model.cpp:1394-1476, 3351-3452): thread t < H/16 owns the
  * 16-column half t (beat t/2, half t%2): x = round(xres + y) (or the embedding
- * for layer 0), s_t = its squares summed sequentially; then thread 0 sums the
- * s_t sequentially; scale = 1/sqrtf(sum/H + eps); out = round((x*scale)*w). */
+ * for layer 0), s_t = its squares summed sequentially; the s_t are summed
+ * sequentially (by lane 0 of every working warp, so no second barrier);
+ * scale = 1/sqrtf(sum/H + eps); out = round((x*scale)*w). */
 template <int MODE>
-__device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s, const xword *y, uint32_t tag, const float *w,
-                              bool embed, float *hidden, int pidx) {
-    const int t = threadIdx.x;
+__device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s, const xword *y, uint32_t tag,
+                                           const float *w, bool embed, float *hidden, int pidx) {
+    const int t = threadIdx.x, lane = t & 31;
     const int halves = p.H >> 4;
     bool ok = true;
+    float x[16];
     float wv[16];
     if (t < halves) {
-        float x[16];
         const float4 *w4 = reinterpret_cast<const float4 *>(w + 16 * t);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -630,9 +656,14 @@ __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s,
         if (embed) {
             if (p.token_src != nullptr) {
                 const int32_t tok = *p.token_src;
-                const uint16_t *e = p.emb + (size_t)tok * p.H + 16 * t;
+                const uint4 *e4 = reinterpret_cast<const uint4 *>(p.emb + (size_t)tok * p.H + 16 * t);
+                const uint4 e0 = __ldg(e4), e1 = __ldg(e4 + 1);
+                const uint32_t ew[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
 #pragma unroll
-                for (int i = 0; i < 16; ++i) x[i] = bnd<MODE>(__uint_as_float((uint32_t)e[i] << 16));
+                for (int i = 0; i < 8; ++i) {
+                    x[2 * i] = bnd<MODE>(bf_lo(ew[i]));
+                    x[2 * i + 1] = bnd<MODE>(bf_hi(ew[i]));
+                }
             } else {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) x[i] = bnd<MODE>(p.x_embed[16 * t + i]);
@@ -653,24 +684,17 @@ __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s,
         s.red[t] = hs;
     }
     named_sync(1, kConsumerThreads);
-    if (t == 0) {
-        float sum = 0.0f;
-        for (int j = 0; j < halves; j += 4) {
-            const float4 v = *reinterpret_cast<const float4 *>(s.red + j);
-            sum = __fadd_rn(sum, v.x);
-            sum = __fadd_rn(sum, v.y);
-            sum = __fadd_rn(sum, v.z);
-            sum = __fadd_rn(sum, v.w);
-        }
-        s.red[128] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)p.H), p.eps)));
-        trace_put(p, pidx, 6);
-    }
-    named_sync(1, kConsumerThreads);
-    const float scale = s.red[128];
     if (t < halves) {
+        float scale = 0.0f;
+        if (lane == 0) {
+            const float sum = seq_sum(s.red, halves);
+            scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)p.H), p.eps)));
+            if (t == 0) trace_put(p, pidx, 6);
+        }
+        scale = __shfl_sync(0xffffffffu, scale, 0);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const float o = bnd<MODE>(__fmul_rn(__fmul_rn(s.xres[16 * t + i], scale), wv[i]));
+            const float o = bnd<MODE>(__fmul_rn(__fmul_rn(x[i], scale), wv[i]));
             s.xs[xs_pos(16 * t + i)] = o;
             if (hidden != nullptr) hidden[16 * t + i] = o;
         }
@@ -681,25 +705,19 @@ __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s,
 /* Per-head RMSNorm of the attention output times swish(gate) in the
  * reference's order (c_impl/gdn_model.cpp:3226-3349): per head, 16 half sums
  * of 16 sequential squares, summed sequentially; scale = 1/sqrtf(sum/256 +
- * eps); out = round(((a*scale)*w) * g * sigmoid(g)). */
+ * eps); out = round(((a*scale)*w) * g * sigmoid(g)). The elementwise tail runs
+ * on all consumer threads, eight independent elements each. */
 template <int MODE>
-__device__ __noinline__ bool prologue_norm_gate(const DecodeParams &p, const Smem &s, const float *o_norm, uint32_t tag_a,
-                                   uint32_t tag_b, int pidx) {
+__device__ __noinline__ bool prologue_norm_gate(const DecodeParams &p, const Smem &s, const float *o_norm,
+                                                uint32_t tag_a, uint32_t tag_b, int pidx) {
     const int t = threadIdx.x;
     const int halves = p.H >> 4;
     bool ok = true;
-    float wv[16];
-    float *a_sh = s.chain, *g_sh = s.chain + p.H;   /* H <= 2048: both fit the 16 KB scratch */
+    float *a_sh = s.chain, *g_sh = s.chain + p.H; /* H <= 2048: both fit the 16 KB scratch */
     if (t < halves) {
         float a[16], g[16];
-        const float4 *w4 = reinterpret_cast<const float4 *>(o_norm + 16 * (t & 15));
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 v = __ldg(w4 + q);
-            wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
-        }
-        ok = xread<16>(p, s, p.attn + 16 * t, 1, 16, tag_b, a);
-        ok = xread<16>(p, s, p.gate + 16 * t, 1, 16, tag_a, g) && ok;
+        ok = xread<16>(p, s, p.gate + 16 * t, 1, 16, tag_a, g);
+        ok = xread<16>(p, s, p.attn + 16 * t, 1, 16, tag_b, a) && ok;
         if (t == 0) trace_put(p, pidx, 1);
         float hs = 0.0f;
 #pragma unroll
@@ -719,50 +737,96 @@ __device__ __noinline__ bool prologue_norm_gate(const DecodeParams &p, const Sme
         if (t == 0) trace_put(p, pidx, 6);
     }
     named_sync(1, kConsumerThreads);
-    if (t < halves) {
-        const float scale = s.hscal[8 + (t >> 4)];
+    const int per = p.H >> 8; /* <= 8 elements per thread */
+    float wv[8], av[8], gv[8], out[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const float gi = g_sh[16 * t + i];
-            const float normalized = __fmul_rn(__fmul_rn(a_sh[16 * t + i], scale), wv[i]);
-            s.xs[xs_pos(16 * t + i)] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gi), sigmoid_ref(gi)));
+    for (int i = 0; i < 8; ++i) {
+        if (i < per) {
+            const int e = per * t + i;
+            wv[i] = __ldg(o_norm + (e & 255));
+            av[i] = a_sh[e];
+            gv[i] = g_sh[e];
         }
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (i < per) {
+            const int e = per * t + i;
+            const float scale = s.hscal[8 + (e >> 8)];
+            const float normalized = __fmul_rn(__fmul_rn(av[i], scale), wv[i]);
+            out[i] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv[i]), sigmoid_ref(gv[i])));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if (i < per) s.xs[xs_pos(per * t + i)] = out[i];
     return ok;
 }
 
 /* q/k L2 norms (balanced tree order of gdn_tree_reduce_256), alpha, beta
- * and decay for the CTA's heads (c_impl/gdn_model.cpp:2059-2124). */
-__device__ __noinline__ bool prologue_state(const DecodeParams &p, const Smem &s, int l, int h0, int h1, uint32_t tag) {
+ * and decay for the CTA's heads (c_impl/gdn_model.cpp:2059-2124); all reads
+ * are issued before any reduction. */
+__device__ __noinline__ bool prologue_state(const DecodeParams &p, const Smem &s, int l, int h0, int h1,
+                                            uint32_t tag) {
     const int t = threadIdx.x;
+    const int nhl = h1 - h0 + 1; /* 1 or 2 */
     const float *aux = p.aux + (size_t)l * p.aux_stride;
     const float *a_log = aux + 14 * p.H + kHeadDim;
     const float *dt_bias = a_log + p.nh;
+    float qk[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float av = 0.0f, bv = 0.0f, alog = 0.0f, dtb = 0.0f;
     bool ok = true;
-    for (int hs = 0; hs <= h1 - h0; ++hs) {
-        const int h = h0 + hs;
-        float qk[2];
-        float qv[1], kv[1];
-        ok = xread<1>(p, s, p.qkv + h * kHeadDim + t, 1, 1, tag, qv) && ok;
-        ok = xread<1>(p, s, p.qkv + p.H + h * kHeadDim + t, 1, 1, tag, kv) && ok;  /* all 256 threads */
-        qk[0] = __fmul_rn(qv[0], qv[0]);
-        qk[1] = __fmul_rn(kv[0], kv[0]);
-        block_sum<2>(qk, s.red);
-        const float q_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(qk[0], 1e-6f)));
-        const float k_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(qk[1], 1e-6f)));
-        const float qn = __fmul_rn(qv[0], q_inv), kn = __fmul_rn(kv[0], k_inv);
-        s.qn[hs * kHeadDim + t] = qn;
-        s.kn[hs * kHeadDim + t] = kn;
-        float al[1] = {__fmul_rn(qn, kn)};
-        block_sum<1>(al, s.red);
-        if (t == 0) {
-            float av, bv;
-            ok = xread1(p, s, p.ab + h, tag, av) && ok;
-            ok = xread1(p, s, p.ab + p.nh + h, tag, bv) && ok;
-            const float beta = sigmoid_ref(bv);
-            const float decay_in = __fadd_rn(av, __ldg(dt_bias + h));
-            const float decay_val = __fmul_rn(-exp_ref(__ldg(a_log + h)), softplus_ref(decay_in));
-            s.hscal[hs * 4 + 0] = al[0];
+    if (t < 2 * nhl) {
+        const int h = h0 + (t >> 1);
+        alog = __ldg(a_log + h);
+        dtb = __ldg(dt_bias + h);
+    }
+    {
+        /* words: q h0, k h0 [, q h1, k h1] at stride H between q and k */
+        float v4[4];
+        const xword *base = p.qkv + h0 * kHeadDim + t;
+        float vq[2], vk[2];
+        ok = xread<2>(p, s, base, kHeadDim, nhl, tag, vq) && ok;
+        ok = xread<2>(p, s, base + p.H, kHeadDim, nhl, tag, vk) && ok;
+        v4[0] = vq[0];
+        v4[1] = vk[0];
+        v4[2] = nhl > 1 ? vq[1] : 0.0f;
+        v4[3] = nhl > 1 ? vk[1] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) qk[i] = v4[i];
+    }
+    if (t < 2 * nhl) {
+        const int h = h0 + (t >> 1);
+        ok = xread1(p, s, p.ab + ((t & 1) ? p.nh + h : h), tag, (t & 1) ? bv : av) && ok;
+    }
+    float sq[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sq[i] = __fmul_rn(qk[i], qk[i]);
+    block_sum<4>(sq, s.red);
+    float al[2];
+#pragma unroll
+    for (int hs = 0; hs < 2; ++hs) {
+        const float q_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sq[2 * hs], 1e-6f)));
+        const float k_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sq[2 * hs + 1], 1e-6f)));
+        const float qn = __fmul_rn(qk[2 * hs], q_inv), kn = __fmul_rn(qk[2 * hs + 1], k_inv);
+        if (hs < nhl) {
+            s.qn[hs * kHeadDim + t] = qn;
+            s.kn[hs * kHeadDim + t] = kn;
+        }
+        al[hs] = __fmul_rn(qn, kn);
+    }
+    block_sum<2>(al, s.red + 32);
+    /* beta and decay: thread 2h read a_h, thread 2h+1 read b_h (full-warp
+     * shuffle; only threads 0..3 use the result) */
+    const float other = __shfl_xor_sync(0xffffffffu, (t & 1) ? bv : av, 1);
+    if (t < 2 * nhl) {
+        const int hs = t >> 1;
+        if ((t & 1) == 0) {
+            const float b_h = other;
+            const float beta = sigmoid_ref(b_h);
+            const float decay_in = __fadd_rn(av, dtb);
+            const float decay_val = __fmul_rn(-exp_ref(alog), softplus_ref(decay_in));
+            s.hscal[hs * 4 + 0] = al[hs];
             s.hscal[hs * 4 + 1] = beta;
             s.hscal[hs * 4 + 2] = exp_ref(decay_val);
         }

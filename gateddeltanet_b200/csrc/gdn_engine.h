@@ -106,7 +106,8 @@ struct DecodeParams {
      * layer * 5 + {A..E}, L * 5 = LM head. Slots: 0 consumers done with the
      * previous phase, 1 phase inputs arrived, 2 phase input built, 3 consumer
      * chunks done (warp 0), 4 producer's first copy of the phase issued, 5 its
-     * last copy issued. */
+     * last copy issued, 6 input reduction (norm sums, head scalars) done,
+     * 7 unused. */
     unsigned long long *trace;
 };
 
