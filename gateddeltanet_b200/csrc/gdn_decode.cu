@@ -173,6 +173,9 @@ __device__ __forceinline__ int xs_pos(int c) {
 
 /* ------------------------------------------------------------ schedule */
 
+/* Where a CTA's share of one phase lives: units [u0, u1) of unit_bytes each,
+ * upc units per ring chunk. The shape depends on the phase kind only (not on
+ * the layer); kernel start tabulates it in shared memory. */
 struct Geom {
     const uint8_t *src;
     uint32_t unit_bytes, upc, u0, u1;
@@ -180,41 +183,36 @@ struct Geom {
 
 enum { PH_QKVG = 0, PH_STATE = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_LM = 5 };
 
-__device__ __forceinline__ Geom geom(const DecodeParams &p, int l, int ph, uint32_t cta, uint32_t ncta) {
+__device__ __forceinline__ Geom geom_compute(const DecodeParams &p, int ph, uint32_t cta, uint32_t ncta) {
     Geom g;
     uint32_t total;
-    const uint8_t *lw = p.wimg + (size_t)l * p.layer_stride;
     const uint32_t rowH = 2u * (uint32_t)p.H;
     uint32_t rpcH = (uint32_t)kSlotBytes / rowH;
     if (rpcH > (uint32_t)kMaxRowsPerChunk) rpcH = kMaxRowsPerChunk;
+    g.src = nullptr;
     switch (ph) {
     case PH_QKVG:
         total = 4u * p.H + 2u * p.nh;
-        g.src = lw;
         g.unit_bytes = rowH;
         g.upc = rpcH;
         break;
     case PH_STATE:
         total = (uint32_t)p.nh * kHeadDim;
-        g.src = reinterpret_cast<const uint8_t *>(p.S + (size_t)l * p.nh * kHeadDim * kHeadDim);
         g.unit_bytes = kHeadDim * 4u;
         g.upc = kColsPerChunk;
         break;
     case PH_O:
         total = (uint32_t)p.H;
-        g.src = lw + p.off_o;
         g.unit_bytes = rowH;
         g.upc = rpcH;
         break;
     case PH_GU:
         total = (uint32_t)p.I;
-        g.src = lw + p.off_gu;
         g.unit_bytes = 2u * rowH;
         g.upc = rpcH / 2u > 0 ? rpcH / 2u : 1u;
         break;
     case PH_DOWN: {
         total = (uint32_t)p.H;
-        g.src = lw + p.off_down;
         g.unit_bytes = 2u * (uint32_t)p.I;
         uint32_t r = (uint32_t)kSlotBytes / g.unit_bytes;
         g.upc = r > (uint32_t)kMaxRowsPerChunk ? (uint32_t)kMaxRowsPerChunk : (r > 0 ? r : 1u);
@@ -222,7 +220,6 @@ __device__ __forceinline__ Geom geom(const DecodeParams &p, int l, int ph, uint3
     }
     default:
         total = (uint32_t)p.V;
-        g.src = p.w_lm;
         g.unit_bytes = rowH;
         g.upc = rpcH;
         break;
@@ -230,6 +227,19 @@ __device__ __forceinline__ Geom geom(const DecodeParams &p, int l, int ph, uint3
     g.u0 = (uint32_t)(((uint64_t)cta * total) / ncta);
     g.u1 = (uint32_t)(((uint64_t)(cta + 1) * total) / ncta);
     return g;
+}
+
+/* Base address of phase ph's units in layer l (ignored for the LM head). */
+__device__ __forceinline__ const uint8_t *phase_src(const DecodeParams &p, int l, int ph) {
+    const uint8_t *lw = p.wimg + (size_t)l * p.layer_stride;
+    switch (ph) {
+    case PH_QKVG: return lw;
+    case PH_STATE: return reinterpret_cast<const uint8_t *>(p.S + (size_t)l * p.nh * kHeadDim * kHeadDim);
+    case PH_O: return lw + p.off_o;
+    case PH_GU: return lw + p.off_gu;
+    case PH_DOWN: return lw + p.off_down;
+    default: return p.w_lm;
+    }
 }
 
 /* ------------------------------------------------------ exchange words */
@@ -246,62 +256,7 @@ __device__ __forceinline__ xword xget(const xword *p) {
 __device__ __forceinline__ uint32_t xtag(xword w) { return (uint32_t)(w >> 32); }
 __device__ __forceinline__ float xval(xword w) { return __uint_as_float((uint32_t)w); }
 
-/* A position in a CTA's chunk schedule: layers' phases A..E, then the LM
- * head. The producer walks one cursor to fill the ring and a second one,
- * kPrefetchBytes ahead of it, to pull the same chunks from HBM into L2. */
-struct Cursor {
-    int l, pi;
-    uint32_t u;
-    Geom g;
-};
-
-__device__ __forceinline__ bool cursor_valid(const DecodeParams &p, const Cursor &c) {
-    return c.l < p.L || (c.l == p.L && c.pi == 0);
-}
-
-__device__ __forceinline__ void cursor_settle(const DecodeParams &p, Cursor &c, uint32_t cta, uint32_t ncta) {
-    while (cursor_valid(p, c) && c.u >= c.g.u1) {
-        if (c.l == p.L) {
-            c.pi = 1;  /* past the LM head */
-            return;
-        }
-        if (++c.pi == kPhasesPerLayer) {
-            c.pi = 0;
-            ++c.l;
-        }
-        c.g = geom(p, c.l < p.L ? c.l : 0, c.l < p.L ? c.pi : PH_LM, cta, ncta);
-        c.u = c.g.u0;
-    }
-}
-
-__device__ __forceinline__ void cursor_init(const DecodeParams &p, Cursor &c, uint32_t cta, uint32_t ncta) {
-    c.l = 0;
-    c.pi = 0;
-    c.g = geom(p, 0, PH_QKVG, cta, ncta);
-    c.u = c.g.u0;
-    cursor_settle(p, c, cta, ncta);
-}
-
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 /* ------------------------------------------------------- shared memory */
-
-struct Smem {
-    uint8_t *ring;
-    float *xs;        /* permuted phase input, max(H, I) floats; phase B: qn | kn */
-    float *qn, *kn;   /* [2][256] normalised q/k of the CTA's (at most two) heads */
-    float *xres;      /* residual stream, H floats (the same in every CTA) */
-    float *red;       /* 160 floats: half sums [0,128), block partials [0,64), scalars [128,160) */
-    float *chain;     /* [8 warps][512] per-warp GEMV bank partials */
-    float *hscal;     /* [2][4] alpha, beta, decay per local head; [8, 16) per-head norm scales */
-    float *wbest;     /* [8] */
-    int32_t *wbest_i; /* [8] */
-    uint64_t *full, *empty;
-    volatile int32_t *abort_flag;  /* set by any thread of the CTA that gives up */
-    volatile int32_t *decision;    /* thread 0's CTA-uniform go/stop, read after a barrier */
-};
 
 /* Shared-memory layout: every region sits at a compile-time offset (so the
  * region pointers fold into immediate addresses instead of occupying
@@ -313,41 +268,99 @@ constexpr size_t kOffHscal = kOffRed + 160 * 4;
 constexpr size_t kOffWbest = kOffHscal + 16 * 4;
 constexpr size_t kOffWbestI = kOffWbest + 8 * 4;
 constexpr size_t kOffBars = kOffWbestI + 8 * 4;
-constexpr size_t kOffFlags = kOffBars + 2 * kSlots * 8;
-constexpr size_t kOffExpTab = (kOffFlags + 16 + 15) & ~(size_t)15;
+constexpr size_t kOffFlags = kOffBars + kSlots * 8;
+constexpr size_t kOffShape = kOffFlags + 16;          /* [6 phase kinds][8] u32, see PhaseShape */
+constexpr size_t kOffIssued = kOffShape + 6 * 8 * 4;  /* [kSlots] u32 copies issued per ring slot */
+constexpr size_t kOffExpTab = (kOffIssued + kSlots * 4 + 15) & ~(size_t)15;
 constexpr size_t kOffXres = kOffExpTab + 128 * 4;
 constexpr size_t kMaxHidden = 2048;
 constexpr size_t kOffXs = kOffXres + kMaxHidden * 4;
 
-__device__ __forceinline__ Smem carve(uint8_t *base, int H, int I) {
-    (void)H;
-    (void)I;
-    Smem s;
-    s.ring = base + kOffRing;
-    s.xs = reinterpret_cast<float *>(base + kOffXs);
-    s.qn = s.xs;
-    s.kn = s.xs + 2 * kHeadDim;
-    s.xres = reinterpret_cast<float *>(base + kOffXres);
-    s.red = reinterpret_cast<float *>(base + kOffRed);
-    s.chain = reinterpret_cast<float *>(base + kOffChain);
-    s.hscal = reinterpret_cast<float *>(base + kOffHscal);
-    s.wbest = reinterpret_cast<float *>(base + kOffWbest);
-    s.wbest_i = reinterpret_cast<int32_t *>(base + kOffWbestI);
-    s.full = reinterpret_cast<uint64_t *>(base + kOffBars);
-    s.empty = reinterpret_cast<uint64_t *>(base + kOffBars + kSlots * 8);
-    s.abort_flag = reinterpret_cast<volatile int32_t *>(base + kOffFlags);
-    s.decision = reinterpret_cast<volatile int32_t *>(base + kOffFlags + 4);
-    return s;
+extern __shared__ __align__(128) uint8_t smem_raw[];
+
+/* Region accessors: constant offsets from the dynamic shared-memory base, so
+ * they fold into immediate addresses and need no registers or stack. */
+__device__ __forceinline__ uint8_t *sm_ring() { return smem_raw + kOffRing; }
+/* permuted phase input, max(H, I) floats; phase B: qn | kn */
+__device__ __forceinline__ float *sm_xs() { return reinterpret_cast<float *>(smem_raw + kOffXs); }
+/* [2][256] normalised q/k of the CTA's (at most two) heads */
+__device__ __forceinline__ float *sm_qn() { return sm_xs(); }
+__device__ __forceinline__ float *sm_kn() { return sm_xs() + 2 * kHeadDim; }
+/* residual stream, H floats (the same in every CTA) */
+__device__ __forceinline__ float *sm_xres() { return reinterpret_cast<float *>(smem_raw + kOffXres); }
+/* 160 floats: half sums [0,128), block partials [0,64), scalars [128,160) */
+__device__ __forceinline__ float *sm_red() { return reinterpret_cast<float *>(smem_raw + kOffRed); }
+/* [8 warps][512] per-warp GEMV bank partials */
+__device__ __forceinline__ float *sm_chain() { return reinterpret_cast<float *>(smem_raw + kOffChain); }
+/* [2][4] alpha, beta, decay per local head; [8, 16) per-head norm scales */
+__device__ __forceinline__ float *sm_hscal() { return reinterpret_cast<float *>(smem_raw + kOffHscal); }
+__device__ __forceinline__ float *sm_wbest() { return reinterpret_cast<float *>(smem_raw + kOffWbest); }
+__device__ __forceinline__ int32_t *sm_wbest_i() { return reinterpret_cast<int32_t *>(smem_raw + kOffWbestI); }
+__device__ __forceinline__ uint64_t *sm_full() { return reinterpret_cast<uint64_t *>(smem_raw + kOffBars); }
+/* per phase kind: unit_bytes, upc, u0, u1, chunks; then [8] = chunks per layer */
+__device__ __forceinline__ uint32_t *sm_shape() { return reinterpret_cast<uint32_t *>(smem_raw + kOffShape); }
+__device__ __forceinline__ uint32_t *sm_issued() { return reinterpret_cast<uint32_t *>(smem_raw + kOffIssued); }
+/* set by any thread of the CTA that gives up */
+__device__ __forceinline__ volatile int32_t *sm_abort_flag() {
+    return reinterpret_cast<volatile int32_t *>(smem_raw + kOffFlags);
+}
+/* thread 0's CTA-uniform go/stop, read after a barrier */
+__device__ __forceinline__ volatile int32_t *sm_decision() {
+    return reinterpret_cast<volatile int32_t *>(smem_raw + kOffFlags + 4);
 }
 
 size_t decode_smem_bytes(int H, int I) {
     return kOffXs + (size_t)4 * (H > I ? H : I);
 }
 
-extern __shared__ __align__(128) uint8_t smem_raw[];
-
 __device__ __forceinline__ const float *exp_table() {
     return reinterpret_cast<const float *>(smem_raw + kOffExpTab);
+}
+
+/* This CTA's share of phase kind ph in layer l, from the table. */
+__device__ __forceinline__ Geom geom(const DecodeParams &p, int l, int ph) {
+    const uint32_t *t = sm_shape() + ph * 8;
+    Geom g;
+    g.unit_bytes = t[0];
+    g.upc = t[1];
+    g.u0 = t[2];
+    g.u1 = t[3];
+    g.src = phase_src(p, l, ph);
+    return g;
+}
+
+/* Start the bulk copy of chunk q of the CTA's schedule (each layer's phases
+ * A..E, then the LM head) into ring slot q % kSlots; nothing past the end of
+ * the schedule. One lane calls this, once the slot's previous chunk has been
+ * read. Weights stream with L2 evict_first, the recurrent state with
+ * evict_last (it is written back right after). */
+__device__ __forceinline__ void issue_chunk(const DecodeParams &p, uint32_t q) {
+    const uint32_t *sh = sm_shape();
+    const uint32_t per_layer = sh[PH_LM * 8 + 7];
+    int l, ph;
+    uint32_t r;
+    if (q < (uint32_t)p.L * per_layer) {
+        l = (int)(q / per_layer);
+        r = q - (uint32_t)l * per_layer;
+        ph = 0;
+        while (ph < kPhasesPerLayer - 1 && r >= sh[(ph + 1) * 8 + 5]) ++ph;
+        r -= sh[ph * 8 + 5];
+    } else {
+        l = 0;
+        ph = PH_LM;
+        r = q - (uint32_t)p.L * per_layer;
+        if (r >= sh[PH_LM * 8 + 4]) return;
+    }
+    const uint32_t *t = sh + ph * 8;
+    const uint32_t u = t[2] + r * t[1];
+    const uint32_t n = (t[3] - u) < t[1] ? (t[3] - u) : t[1];
+    const uint32_t bytes = n * t[0];
+    const uint32_t slot = q % kSlots;
+    const uint32_t fb = smem_u32(&sm_full()[slot]);
+    atomicAdd(&sm_issued()[slot], 1u);
+    mbar_expect_tx(fb, bytes);
+    bulk_g2s(smem_u32(sm_ring() + (size_t)slot * kSlotBytes), phase_src(p, l, ph) + (size_t)u * t[0], bytes, fb,
+             ph == PH_STATE ? policy_evict_last() : policy_evict_first());
 }
 
 /* --------------------------------------------------- block-level helpers */
@@ -382,30 +395,30 @@ __device__ __forceinline__ void trace_put(const DecodeParams &p, int phase, int 
         p.trace[((size_t)blockIdx.x * (p.L * kPhasesPerLayer + 1) + phase) * kTraceSlots + slot] = gtimer();
 }
 
-__device__ __forceinline__ void raise_error(const DecodeParams &p, const Smem &s, int code, uint32_t where) {
+__device__ __forceinline__ void raise_error(const DecodeParams &p, int code, uint32_t where) {
     if (atomicCAS(&p.status->err, 0, code) == 0) {
         p.status->err_cta = blockIdx.x;
         p.status->err_where = where;
     }
-    *s.abort_flag = 1;
+    *sm_abort_flag() = 1;
 }
 
 /* Spin on one exchange word until it carries `tag`; returns the last word
  * read, whose tag differs from `tag` on abort/timeout. */
-__device__ __noinline__ xword xwait(const DecodeParams &p, const Smem &s, const xword *a, uint32_t tag) {
+__device__ __noinline__ xword xwait(const DecodeParams &p, const xword *a, uint32_t tag) {
     const uint64_t t0 = gtimer();
     uint32_t spins = 0;
     while (true) {
         const xword w = xget(a);
         if (xtag(w) == tag) return w;
-        if (*s.abort_flag) return w;
+        if (*sm_abort_flag()) return w;
         if ((++spins & 63u) == 0) {
             if (ld_volatile_i32(&p.status->err) != 0) {
-                *s.abort_flag = 1;
+                *sm_abort_flag() = 1;
                 return w;
             }
             if (gtimer() - t0 > kWaitNs) {
-                raise_error(p, s, kErrExchangeTimeout, tag);
+                raise_error(p, kErrExchangeTimeout, tag);
                 return w;
             }
         }
@@ -424,7 +437,7 @@ __device__ __forceinline__ void xget2(const xword *p, xword &a, xword &b) {
  * warp re-reads everything still missing. All 32 lanes must call; lanes with
  * n == 0 take part in the protocol only. */
 template <int N>
-__device__ __forceinline__ bool xread(const DecodeParams &p, const Smem &s, const xword *src, int stride, int n,
+__device__ __forceinline__ bool xread(const DecodeParams &p, const xword *src, int stride, int n,
                                       uint32_t tag, float (&v)[N]) {
     const int lane = threadIdx.x & 31;
     xword w[N];
@@ -449,7 +462,7 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Smem &s, cons
         int ok = 1;
         if (lane == leader) {
             const int i = __ffs(missing) - 1;
-            ok = xtag(xwait(p, s, src + (size_t)i * stride, tag)) == tag;
+            ok = xtag(xwait(p, src + (size_t)i * stride, tag)) == tag;
         }
         if (!__shfl_sync(0xffffffffu, ok, leader)) return false;
 #pragma unroll
@@ -460,7 +473,7 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Smem &s, cons
             if (((missing >> i) & 1u) && xtag(w[i]) == tag) missing &= ~(1u << i);
         if (t0 == 0) t0 = gtimer();
         else if (gtimer() - t0 > kWaitNs) {
-            if (missing) raise_error(p, s, kErrExchangeTimeout, tag);
+            if (missing) raise_error(p, kErrExchangeTimeout, tag);
             return false;
         }
     }
@@ -470,37 +483,41 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Smem &s, cons
     return true;
 }
 
-/* Read n exchange words (element t + 256 j, n/256 <= 32 per thread) into the
- * permuted shared input, with xread's protocol. All consumer threads call. */
-__device__ __noinline__ bool xread_to_xs(const DecodeParams &p, const Smem &s, const xword *src, int n, uint32_t tag) {
+/* Read n exchange words into the permuted shared input, with xread's
+ * protocol: thread t takes the n/256 consecutive words from t * n/256 (an
+ * even count, so 16-byte vector loads; n <= 5632, the workspace ABI's
+ * intermediate size). All consumer threads call. */
+constexpr int kMaxWordsPerThread = 22;
+__device__ __forceinline__ bool xread_to_xs(const DecodeParams &p, const xword *src, int n, uint32_t tag) {
     const int t = threadIdx.x;
-    float v[32];
-    const bool ok = xread<32>(p, s, src + t, 256, n >> 8, tag, v);
+    const int per = n >> 8;
+    float v[kMaxWordsPerThread];
+    const bool ok = xread<kMaxWordsPerThread>(p, src + t * per, 1, per, tag, v);
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-        if (j < (n >> 8)) s.xs[xs_pos(t + (j << 8))] = v[j];
+    for (int j = 0; j < kMaxWordsPerThread; ++j)
+        if (j < per) sm_xs()[xs_pos(t * per + j)] = v[j];
     return ok;
 }
 
 /* Single-lane read of one exchange word. */
-__device__ __forceinline__ bool xread1(const DecodeParams &p, const Smem &s, const xword *src, uint32_t tag,
+__device__ __forceinline__ bool xread1(const DecodeParams &p, const xword *src, uint32_t tag,
                                        float &v) {
     xword w = xget(src);
-    if (xtag(w) != tag) w = xwait(p, s, src, tag);
+    if (xtag(w) != tag) w = xwait(p, src, tag);
     v = xval(w);
     return xtag(w) == tag;
 }
 
 /* Wait for a ring slot to be filled; false on abort. */
-__device__ __forceinline__ bool wait_full(const DecodeParams &p, const Smem &s, uint32_t slot, uint32_t parity) {
-    const uint32_t bar = smem_u32(&s.full[slot]);
+__device__ __forceinline__ bool wait_full(const DecodeParams &p, uint32_t slot, uint32_t parity) {
+    const uint32_t bar = smem_u32(&sm_full()[slot]);
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = gtimer();
     while (true) {
         if (mbar_try(bar, parity)) return true;
-        if (*s.abort_flag) return false;
+        if (*sm_abort_flag()) return false;
         if (gtimer() - t0 > kWaitNs) {
-            raise_error(p, s, kErrChunkTimeout, slot);
+            raise_error(p, kErrChunkTimeout, slot);
             return false;
         }
     }
@@ -556,7 +573,8 @@ __device__ __forceinline__ float tree16_half(const uint4 &w0, const uint4 &w1, c
  * Every lane returns all row sums. */
 template <int MODE>
 __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, unsigned tiny, const float *xs,
-                                         float *chain, uint32_t empty_bar, float (&out)[4]) {
+                                         float *chain, const DecodeParams &p, uint32_t refill_q,
+                                         float (&out)[4]) {
     const int lane = threadIdx.x & 31;
     const int G = K >> 9;           /* 512-column groups */
     const int C = K >> 6;           /* halves per bank of one row */
@@ -580,10 +598,10 @@ __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, 
             }
         }
     }
-    /* the weights have been read: hand the ring slot back before the bank
-     * chains and the epilogue, so it can be refilled sooner */
+    /* the weights have been read: refill the ring slot before the bank
+     * chains and the epilogue */
     __syncwarp();
-    if (lane == 0) mbar_arrive(empty_bar);
+    if (lane == 0) issue_chunk(p, refill_q);
     const int r = lane >> 2, b = lane & 3;
     float acc = 0.0f;
     const bool is_tiny = r < nrows && ((tiny >> r) & 1u);
@@ -639,7 +657,7 @@ __device__ __forceinline__ float seq_sum(const float *a, int n) {
  * sequentially (by lane 0 of every working warp, so no second barrier);
  * scale = 1/sqrtf(sum/H + eps); out = round((x*scale)*w). */
 template <int MODE>
-__device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s, const xword *y, uint32_t tag,
+__device__ __forceinline__ bool prologue_norm(const DecodeParams &p, const xword *y, uint32_t tag,
                                            const float *w, bool embed, float *hidden, int pidx) {
     const int t = threadIdx.x, lane = t & 31;
     const int halves = p.H >> 4;
@@ -670,24 +688,24 @@ __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s,
             }
         } else {
             float yv[16];
-            ok = xread<16>(p, s, y + 16 * t, 1, 16, tag, yv);
+            ok = xread<16>(p, y + 16 * t, 1, 16, tag, yv);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) x[i] = bnd<MODE>(__fadd_rn(s.xres[16 * t + i], yv[i]));
+            for (int i = 0; i < 16; ++i) x[i] = bnd<MODE>(__fadd_rn(sm_xres()[16 * t + i], yv[i]));
         }
         if (t == 0) trace_put(p, pidx, 1);
         float hs = 0.0f;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             hs = __fadd_rn(hs, __fmul_rn(x[i], x[i]));
-            s.xres[16 * t + i] = x[i];
+            sm_xres()[16 * t + i] = x[i];
         }
-        s.red[t] = hs;
+        sm_red()[t] = hs;
     }
     named_sync(1, kConsumerThreads);
     if (t < halves) {
         float scale = 0.0f;
         if (lane == 0) {
-            const float sum = seq_sum(s.red, halves);
+            const float sum = seq_sum(sm_red(), halves);
             scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)p.H), p.eps)));
             if (t == 0) trace_put(p, pidx, 6);
         }
@@ -695,7 +713,7 @@ __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s,
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const float o = bnd<MODE>(__fmul_rn(__fmul_rn(x[i], scale), wv[i]));
-            s.xs[xs_pos(16 * t + i)] = o;
+            sm_xs()[xs_pos(16 * t + i)] = o;
             if (hidden != nullptr) hidden[16 * t + i] = o;
         }
     }
@@ -708,32 +726,35 @@ __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const Smem &s,
  * eps); out = round(((a*scale)*w) * g * sigmoid(g)). The elementwise tail runs
  * on all consumer threads, eight independent elements each. */
 template <int MODE>
-__device__ __noinline__ bool prologue_norm_gate(const DecodeParams &p, const Smem &s, const float *o_norm,
+__device__ __forceinline__ bool prologue_norm_gate(const DecodeParams &p, const float *o_norm,
                                                 uint32_t tag_a, uint32_t tag_b, int pidx) {
     const int t = threadIdx.x;
-    const int halves = p.H >> 4;
+    const int halves = p.H >> 4; /* a multiple of 32, at most 128 */
     bool ok = true;
-    float *a_sh = s.chain, *g_sh = s.chain + p.H; /* H <= 2048: both fit the 16 KB scratch */
-    if (t < halves) {
-        float a[16], g[16];
-        ok = xread<16>(p, s, p.gate + 16 * t, 1, 16, tag_a, g);
-        ok = xread<16>(p, s, p.attn + 16 * t, 1, 16, tag_b, a) && ok;
-        if (t == 0) trace_put(p, pidx, 1);
+    float *a_sh = sm_chain(), *g_sh = sm_chain() + p.H; /* H <= 2048: both fit the 16 KB scratch */
+    if (t < 2 * halves) {
+        /* warps [0, halves/32) read the gate, the next ones the attention
+         * output, 16 words per thread, all in one round trip */
+        const bool is_attn = t >= halves;
+        const int hidx = is_attn ? t - halves : t;
+        float v[16];
+        ok = xread<16>(p, (is_attn ? p.attn : p.gate) + 16 * hidx, 1, 16, is_attn ? tag_b : tag_a, v);
+        if (t == halves) trace_put(p, pidx, 1);
+        float *dst = (is_attn ? a_sh : g_sh) + 16 * hidx;
         float hs = 0.0f;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            hs = __fadd_rn(hs, __fmul_rn(a[i], a[i]));
-            a_sh[16 * t + i] = a[i];
-            g_sh[16 * t + i] = g[i];
+            hs = __fadd_rn(hs, __fmul_rn(v[i], v[i]));
+            dst[i] = v[i];
         }
-        s.red[t] = hs;
+        if (is_attn) sm_red()[hidx] = hs;
     }
     named_sync(1, kConsumerThreads);
     if (t < p.nh) {
         float sum = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) sum = __fadd_rn(sum, s.red[16 * t + j]);
-        s.hscal[8 + t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 256.0f), p.eps)));
+        for (int j = 0; j < 16; ++j) sum = __fadd_rn(sum, sm_red()[16 * t + j]);
+        sm_hscal()[8 + t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 256.0f), p.eps)));
         if (t == 0) trace_put(p, pidx, 6);
     }
     named_sync(1, kConsumerThreads);
@@ -752,21 +773,21 @@ __device__ __noinline__ bool prologue_norm_gate(const DecodeParams &p, const Sme
     for (int i = 0; i < 8; ++i) {
         if (i < per) {
             const int e = per * t + i;
-            const float scale = s.hscal[8 + (e >> 8)];
+            const float scale = sm_hscal()[8 + (e >> 8)];
             const float normalized = __fmul_rn(__fmul_rn(av[i], scale), wv[i]);
             out[i] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv[i]), sigmoid_ref(gv[i])));
         }
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-        if (i < per) s.xs[xs_pos(per * t + i)] = out[i];
+        if (i < per) sm_xs()[xs_pos(per * t + i)] = out[i];
     return ok;
 }
 
 /* q/k L2 norms (balanced tree order of gdn_tree_reduce_256), alpha, beta
  * and decay for the CTA's heads (c_impl/gdn_model.cpp:2059-2124); all reads
  * are issued before any reduction. */
-__device__ __noinline__ bool prologue_state(const DecodeParams &p, const Smem &s, int l, int h0, int h1,
+__device__ __forceinline__ bool prologue_state(const DecodeParams &p, int l, int h0, int h1,
                                             uint32_t tag) {
     const int t = threadIdx.x;
     const int nhl = h1 - h0 + 1; /* 1 or 2 */
@@ -786,8 +807,8 @@ __device__ __noinline__ bool prologue_state(const DecodeParams &p, const Smem &s
         float v4[4];
         const xword *base = p.qkv + h0 * kHeadDim + t;
         float vq[2], vk[2];
-        ok = xread<2>(p, s, base, kHeadDim, nhl, tag, vq) && ok;
-        ok = xread<2>(p, s, base + p.H, kHeadDim, nhl, tag, vk) && ok;
+        ok = xread<2>(p, base, kHeadDim, nhl, tag, vq) && ok;
+        ok = xread<2>(p, base + p.H, kHeadDim, nhl, tag, vk) && ok;
         v4[0] = vq[0];
         v4[1] = vk[0];
         v4[2] = nhl > 1 ? vq[1] : 0.0f;
@@ -797,12 +818,12 @@ __device__ __noinline__ bool prologue_state(const DecodeParams &p, const Smem &s
     }
     if (t < 2 * nhl) {
         const int h = h0 + (t >> 1);
-        ok = xread1(p, s, p.ab + ((t & 1) ? p.nh + h : h), tag, (t & 1) ? bv : av) && ok;
+        ok = xread1(p, p.ab + ((t & 1) ? p.nh + h : h), tag, (t & 1) ? bv : av) && ok;
     }
     float sq[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) sq[i] = __fmul_rn(qk[i], qk[i]);
-    block_sum<4>(sq, s.red);
+    block_sum<4>(sq, sm_red());
     float al[2];
 #pragma unroll
     for (int hs = 0; hs < 2; ++hs) {
@@ -810,12 +831,12 @@ __device__ __noinline__ bool prologue_state(const DecodeParams &p, const Smem &s
         const float k_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sq[2 * hs + 1], 1e-6f)));
         const float qn = __fmul_rn(qk[2 * hs], q_inv), kn = __fmul_rn(qk[2 * hs + 1], k_inv);
         if (hs < nhl) {
-            s.qn[hs * kHeadDim + t] = qn;
-            s.kn[hs * kHeadDim + t] = kn;
+            sm_qn()[hs * kHeadDim + t] = qn;
+            sm_kn()[hs * kHeadDim + t] = kn;
         }
         al[hs] = __fmul_rn(qn, kn);
     }
-    block_sum<2>(al, s.red + 32);
+    block_sum<2>(al, sm_red() + 32);
     /* beta and decay: thread 2h read a_h, thread 2h+1 read b_h (full-warp
      * shuffle; only threads 0..3 use the result) */
     const float other = __shfl_xor_sync(0xffffffffu, (t & 1) ? bv : av, 1);
@@ -826,9 +847,9 @@ __device__ __noinline__ bool prologue_state(const DecodeParams &p, const Smem &s
             const float beta = sigmoid_ref(b_h);
             const float decay_in = __fadd_rn(av, dtb);
             const float decay_val = __fmul_rn(-exp_ref(alog), softplus_ref(decay_in));
-            s.hscal[hs * 4 + 0] = al[hs];
-            s.hscal[hs * 4 + 1] = beta;
-            s.hscal[hs * 4 + 2] = exp_ref(decay_val);
+            sm_hscal()[hs * 4 + 0] = al[hs];
+            sm_hscal()[hs * 4 + 1] = beta;
+            sm_hscal()[hs * 4 + 2] = exp_ref(decay_val);
         }
     }
     return ok;
@@ -837,95 +858,43 @@ __device__ __noinline__ bool prologue_state(const DecodeParams &p, const Smem &s
 /* ------------------------------------------------------------ the kernel */
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodeParams p) {
-    const Smem s = carve(smem_raw, p.H, p.I);
+__global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_constant__ DecodeParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t cta = blockIdx.x, ncta = gridDim.x;
 
     if (threadIdx.x < 128)
         reinterpret_cast<float *>(smem_raw + kOffExpTab)[threadIdx.x] = __ldg(p.exp_table + threadIdx.x);
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < kSlots; ++i) {
-            mbar_init(smem_u32(&s.full[i]), 1);
-            mbar_init(smem_u32(&s.empty[i]), 1);
-        }
-        *s.abort_flag = 0;
-        *s.decision = 1;
+    if (threadIdx.x < 6) {
+        const Geom g = geom_compute(p, threadIdx.x, cta, ncta);
+        uint32_t *t = sm_shape() + threadIdx.x * 8;
+        t[0] = g.unit_bytes;
+        t[1] = g.upc;
+        t[2] = g.u0;
+        t[3] = g.u1;
+        t[4] = (g.u1 - g.u0 + g.upc - 1) / g.upc;
+    }
+    if (threadIdx.x >= 32 && threadIdx.x < 32 + kSlots) sm_issued()[threadIdx.x - 32] = 0;
+    if (threadIdx.x == 64) {
+        for (int i = 0; i < kSlots; ++i) mbar_init(smem_u32(&sm_full()[i]), 1);
+        *sm_abort_flag() = 0;
+        *sm_decision() = 1;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-
-    if (warp == kConsumerWarps) {
-        /* ------------------------------------------------ producer warp */
-        if (lane == 0) {
-            const uint64_t pol_w = policy_evict_first();
-            const uint64_t pol_s = policy_evict_last();
-            uint32_t seq = 0;
-            bool ok = true;
-            Cursor pf;
-            cursor_init(p, pf, cta, ncta);
-            uint32_t pf_ahead = 0;  /* bytes prefetched into L2 but not yet copied to the ring */
-            for (int l = 0; l <= p.L && ok; ++l) {
-                const int nph = (l < p.L) ? kPhasesPerLayer : 1;
-                for (int pi = 0; pi < nph && ok; ++pi) {
-                    const int ph = (l < p.L) ? pi : PH_LM;
-                    const Geom g = geom(p, l < p.L ? l : 0, ph, cta, ncta);
-                    for (uint32_t u = g.u0; u < g.u1; u += g.upc, ++seq) {
-                        const uint32_t n = (g.u1 - u) < g.upc ? (g.u1 - u) : g.upc;
-                        const uint32_t slot = seq % kSlots;
-                        if (seq >= (uint32_t)kSlots) {
-                            const uint32_t bar = smem_u32(&s.empty[slot]);
-                            const uint32_t par = ((seq / kSlots) + 1u) & 1u;
-                            if (!mbar_try(bar, par)) {
-                                const uint64_t t0 = gtimer();
-                                while (!mbar_try(bar, par)) {
-                                    if (*s.abort_flag) { ok = false; break; }
-                                    if (gtimer() - t0 > kWaitNs) {
-                                        raise_error(p, s, kErrSlotTimeout, seq);
-                                        ok = false;
-                                        break;
-                                    }
-                                }
-                                if (!ok) break;
-                            }
-                        }
-                        if (*s.abort_flag) { ok = false; break; }
-                        const uint32_t bytes = n * g.unit_bytes;
-                        while (pf_ahead < (uint32_t)kPrefetchBytes && cursor_valid(p, pf)) {
-                            const uint32_t pn = (pf.g.u1 - pf.u) < pf.g.upc ? (pf.g.u1 - pf.u) : pf.g.upc;
-                            const uint32_t pbytes = pn * pf.g.unit_bytes;
-                            bulk_prefetch_l2(pf.g.src + (size_t)pf.u * pf.g.unit_bytes, pbytes);
-                            pf_ahead += pbytes;
-                            pf.u += pf.g.upc;
-                            cursor_settle(p, pf, cta, ncta);
-                        }
-                        pf_ahead -= bytes;
-                        const uint32_t fb = smem_u32(&s.full[slot]);
-                        if (p.trace != nullptr) {
-                            const int pidx = l * kPhasesPerLayer + pi;
-                            if (u == g.u0) trace_put(p, pidx, 4);
-                            trace_put(p, pidx, 5);
-                        }
-                        mbar_expect_tx(fb, bytes);
-                        bulk_g2s(smem_u32(s.ring + (size_t)slot * kSlotBytes), g.src + (size_t)u * g.unit_bytes,
-                                 bytes, fb, ph == PH_STATE ? pol_s : pol_w);
-                    }
-                }
-            }
-            /* Drain: every issued copy must land before the CTA may exit. */
-            const uint32_t issued = seq;
-            const uint32_t first = issued > (uint32_t)kSlots ? issued - kSlots : 0u;
-            for (uint32_t q = first; q < issued; ++q) {
-                const uint32_t bar = smem_u32(&s.full[q % kSlots]);
-                const uint32_t par = (q / kSlots) & 1u;
-                const uint64_t t0 = gtimer();
-                while (!mbar_try(bar, par)) {
-                    if (gtimer() - t0 > kWaitNs) break;
-                }
-            }
+    if (threadIdx.x == 0) {
+        /* chunk index of each phase's first chunk inside a layer, chunks per layer */
+        uint32_t acc = 0;
+        for (int ph = 0; ph < kPhasesPerLayer; ++ph) {
+            sm_shape()[ph * 8 + 5] = acc;
+            acc += sm_shape()[ph * 8 + 4];
         }
-        __syncwarp();
-    } else {
+        sm_shape()[PH_LM * 8 + 5] = 0;
+        sm_shape()[PH_LM * 8 + 7] = acc;
+        for (uint32_t q = 0; q < (uint32_t)kSlots; ++q) issue_chunk(p, q);
+    }
+    __syncthreads();
+
+    {
         /* ---------------------------------------------- consumer warps */
         uint32_t seq = 0;
         float best = -3.402823466e38f;
@@ -938,62 +907,74 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
             for (int pi = 0; pi < nph && ok; ++pi) {
                 const int ph = (l < p.L) ? pi : PH_LM;
                 const int pidx = l * kPhasesPerLayer + pi;
-                const Geom g = geom(p, l < p.L ? l : 0, ph, cta, ncta);
+                const Geom g = geom(p, l < p.L ? l : 0, ph);
                 /* every consumer warp is done with the previous phase's chunks
                  * (shared inputs may be overwritten) */
                 named_sync(1, kConsumerThreads);
                 if (threadIdx.x == 0) trace_put(p, pidx, 0);
                 int h0 = 0, h1 = 0;
                 bool in_ok = true;
+                /* the residual-stream RMSNorm phases (A, D, LM head) share one
+                 * call site, so its body is instantiated once */
+                bool norm_phase = false, embed = false;
+                const xword *ny = nullptr;
+                uint32_t ntag = 0;
+                const float *nw = aux;
+                float *hidden = nullptr;
                 switch (ph) {
                 case PH_QKVG:
+                    norm_phase = true;
                     if (l == 0) {
                         if (p.token_src != nullptr) {
                             const int32_t tok = *p.token_src;
                             if (tok < 0 || tok >= p.V) {
                                 /* every consumer thread reads the same token: uniform exit */
-                                if (threadIdx.x == 0) raise_error(p, s, kErrBadToken, (uint32_t)tok);
+                                if (threadIdx.x == 0) raise_error(p, kErrBadToken, (uint32_t)tok);
                                 ok = false;
                                 break;
                             }
                         }
-                        in_ok = prologue_norm<MODE>(p, s, nullptr, 0, aux, true, nullptr, pidx);
+                        embed = true;
                     } else {
-                        in_ok = prologue_norm<MODE>(p, s, p.y_down, tag_base - kPhasesPerLayer + PH_DOWN, aux,
-                                                    false, nullptr, pidx);
+                        ny = p.y_down;
+                        ntag = tag_base - kPhasesPerLayer + PH_DOWN;
                     }
                     break;
                 case PH_STATE:
                     if (g.u1 > g.u0) {
                         h0 = (int)(g.u0 >> 8);
                         h1 = (int)((g.u1 - 1) >> 8);
-                        in_ok = prologue_state(p, s, l, h0, h1, tag_base + PH_QKVG);
+                        in_ok = prologue_state(p, l, h0, h1, tag_base + PH_QKVG);
                         if (threadIdx.x == 0) trace_put(p, pidx, 1);
                     }
                     break;
                 case PH_O:
-                    in_ok = prologue_norm_gate<MODE>(p, s, aux + p.H, tag_base + PH_QKVG, tag_base + PH_STATE, pidx);
+                    in_ok = prologue_norm_gate<MODE>(p, aux + p.H, tag_base + PH_QKVG, tag_base + PH_STATE, pidx);
                     break;
                 case PH_GU:
-                    in_ok = prologue_norm<MODE>(p, s, p.y_o, tag_base + PH_O, aux + p.H + kHeadDim, false, nullptr, pidx);
+                    norm_phase = true;
+                    ny = p.y_o;
+                    ntag = tag_base + PH_O;
+                    nw = aux + p.H + kHeadDim;
                     break;
                 case PH_DOWN:
-                    in_ok = xread_to_xs(p, s, p.m, p.I, tag_base + PH_GU);
+                    in_ok = xread_to_xs(p, p.m, p.I, tag_base + PH_GU);
                     if (threadIdx.x == 0) trace_put(p, pidx, 1);
                     break;
-                default: {
-                    const float *final_norm = p.aux + (size_t)p.L * p.aux_stride;
-                    in_ok = prologue_norm<MODE>(p, s, p.y_down,
-                                                p.epoch + (uint32_t)((p.L - 1) * kPhasesPerLayer + PH_DOWN),
-                                                final_norm, false, cta == 0 ? p.hidden_out : nullptr, pidx);
+                default:
+                    norm_phase = true;
+                    ny = p.y_down;
+                    ntag = p.epoch + (uint32_t)((p.L - 1) * kPhasesPerLayer + PH_DOWN);
+                    nw = p.aux + (size_t)p.L * p.aux_stride;
+                    hidden = cta == 0 ? p.hidden_out : nullptr;
                     break;
                 }
-                }
+                if (ok && norm_phase) in_ok = prologue_norm<MODE>(p, ny, ntag, nw, embed, hidden, pidx);
                 if (!ok) break;
                 (void)in_ok;  /* a failed read has raised the abort flag */
-                if (threadIdx.x == 0) *s.decision = (*s.abort_flag == 0) ? 1 : 0;
+                if (threadIdx.x == 0) *sm_decision() = (*sm_abort_flag() == 0) ? 1 : 0;
                 named_sync(1, kConsumerThreads);
-                if (*s.decision == 0) { ok = false; break; }
+                if (*sm_decision() == 0) { ok = false; break; }
                 if (threadIdx.x == 0) trace_put(p, pidx, 2);
 
                 const uint32_t tag_out = tag_base + (uint32_t)ph;
@@ -1003,10 +984,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                  * barriers; the stop is taken uniformly at the next phase. */
                 for (uint32_t u = g.u0; u < g.u1; u += g.upc, ++seq) {
                     if ((int)(seq % kConsumerWarps) != warp) continue;
-                    if (*s.abort_flag) continue;
+                    if (*sm_abort_flag()) continue;
                     const uint32_t n = (g.u1 - u) < g.upc ? (g.u1 - u) : g.upc;
                     const uint32_t slot = seq % kSlots;
-                    const uint8_t *buf = s.ring + (size_t)slot * kSlotBytes;
+                    const uint8_t *buf = sm_ring() + (size_t)slot * kSlotBytes;
 
                     /* per-row side inputs, fetched before waiting for the chunk */
                     float4 tail = make_float4(0.f, 0.f, 0.f, 0.f), cw = tail;
@@ -1023,9 +1004,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                         }
                     }
                     float vv = 0.0f;
-                    if (ph == PH_STATE && lane < (int)n) xread1(p, s, p.qkv + 2 * p.H + u + lane, tag_base + PH_QKVG, vv);
+                    if (ph == PH_STATE && lane < (int)n) xread1(p, p.qkv + 2 * p.H + u + lane, tag_base + PH_QKVG, vv);
 
-                    if (!wait_full(p, s, slot, (seq / kSlots) & 1u)) continue;
+                    if (!wait_full(p, slot, (seq / kSlots) & 1u)) continue;
 
                     if (ph == PH_STATE) {
                         /* read pass, sequential over k for each column (lane j owns
@@ -1034,8 +1015,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                         if (lane < (int)n) {
                             const int hs = (int)((u + lane) >> 8) - h0;
                             const float4 *col = reinterpret_cast<const float4 *>(buf) + lane * (kHeadDim / 4);
-                            const float4 *kn4 = reinterpret_cast<const float4 *>(s.kn + hs * kHeadDim);
-                            const float4 *qn4 = reinterpret_cast<const float4 *>(s.qn + hs * kHeadDim);
+                            const float4 *kn4 = reinterpret_cast<const float4 *>(sm_kn() + hs * kHeadDim);
+                            const float4 *qn4 = reinterpret_cast<const float4 *>(sm_qn() + hs * kHeadDim);
 #pragma unroll 4
                             for (int k = 0; k < kHeadDim / 4; ++k) {
                                 const float4 sv = col[k], kv = kn4[k], qv = qn4[k];
@@ -1055,9 +1036,9 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                             const float rj = __shfl_sync(0xffffffffu, r, j);
                             const float pj = __shfl_sync(0xffffffffu, pp, j);
                             const float vj = __shfl_sync(0xffffffffu, vv, j);
-                            const float alpha = s.hscal[hs * 4 + 0];
-                            const float beta = s.hscal[hs * 4 + 1];
-                            const float decay = s.hscal[hs * 4 + 2];
+                            const float alpha = sm_hscal()[hs * 4 + 0];
+                            const float beta = sm_hscal()[hs * 4 + 1];
+                            const float decay = sm_hscal()[hs * 4 + 2];
                             /* c_impl/gdn_model.cpp:2214-2243 */
                             const float delta = __fmul_rn(beta, __fsub_rn(vj, __fmul_rn(decay, rj)));
                             const float o =
@@ -1065,7 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                             if (lane == 0) xput(p.attn + c, bnd<MODE>(o), tag_out);
                             /* update, c_impl/gdn_model.cpp:2268-2300 */
                             const float *colp = reinterpret_cast<const float *>(buf) + j * kHeadDim + lane * 8;
-                            const float *knp = s.kn + hs * kHeadDim + lane * 8;
+                            const float *knp = sm_kn() + hs * kHeadDim + lane * 8;
                             const float4 s0 = *reinterpret_cast<const float4 *>(colp);
                             const float4 s1 = *reinterpret_cast<const float4 *>(colp + 4);
                             const float4 k0 = *reinterpret_cast<const float4 *>(knp);
@@ -1097,8 +1078,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                             for (uint32_t j = 0; j < n; ++j)
                                 if (u + j >= 4u * p.H) tiny |= 1u << j;
                         }
-                        warp_dot<MODE>(buf, K, (int)((ph == PH_GU) ? 2 * n : n), tiny, s.xs,
-                                       s.chain + warp * 512, smem_u32(&s.empty[slot]), out);
+                        warp_dot<MODE>(buf, K, (int)((ph == PH_GU) ? 2 * n : n), tiny, sm_xs(),
+                                       sm_chain() + warp * 512, p, seq + kSlots, out);
                         float y = out[0];
                         if (lane == 1) y = out[1];
                         if (lane == 2) y = out[2];
@@ -1153,7 +1134,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
                         }
                     }
                     __syncwarp();
-                    if (ph == PH_STATE && lane == 0) mbar_arrive(smem_u32(&s.empty[slot]));
+                    if (ph == PH_STATE && lane == 0) issue_chunk(p, seq + kSlots);
                 }
                 if (threadIdx.x == 0) trace_put(p, pidx, 3);
             }
@@ -1161,20 +1142,20 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
 
         /* LM-head argmax: warps -> CTA candidate -> the last CTA picks the token */
         named_sync(1, kConsumerThreads);
-        if (threadIdx.x == 0) *s.decision = (ok && *s.abort_flag == 0) ? 1 : 0;
+        if (threadIdx.x == 0) *sm_decision() = (ok && *sm_abort_flag() == 0) ? 1 : 0;
         named_sync(1, kConsumerThreads);
-        if (*s.decision != 0) {
+        if (*sm_decision() != 0) {
             if (lane == 0) {
-                s.wbest[warp] = best;
-                s.wbest_i[warp] = best_i;
+                sm_wbest()[warp] = best;
+                sm_wbest_i()[warp] = best_i;
             }
             named_sync(1, kConsumerThreads);
             if (threadIdx.x == 0) {
-                float b = s.wbest[0];
-                int32_t bi = s.wbest_i[0];
+                float b = sm_wbest()[0];
+                int32_t bi = sm_wbest_i()[0];
                 for (int w = 1; w < kConsumerWarps; ++w) {
-                    const float v = s.wbest[w];
-                    const int32_t vi = s.wbest_i[w];
+                    const float v = sm_wbest()[w];
+                    const int32_t vi = sm_wbest_i()[w];
                     if (v > b || (v == b && vi < bi)) { b = v; bi = vi; }
                 }
                 p.cand_val[cta] = b;
@@ -1200,6 +1181,19 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const DecodePar
         }
     }
     __syncthreads();
+    /* Every bulk copy issued into the ring must land before the CTA exits
+     * (only a CTA that gave up mid-schedule can have one in flight; each
+     * slot has at most one, its latest). */
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kSlots; ++i) {
+            const uint32_t n = sm_issued()[i];
+            if (n == 0) continue;
+            const uint32_t bar = smem_u32(&sm_full()[i]);
+            const uint64_t t0 = gtimer();
+            while (!mbar_try(bar, (n - 1) & 1u))
+                if (gtimer() - t0 > kWaitNs) break;
+        }
+    }
 }
 
 template <int MODE>

@@ -40,14 +40,13 @@ namespace gdn {
 constexpr int kHeadDim = 256;
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;      /* + one producer warp */
+constexpr int kThreads = kConsumerThreads;
 constexpr int kSlotBytes = 16384;
 constexpr int kSlots = 11;
 constexpr int kMaxRowsPerChunk = 4;
 constexpr int kColsPerChunk = 2;
 constexpr int kPhasesPerLayer = 5;
 constexpr int kTraceSlots = 8;
-constexpr int kPrefetchBytes = 256 * 1024;  /* per-CTA L2 prefetch lookahead of the weight stream */
 
 /* error codes written to DecodeStatus.err */
 enum {
@@ -105,9 +104,8 @@ struct DecodeParams {
     /* optional phase trace, %globaltimer ns: [cta][phase][kTraceSlots], phase =
      * layer * 5 + {A..E}, L * 5 = LM head. Slots: 0 consumers done with the
      * previous phase, 1 phase inputs arrived, 2 phase input built, 3 consumer
-     * chunks done (warp 0), 4 producer's first copy of the phase issued, 5 its
-     * last copy issued, 6 input reduction (norm sums, head scalars) done,
-     * 7 unused. */
+     * chunks done (warp 0), 6 input reduction (norm sums, head scalars) done;
+     * 4, 5 and 7 unused. */
     unsigned long long *trace;
 };
 
