@@ -508,16 +508,23 @@ __device__ __forceinline__ bool xread1(const DecodeParams &p, const xword *src, 
     return xtag(w) == tag;
 }
 
-/* Wait for a ring slot to be filled; false on abort. */
-__device__ __forceinline__ bool wait_full(const DecodeParams &p, uint32_t slot, uint32_t parity) {
+/* Wait until chunk q of the schedule sits in its ring slot; false on abort.
+ * The slot's copy of q is issued only after the slot's previous chunk
+ * (q - kSlots) has been read, but a warp may reach q earlier than that: it
+ * first waits (in shared memory) for the issue, so that the mbarrier it then
+ * waits on is never more than one phase ahead of the copy -- the parity test
+ * cannot tell phase k from phase k - 2. */
+__device__ __forceinline__ bool wait_full(const DecodeParams &p, uint32_t q) {
+    const uint32_t slot = q % kSlots, k = q / kSlots;
     const uint32_t bar = smem_u32(&sm_full()[slot]);
-    if (mbar_try(bar, parity)) return true;
+    const volatile uint32_t *issued = sm_issued() + slot;
+    if (*issued > k && mbar_try(bar, k & 1u)) return true;
     const uint64_t t0 = gtimer();
     while (true) {
-        if (mbar_try(bar, parity)) return true;
+        if (*issued > k && mbar_try(bar, k & 1u)) return true;
         if (*sm_abort_flag()) return false;
         if (gtimer() - t0 > kWaitNs) {
-            raise_error(p, kErrChunkTimeout, slot);
+            raise_error(p, kErrChunkTimeout, q);
             return false;
         }
     }
@@ -758,29 +765,19 @@ __device__ __forceinline__ bool prologue_norm_gate(const DecodeParams &p, const 
         if (t == 0) trace_put(p, pidx, 6);
     }
     named_sync(1, kConsumerThreads);
+    /* thread t takes elements t + 256 i (head i): conflict-free shared
+     * accesses and a single o_norm weight per thread */
     const int per = p.H >> 8; /* <= 8 elements per thread */
-    float wv[8], av[8], gv[8], out[8];
+    const float wv = __ldg(o_norm + t);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         if (i < per) {
-            const int e = per * t + i;
-            wv[i] = __ldg(o_norm + (e & 255));
-            av[i] = a_sh[e];
-            gv[i] = g_sh[e];
+            const int e = t + (i << 8);
+            const float gv = g_sh[e];
+            const float normalized = __fmul_rn(__fmul_rn(a_sh[e], sm_hscal()[8 + i]), wv);
+            sm_xs()[xs_pos(e)] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv), sigmoid_ref(gv)));
         }
     }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        if (i < per) {
-            const int e = per * t + i;
-            const float scale = sm_hscal()[8 + (e >> 8)];
-            const float normalized = __fmul_rn(__fmul_rn(av[i], scale), wv[i]);
-            out[i] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv[i]), sigmoid_ref(gv[i])));
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        if (i < per) sm_xs()[xs_pos(per * t + i)] = out[i];
     return ok;
 }
 
@@ -900,10 +897,15 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
         float best = -3.402823466e38f;
         int32_t best_i = 0;
         bool ok = true;
+        /* the layer, phase and chunk loops stay rolled: unrolled, every phase
+         * kind gets its own copy of the chunk code and the kernel outgrows the
+         * instruction caches */
+#pragma unroll 1
         for (int l = 0; l <= p.L && ok; ++l) {
             const int nph = (l < p.L) ? kPhasesPerLayer : 1;
             const float *aux = p.aux + (size_t)(l < p.L ? l : 0) * p.aux_stride;
             const uint32_t tag_base = p.epoch + (uint32_t)(l * kPhasesPerLayer);
+#pragma unroll 1
             for (int pi = 0; pi < nph && ok; ++pi) {
                 const int ph = (l < p.L) ? pi : PH_LM;
                 const int pidx = l * kPhasesPerLayer + pi;
@@ -982,6 +984,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                  * gives up (abort) skips its remaining chunks but keeps walking
                  * the schedule, so all consumer warps meet the same named
                  * barriers; the stop is taken uniformly at the next phase. */
+#pragma unroll 1
                 for (uint32_t u = g.u0; u < g.u1; u += g.upc, ++seq) {
                     if ((int)(seq % kConsumerWarps) != warp) continue;
                     if (*sm_abort_flag()) continue;
@@ -1006,7 +1009,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     float vv = 0.0f;
                     if (ph == PH_STATE && lane < (int)n) xread1(p, p.qkv + 2 * p.H + u + lane, tag_base + PH_QKVG, vv);
 
-                    if (!wait_full(p, slot, (seq / kSlots) & 1u)) continue;
+                    if (!wait_full(p, seq)) continue;
 
                     if (ph == PH_STATE) {
                         /* read pass, sequential over k for each column (lane j owns

@@ -73,15 +73,18 @@ GDN_HD float gdn_pow2f(int k) {
 #endif
 }
 
-/* exp(x); `table` = {hi[64], lo[64]} (see the header comment). */
+/* exp(x); `table` = {hi[64], lo[64]} (see the header comment). Branch-free
+ * (the special cases are selected at the end), so that independent calls
+ * interleave. The final scaling by 2^k is split into two exact power-of-two
+ * multiplies, 2^(k>>1) then 2^(k - (k>>1)): the first never leaves the normal
+ * range, so the only rounding is the second one, and only when the result is
+ * subnormal -- the single rounding ldexpf would do. */
 GDN_HD float gdn_expf(float x, const float *table) {
-    if (x != x) return x;
-    if (x > 88.72283935546875f) return INFINITY;
-    if (x < -103.97208404541015625f) return 0.0f;
-    const float n = rintf(GDN_MUL(x, GDN_EXP_INV_L));
+    const float xc = fminf(fmaxf(x, -104.0f), 89.0f); /* keeps N in int range; NaN -> -104 */
+    const float n = rintf(GDN_MUL(xc, GDN_EXP_INV_L));
     const int N = (int)n;
     /* r = x - n ln2/64 as rh + rl */
-    const float r1 = fmaf(-n, GDN_EXP_L1, x);          /* exact */
+    const float r1 = fmaf(-n, GDN_EXP_L1, xc);         /* exact */
     const float p2 = GDN_MUL(n, GDN_EXP_L2);           /* exact */
     const float rh = GDN_SUB(r1, p2);
     const float bb = GDN_SUB(rh, r1);
@@ -99,9 +102,14 @@ GDN_HD float gdn_expf(float x, const float *table) {
     const float s = GDN_ADD(th, a);
     const float s_err = GDN_SUB(a, GDN_SUB(s, th));    /* Fast2Sum, |th| >= |a| */
     const float tail = GDN_ADD(GDN_ADD(GDN_ADD(a_err, s_err), GDN_MUL(th, q)), GDN_MUL(tl, GDN_ADD(1.0f, rh)));
-    const float m = GDN_ADD(s, tail);
-    if (k >= -125 && k <= 127) return GDN_MUL(m, gdn_pow2f(k)); /* exact: m in [0.99, 1.99] */
-    return ldexpf(m, k);
+    const float m = GDN_ADD(s, tail);                  /* in [0.99, 1.99] */
+    const int k1 = k >> 1;
+    const float v = GDN_MUL(GDN_MUL(m, gdn_pow2f(k1)), gdn_pow2f(k - k1));
+    float out = v;
+    out = (x < -103.97208404541015625f) ? 0.0f : out;
+    out = (x > 88.72283935546875f) ? INFINITY : out;
+    out = (x != x) ? x : out;
+    return out;
 }
 
 #if defined(__CUDA_ARCH__)
@@ -116,14 +124,13 @@ GDN_HD float gdn_divf(float a, float b) {
 GDN_HD float gdn_divf(float a, float b) { return a / b; }
 #endif
 
-/* gdn_sigmoid (c_impl/gdn_model.cpp:1307-1316) on these primitives. */
+/* gdn_sigmoid (c_impl/gdn_model.cpp:1307-1316) on these primitives:
+ * x >= 0: 1 / (1 + exp(-x)); x < 0: exp(x) / (1 + exp(x)); both are
+ * num / (1 + z) with z = exp(-|x|), written without a branch. */
 GDN_HD float gdn_sigmoidf(float x, const float *table) {
-    if (x >= 0.0f) {
-        const float z = gdn_expf(-x, table);
-        return gdn_divf(1.0f, GDN_ADD(1.0f, z));
-    }
-    const float z = gdn_expf(x, table);
-    return gdn_divf(z, GDN_ADD(1.0f, z));
+    const bool pos = x >= 0.0f;
+    const float z = gdn_expf(pos ? -x : x, table);
+    return gdn_divf(pos ? 1.0f : z, GDN_ADD(1.0f, z));
 }
 
 #endif
