@@ -429,31 +429,35 @@ __device__ __forceinline__ void xget2(const xword *p, xword &a, xword &b) {
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-/* Warp-wide read of exchange words: lane i reads n (<= N) words at
- * src_i + j * stride (stride 1: 16-byte vector loads; src 16-byte aligned,
- * n even). Every load is issued at once, so data that is already there costs
+/* Warp-wide read of exchange words: lane word i (i < N, where use(i)) lives
+ * at addr(i) and must carry tag tagof(i). PAIRS: words 2k and 2k + 1 are
+ * adjacent and 16-byte aligned, and are fetched with one vector load. Callers
+ * lay the words out so that a warp's loads are coalesced (consecutive lanes
+ * at consecutive addresses): per-thread contiguous runs cost several times
+ * more. Every load is issued at once, so data that is already there costs
  * one round trip. While words are missing, one lane of the warp polls a
  * missing word (no flood of loads while producers are still busy), then the
- * warp re-reads everything still missing. All 32 lanes must call; lanes with
- * n == 0 take part in the protocol only. */
-template <int N>
-__device__ __forceinline__ bool xread(const DecodeParams &p, const xword *src, int stride, int n,
-                                      uint32_t tag, float (&v)[N]) {
+ * warp re-reads everything still missing. All 32 lanes must call; lanes
+ * that use no word take part in the protocol only. With PAIRS, use(2k) must
+ * equal use(2k + 1). */
+template <int N, bool PAIRS, class Addr, class TagOf, class Use>
+__device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, const TagOf &tagof, const Use &use,
+                                      float (&v)[N]) {
     const int lane = threadIdx.x & 31;
     xword w[N];
-    if (stride == 1) {
+    if (PAIRS) {
 #pragma unroll
         for (int i = 0; i < N; i += 2)
-            if (i < n) xget2(src + i, w[i], w[i + 1]);
+            if (use(i)) xget2(addr(i), w[i], w[i + 1]);
     } else {
 #pragma unroll
         for (int i = 0; i < N; ++i)
-            if (i < n) w[i] = xget(src + (size_t)i * stride);
+            if (use(i)) w[i] = xget(addr(i));
     }
     uint32_t missing = 0;
 #pragma unroll
     for (int i = 0; i < N; ++i)
-        if (i < n && xtag(w[i]) != tag) missing |= 1u << i;
+        if (use(i) && xtag(w[i]) != tagof(i)) missing |= 1u << i;
     uint64_t t0 = 0;
     while (__any_sync(0xffffffffu, missing != 0)) {
         /* the lowest lane with a missing word polls it until it lands */
@@ -462,40 +466,46 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const xword *src, i
         int ok = 1;
         if (lane == leader) {
             const int i = __ffs(missing) - 1;
-            ok = xtag(xwait(p, src + (size_t)i * stride, tag)) == tag;
+            ok = xtag(xwait(p, addr(i), tagof(i))) == tagof(i);
         }
         if (!__shfl_sync(0xffffffffu, ok, leader)) return false;
 #pragma unroll
         for (int i = 0; i < N; ++i)
-            if ((missing >> i) & 1u) w[i] = xget(src + (size_t)i * stride);
+            if ((missing >> i) & 1u) w[i] = xget(addr(i));
 #pragma unroll
         for (int i = 0; i < N; ++i)
-            if (((missing >> i) & 1u) && xtag(w[i]) == tag) missing &= ~(1u << i);
+            if (((missing >> i) & 1u) && xtag(w[i]) == tagof(i)) missing &= ~(1u << i);
         if (t0 == 0) t0 = gtimer();
         else if (gtimer() - t0 > kWaitNs) {
-            if (missing) raise_error(p, kErrExchangeTimeout, tag);
+            if (missing) raise_error(p, kErrExchangeTimeout, tagof(__ffs(missing) - 1));
             return false;
         }
     }
 #pragma unroll
     for (int i = 0; i < N; ++i)
-        if (i < n) v[i] = xval(w[i]);
+        if (use(i)) v[i] = xval(w[i]);
     return true;
 }
 
-/* Read n exchange words into the permuted shared input, with xread's
- * protocol: thread t takes the n/256 consecutive words from t * n/256 (an
- * even count, so 16-byte vector loads; n <= 5632, the workspace ABI's
- * intermediate size). All consumer threads call. */
+/* The coalesced element order of a whole-vector read: thread t's word i is
+ * element 2t + 512 (i >> 1) + (i & 1) -- word pairs, consecutive threads on
+ * consecutive pairs. n/256 words per thread for an n-element vector (n a
+ * multiple of 512). */
+__device__ __forceinline__ int vec_elem(int t, int i) { return 2 * t + 512 * (i >> 1) + (i & 1); }
+
+/* Read n exchange words (coalesced order) into the permuted shared input.
+ * n <= 5632, the workspace ABI's intermediate size. All consumer threads
+ * call. */
 constexpr int kMaxWordsPerThread = 22;
 __device__ __forceinline__ bool xread_to_xs(const DecodeParams &p, const xword *src, int n, uint32_t tag) {
     const int t = threadIdx.x;
     const int per = n >> 8;
     float v[kMaxWordsPerThread];
-    const bool ok = xread<kMaxWordsPerThread>(p, src + t * per, 1, per, tag, v);
+    const bool ok = xread<kMaxWordsPerThread, true>(
+        p, [&](int i) { return src + vec_elem(t, i); }, [&](int) { return tag; }, [&](int i) { return i < per; }, v);
 #pragma unroll
     for (int j = 0; j < kMaxWordsPerThread; ++j)
-        if (j < per) sm_xs()[xs_pos(t * per + j)] = v[j];
+        if (j < per) sm_xs()[xs_pos(vec_elem(t, j))] = v[j];
     return ok;
 }
 
@@ -658,70 +668,79 @@ __device__ __forceinline__ float seq_sum(const float *a, int n) {
 }
 
 /* Residual add + RMSNorm into the permuted shared input, in the reference's
- * order (c_impl/gdn_model.cpp:1394-1476, 3351-3452): thread t < H/16 owns the
- * 16-column half t (beat t/2, half t%2): x = round(xres + y) (or the embedding
- * for layer 0), s_t = its squares summed sequentially; the s_t are summed
- * sequentially (by lane 0 of every working warp, so no second barrier);
- * scale = 1/sqrtf(sum/H + eps); out = round((x*scale)*w). */
+ * order (c_impl/gdn_model.cpp:1394-1476, 3351-3452). Elementwise work runs in
+ * the coalesced order of vec_elem: x = round(xres + y) (or the embedding for
+ * layer 0). Thread t < H/16 then sums the squares of the 16-column half t
+ * (beat t/2, half t%2) sequentially; lane 0 of every warp sums the H/16 half
+ * sums sequentially (redundantly, so no third barrier); scale = 1/sqrtf(sum/H
+ * + eps); out = round((x*scale)*w). */
 template <int MODE>
 __device__ __forceinline__ bool prologue_norm(const DecodeParams &p, const xword *y, uint32_t tag,
-                                           const float *w, bool embed, float *hidden, int pidx) {
+                                              const float *w, bool embed, float *hidden, int pidx) {
     const int t = threadIdx.x, lane = t & 31;
     const int halves = p.H >> 4;
+    const int per = p.H >> 8; /* even, <= 8 */
     bool ok = true;
-    float x[16];
-    float wv[16];
-    if (t < halves) {
-        const float4 *w4 = reinterpret_cast<const float4 *>(w + 16 * t);
+    float x[8], wv[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 v = __ldg(w4 + q);
-            wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
-        }
-        if (embed) {
-            if (p.token_src != nullptr) {
-                const int32_t tok = *p.token_src;
-                const uint4 *e4 = reinterpret_cast<const uint4 *>(p.emb + (size_t)tok * p.H + 16 * t);
-                const uint4 e0 = __ldg(e4), e1 = __ldg(e4 + 1);
-                const uint32_t ew[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+    for (int i = 0; i < 8; ++i)
+        if (i < per) wv[i] = __ldg(w + vec_elem(t, i));
+    if (embed) {
+        if (p.token_src != nullptr) {
+            const uint32_t *e2 = reinterpret_cast<const uint32_t *>(p.emb + (size_t)(*p.token_src) * p.H);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    x[2 * i] = bnd<MODE>(bf_lo(ew[i]));
-                    x[2 * i + 1] = bnd<MODE>(bf_hi(ew[i]));
+            for (int i = 0; i < 8; i += 2) {
+                if (i < per) {
+                    const uint32_t ew = __ldg(e2 + (vec_elem(t, i) >> 1));
+                    x[i] = bnd<MODE>(bf_lo(ew));
+                    x[i + 1] = bnd<MODE>(bf_hi(ew));
                 }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) x[i] = bnd<MODE>(p.x_embed[16 * t + i]);
             }
         } else {
-            float yv[16];
-            ok = xread<16>(p, y + 16 * t, 1, 16, tag, yv);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) x[i] = bnd<MODE>(__fadd_rn(sm_xres()[16 * t + i], yv[i]));
+            for (int i = 0; i < 8; ++i)
+                if (i < per) x[i] = bnd<MODE>(p.x_embed[vec_elem(t, i)]);
         }
-        if (t == 0) trace_put(p, pidx, 1);
+    } else {
+        float yv[8];
+        ok = xread<8, true>(p, [&](int i) { return y + vec_elem(t, i); }, [&](int) { return tag; },
+                            [&](int i) { return i < per; }, yv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < per) x[i] = bnd<MODE>(__fadd_rn(sm_xres()[vec_elem(t, i)], yv[i]));
+    }
+    if (t == 0) trace_put(p, pidx, 1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if (i < per) sm_xres()[vec_elem(t, i)] = x[i];
+    named_sync(1, kConsumerThreads);
+    if (t < halves) {
+        const float4 *h4 = reinterpret_cast<const float4 *>(sm_xres() + 16 * t);
         float hs = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            hs = __fadd_rn(hs, __fmul_rn(x[i], x[i]));
-            sm_xres()[16 * t + i] = x[i];
+        for (int q = 0; q < 4; ++q) {
+            const float4 v = h4[q];
+            hs = __fadd_rn(hs, __fmul_rn(v.x, v.x));
+            hs = __fadd_rn(hs, __fmul_rn(v.y, v.y));
+            hs = __fadd_rn(hs, __fmul_rn(v.z, v.z));
+            hs = __fadd_rn(hs, __fmul_rn(v.w, v.w));
         }
         sm_red()[t] = hs;
     }
     named_sync(1, kConsumerThreads);
-    if (t < halves) {
-        float scale = 0.0f;
-        if (lane == 0) {
-            const float sum = seq_sum(sm_red(), halves);
-            scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)p.H), p.eps)));
-            if (t == 0) trace_put(p, pidx, 6);
-        }
-        scale = __shfl_sync(0xffffffffu, scale, 0);
+    float scale = 0.0f;
+    if (lane == 0) {
+        const float sum = seq_sum(sm_red(), halves);
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)p.H), p.eps)));
+        if (t == 0) trace_put(p, pidx, 6);
+    }
+    scale = __shfl_sync(0xffffffffu, scale, 0);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
+        if (i < per) {
             const float o = bnd<MODE>(__fmul_rn(__fmul_rn(x[i], scale), wv[i]));
-            sm_xs()[xs_pos(16 * t + i)] = o;
-            if (hidden != nullptr) hidden[16 * t + i] = o;
+            sm_xs()[xs_pos(vec_elem(t, i))] = o;
+            if (hidden != nullptr) hidden[vec_elem(t, i)] = o;
         }
     }
     return ok;
@@ -730,52 +749,59 @@ __device__ __forceinline__ bool prologue_norm(const DecodeParams &p, const xword
 /* Per-head RMSNorm of the attention output times swish(gate) in the
  * reference's order (c_impl/gdn_model.cpp:3226-3349): per head, 16 half sums
  * of 16 sequential squares, summed sequentially; scale = 1/sqrtf(sum/256 +
- * eps); out = round(((a*scale)*w) * g * sigmoid(g)). The elementwise tail runs
- * on all consumer threads, eight independent elements each. */
+ * eps); out = round(((a*scale)*w) * g * sigmoid(g)). Gate and attention words
+ * are read together in the coalesced order of vec_elem; every warp derives
+ * the head scales itself (lanes 0..nh-1), so three barriers suffice. */
 template <int MODE>
 __device__ __forceinline__ bool prologue_norm_gate(const DecodeParams &p, const float *o_norm,
-                                                uint32_t tag_a, uint32_t tag_b, int pidx) {
-    const int t = threadIdx.x;
-    const int halves = p.H >> 4; /* a multiple of 32, at most 128 */
-    bool ok = true;
-    float *a_sh = sm_chain(), *g_sh = sm_chain() + p.H; /* H <= 2048: both fit the 16 KB scratch */
-    if (t < 2 * halves) {
-        /* warps [0, halves/32) read the gate, the next ones the attention
-         * output, 16 words per thread, all in one round trip */
-        const bool is_attn = t >= halves;
-        const int hidx = is_attn ? t - halves : t;
-        float v[16];
-        ok = xread<16>(p, (is_attn ? p.attn : p.gate) + 16 * hidx, 1, 16, is_attn ? tag_b : tag_a, v);
-        if (t == halves) trace_put(p, pidx, 1);
-        float *dst = (is_attn ? a_sh : g_sh) + 16 * hidx;
+                                                   uint32_t tag_a, uint32_t tag_b, int pidx) {
+    const int t = threadIdx.x, lane = t & 31;
+    const int halves = p.H >> 4;
+    const int per = p.H >> 8; /* even, <= 8 */
+    float *a_sh = sm_chain();  /* H <= 2048 floats: fits the 16 KB scratch */
+    float wv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if (i < per) wv[i] = __ldg(o_norm + (vec_elem(t, i) & (kHeadDim - 1)));
+    /* words [0, per): gate; [8, 8 + per): attention output */
+    float v[16];
+    const bool ok = xread<16, true>(
+        p, [&](int i) { return i < 8 ? p.gate + vec_elem(t, i) : p.attn + vec_elem(t, i - 8); },
+        [&](int i) { return i < 8 ? tag_a : tag_b; }, [&](int i) { return (i & 7) < per; }, v);
+    if (t == 0) trace_put(p, pidx, 1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if (i < per) a_sh[vec_elem(t, i)] = v[8 + i];
+    named_sync(1, kConsumerThreads);
+    if (t < halves) {
+        const float4 *h4 = reinterpret_cast<const float4 *>(a_sh + 16 * t);
         float hs = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            hs = __fadd_rn(hs, __fmul_rn(v[i], v[i]));
-            dst[i] = v[i];
+        for (int q = 0; q < 4; ++q) {
+            const float4 a = h4[q];
+            hs = __fadd_rn(hs, __fmul_rn(a.x, a.x));
+            hs = __fadd_rn(hs, __fmul_rn(a.y, a.y));
+            hs = __fadd_rn(hs, __fmul_rn(a.z, a.z));
+            hs = __fadd_rn(hs, __fmul_rn(a.w, a.w));
         }
-        if (is_attn) sm_red()[hidx] = hs;
+        sm_red()[t] = hs;
     }
     named_sync(1, kConsumerThreads);
-    if (t < p.nh) {
+    float hscale = 0.0f;
+    if (lane < p.nh) {
         float sum = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) sum = __fadd_rn(sum, sm_red()[16 * t + j]);
-        sm_hscal()[8 + t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 256.0f), p.eps)));
-        if (t == 0) trace_put(p, pidx, 6);
+        for (int j = 0; j < 16; ++j) sum = __fadd_rn(sum, sm_red()[16 * lane + j]);
+        hscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 256.0f), p.eps)));
     }
-    named_sync(1, kConsumerThreads);
-    /* thread t takes elements t + 256 i (head i): conflict-free shared
-     * accesses and a single o_norm weight per thread */
-    const int per = p.H >> 8; /* <= 8 elements per thread */
-    const float wv = __ldg(o_norm + t);
+    if (t == 0) trace_put(p, pidx, 6);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
+        const float scale = __shfl_sync(0xffffffffu, hscale, (vec_elem(t, i) >> 8) & 31);
         if (i < per) {
-            const int e = t + (i << 8);
-            const float gv = g_sh[e];
-            const float normalized = __fmul_rn(__fmul_rn(a_sh[e], sm_hscal()[8 + i]), wv);
-            sm_xs()[xs_pos(e)] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv), sigmoid_ref(gv)));
+            const float gv = v[i];
+            const float normalized = __fmul_rn(__fmul_rn(v[8 + i], scale), wv[i]);
+            sm_xs()[xs_pos(vec_elem(t, i))] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv), sigmoid_ref(gv)));
         }
     }
     return ok;
@@ -804,8 +830,12 @@ __device__ __forceinline__ bool prologue_state(const DecodeParams &p, int l, int
         float v4[4];
         const xword *base = p.qkv + h0 * kHeadDim + t;
         float vq[2], vk[2];
-        ok = xread<2>(p, base, kHeadDim, nhl, tag, vq) && ok;
-        ok = xread<2>(p, base + p.H, kHeadDim, nhl, tag, vk) && ok;
+        ok = xread<2, false>(p, [&](int i) { return base + i * kHeadDim; }, [&](int) { return tag; },
+                             [&](int i) { return i < nhl; }, vq) &&
+             ok;
+        ok = xread<2, false>(p, [&](int i) { return base + p.H + i * kHeadDim; }, [&](int) { return tag; },
+                             [&](int i) { return i < nhl; }, vk) &&
+             ok;
         v4[0] = vq[0];
         v4[1] = vk[0];
         v4[2] = nhl > 1 ? vq[1] : 0.0f;
