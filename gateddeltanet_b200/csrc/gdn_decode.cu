@@ -161,6 +161,11 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+/* Two BF16-exact floats as one packed pair {lo, hi} (inputs of the
+ * BF16-boundary contract's mixed-precision products). */
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+}
 
 /* Shared-memory position of input column c. Columns come in groups of 512
  * = 32 halves of 16; lane l owns half l of a group and reads its 16 inputs as
@@ -493,20 +498,55 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, c
  * multiple of 512). */
 __device__ __forceinline__ int vec_elem(int t, int i) { return 2 * t + 512 * (i >> 1) + (i & 1); }
 
-/* Read n exchange words (coalesced order) into the permuted shared input.
- * n <= 5632, the workspace ABI's intermediate size. All consumer threads
- * call. */
+/* Position of the packed BF16 pair of columns c, c + 1 (c even) in the packed
+ * input: per 512-column group, uint4 j (columns 8j..8j+7 of a half) of half h
+ * at (group << 6) + 32 j + h, so lane h reads its half with two conflict-free
+ * 16-byte loads. */
+__device__ __forceinline__ int xsp_pos(int c) {
+    const int k = (c & 15) >> 1;
+    return ((c >> 9) << 8) + ((k >> 2) << 7) + (((c & 511) >> 4) << 2) + (k & 3);
+}
+
+/* Read n exchange words (coalesced order) into the shared input: FP32 in the
+ * permuted order of xs_pos, or, in the BF16-boundary contract, as packed
+ * pairs at xsp_pos. n <= 5632, the workspace ABI's intermediate size. All
+ * consumer threads call. */
 constexpr int kMaxWordsPerThread = 22;
+template <int MODE>
 __device__ __forceinline__ bool xread_to_xs(const DecodeParams &p, const xword *src, int n, uint32_t tag) {
     const int t = threadIdx.x;
     const int per = n >> 8;
     float v[kMaxWordsPerThread];
     const bool ok = xread<kMaxWordsPerThread, true>(
         p, [&](int i) { return src + vec_elem(t, i); }, [&](int) { return tag; }, [&](int i) { return i < per; }, v);
+    if (MODE == 1) {
+        uint32_t *xsp = reinterpret_cast<uint32_t *>(sm_xs());
 #pragma unroll
-    for (int j = 0; j < kMaxWordsPerThread; ++j)
-        if (j < per) sm_xs()[xs_pos(vec_elem(t, j))] = v[j];
+        for (int j = 0; j < kMaxWordsPerThread; j += 2)
+            if (j < per) xsp[xsp_pos(vec_elem(t, j))] = pack_bf16(v[j], v[j + 1]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < kMaxWordsPerThread; ++j)
+            if (j < per) sm_xs()[xs_pos(vec_elem(t, j))] = v[j];
+    }
     return ok;
+}
+
+/* Store this thread's phase-input elements (coalesced order of vec_elem,
+ * count per <= 8, even) into the shared input of the phase's GEMV. */
+template <int MODE>
+__device__ __forceinline__ void store_input(const float (&o)[8], int per) {
+    const int t = threadIdx.x;
+    if (MODE == 1) {
+        uint32_t *xsp = reinterpret_cast<uint32_t *>(sm_xs());
+#pragma unroll
+        for (int i = 0; i < 8; i += 2)
+            if (i < per) xsp[xsp_pos(vec_elem(t, i))] = pack_bf16(o[i], o[i + 1]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (i < per) sm_xs()[xs_pos(vec_elem(t, i))] = o[i];
+    }
 }
 
 /* Single-lane read of one exchange word. */
@@ -577,6 +617,35 @@ __device__ __forceinline__ float tree16_half(const uint4 &w0, const uint4 &w1, c
     return __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
 }
 
+/* w.lo * x.lo + w.hi * x.hi of packed BF16 pairs as the reference's pair sum
+ * (lo product + hi product, both exact, one rounding): mixed-precision FMA
+ * with BF16 multiplicands and FP32 addend, which multiplies exactly and rounds
+ * once; the first FMA adds -0.0 so an exact zero product keeps its sign. */
+__device__ __forceinline__ float pair_sum(uint32_t w, uint32_t x) {
+    float d;
+    asm("{\n .reg .b16 wl, wh, xl, xh;\n mov.b32 {wl, wh}, %1;\n mov.b32 {xl, xh}, %2;\n"
+        " fma.rn.f32.bf16 %0, wl, xl, 0f80000000;\n fma.rn.f32.bf16 %0, wh, xh, %0;\n}"
+        : "=f"(d)
+        : "r"(w), "r"(x));
+    return d;
+}
+
+/* tree16 of one 16-column half from packed pairs (same order as tree16_half). */
+__device__ __forceinline__ float tree16_mx(const uint4 &w0, const uint4 &w1, const uint4 &x0, const uint4 &x1) {
+    const float s0 = pair_sum(w0.x, x0.x), s1 = pair_sum(w0.y, x0.y), s2 = pair_sum(w0.z, x0.z),
+                s3 = pair_sum(w0.w, x0.w);
+    const float s4 = pair_sum(w1.x, x1.x), s5 = pair_sum(w1.y, x1.y), s6 = pair_sum(w1.z, x1.z),
+                s7 = pair_sum(w1.w, x1.w);
+    const float a0 = __fadd_rn(s0, s1), a1 = __fadd_rn(s2, s3), a2 = __fadd_rn(s4, s5), a3 = __fadd_rn(s6, s7);
+    return __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+}
+
+/* Chain scratch layout: row r, bank b holds C = K/64 positions at
+ * (4r + b) C. Position q = 8g + j (group g, lane group j) is stored at
+ * 8 (g ^ b) + j when G % 4 == 0 -- otherwise the four banks of a row would
+ * land on the same shared-memory banks; the XOR keeps every aligned run of 8
+ * positions contiguous (stage 2 reads float4). */
+
 /* Dot products of up to 4 BF16 rows (contiguous in a ring slot, columns
  * permuted per 512-column group) with the shared input, summed in the
  * reference's order (c_impl/gdn_model.cpp:4444-4586):
@@ -587,31 +656,53 @@ __device__ __forceinline__ float tree16_half(const uint4 &w0, const uint4 &w1, c
  *            row = (bank0 + bank1) + (bank2 + bank3).
  * Rows flagged in `tiny` (the a/b projections, c_impl/gdn_model.cpp:1501-1535)
  * instead take one sequential chain over all halves in column order.
+ * In the BF16-boundary contract (MODE 1) the input is BF16-exact and is
+ * kept as packed pairs (xsp_pos), and tree16_mx forms the products; in the
+ * other contracts the FP32 input is read in the order of xs_pos.
  * Every lane returns all row sums. */
 template <int MODE>
 __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, unsigned tiny, const float *xs,
-                                         float *chain, const DecodeParams &p, uint32_t refill_q,
-                                         float (&out)[4]) {
+                                         float *chain, const DecodeParams &p, uint32_t refill_q, float (&out)[4]) {
     const int lane = threadIdx.x & 31;
     const int G = K >> 9;           /* 512-column groups */
     const int C = K >> 6;           /* halves per bank of one row */
-    const int wpos = ((lane & 3) * C) + (lane >> 2);
-    const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
-    for (int g = 0; g < G; ++g) {
-        const float4 x0 = xs4[(g << 7) + lane];
-        const float4 x1 = xs4[(g << 7) + 32 + lane];
-        const float4 x2 = xs4[(g << 7) + 64 + lane];
-        const float4 x3 = xs4[(g << 7) + 96 + lane];
+    const int b_own = lane & 3;
+    /* stage-1 parking slot of group g: bank b_own, position 8g + lane/4, with
+     * the group index XOR-ed by the bank when G % 4 == 0 (chain_pos) */
+    const int sw = (G & 3) ? 0 : b_own;
+    float *park = chain + b_own * C + (lane >> 2);
+    if (MODE == 1) {
+        /* packed BF16 input in shared memory */
+        const uint4 *xsp4 = reinterpret_cast<const uint4 *>(xs);
+#pragma unroll 2
+        for (int g = 0; g < G; ++g) {
+            const uint4 x0 = xsp4[(g << 6) + lane], x1 = xsp4[(g << 6) + 32 + lane];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            if (r < nrows) {
-                const uint4 *wr = reinterpret_cast<const uint4 *>(slot + (size_t)r * K * 2) + (g << 6);
-                /* the a/b projections multiply exactly even in the c_impl
-                 * contract (c_impl/gdn_model.cpp:1517-1520) */
-                const float d = ((MODE & 2) && ((tiny >> r) & 1u))
-                                    ? tree16_half<MODE & 1>(wr[lane], wr[32 + lane], x0, x1, x2, x3)
-                                    : tree16_half<MODE>(wr[lane], wr[32 + lane], x0, x1, x2, x3);
-                chain[r * 4 * C + wpos + (g << 3)] = d;
+            for (int r = 0; r < 4; ++r) {
+                if (r < nrows) {
+                    const uint4 *wr = reinterpret_cast<const uint4 *>(slot + (size_t)r * K * 2) + (g << 6);
+                    park[r * 4 * C + ((g ^ sw) << 3)] = tree16_mx(wr[lane], wr[32 + lane], x0, x1);
+                }
+            }
+        }
+    } else {
+        const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
+        for (int g = 0; g < G; ++g) {
+            const float4 x0 = xs4[(g << 7) + lane];
+            const float4 x1 = xs4[(g << 7) + 32 + lane];
+            const float4 x2 = xs4[(g << 7) + 64 + lane];
+            const float4 x3 = xs4[(g << 7) + 96 + lane];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                if (r < nrows) {
+                    const uint4 *wr = reinterpret_cast<const uint4 *>(slot + (size_t)r * K * 2) + (g << 6);
+                    /* the a/b projections multiply exactly even in the c_impl
+                     * contract (c_impl/gdn_model.cpp:1517-1520) */
+                    const float d = ((MODE & 2) && ((tiny >> r) & 1u))
+                                        ? tree16_half<MODE & 1>(wr[lane], wr[32 + lane], x0, x1, x2, x3)
+                                        : tree16_half<MODE>(wr[lane], wr[32 + lane], x0, x1, x2, x3);
+                    park[r * 4 * C + ((g ^ sw) << 3)] = d;
+                }
             }
         }
     }
@@ -625,8 +716,9 @@ __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, 
     if (r < nrows) {
         if (!is_tiny) {
             const float *c = chain + (r * 4 + b) * C;
+            const int swb = (G & 3) ? 0 : (b << 3);
             for (int k = 0; k < C; k += 4) {
-                const float4 v = *reinterpret_cast<const float4 *>(c + k);
+                const float4 v = *reinterpret_cast<const float4 *>(c + (k ^ swb));
                 acc = __fadd_rn(acc, v.x);
                 acc = __fadd_rn(acc, v.y);
                 acc = __fadd_rn(acc, v.z);
@@ -634,11 +726,12 @@ __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, 
             }
         } else if (b == 0) {
             const float *c = chain + r * 4 * C;
+            const int sw1 = (G & 3) ? 0 : 8, sw2 = (G & 3) ? 0 : 16, sw3 = (G & 3) ? 0 : 24;
             for (int k = 0; k < C; ++k) {
                 acc = __fadd_rn(acc, c[k]);
-                acc = __fadd_rn(acc, c[C + k]);
-                acc = __fadd_rn(acc, c[2 * C + k]);
-                acc = __fadd_rn(acc, c[3 * C + k]);
+                acc = __fadd_rn(acc, c[C + (k ^ sw1)]);
+                acc = __fadd_rn(acc, c[2 * C + (k ^ sw2)]);
+                acc = __fadd_rn(acc, c[3 * C + (k ^ sw3)]);
             }
         }
     }
@@ -735,14 +828,15 @@ __device__ __forceinline__ bool prologue_norm(const DecodeParams &p, const xword
         if (t == 0) trace_put(p, pidx, 6);
     }
     scale = __shfl_sync(0xffffffffu, scale, 0);
+    float o[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         if (i < per) {
-            const float o = bnd<MODE>(__fmul_rn(__fmul_rn(x[i], scale), wv[i]));
-            sm_xs()[xs_pos(vec_elem(t, i))] = o;
-            if (hidden != nullptr) hidden[vec_elem(t, i)] = o;
+            o[i] = bnd<MODE>(__fmul_rn(__fmul_rn(x[i], scale), wv[i]));
+            if (hidden != nullptr) hidden[vec_elem(t, i)] = o[i];
         }
     }
+    store_input<MODE>(o, per);
     return ok;
 }
 
@@ -795,15 +889,17 @@ __device__ __forceinline__ bool prologue_norm_gate(const DecodeParams &p, const 
         hscale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, 256.0f), p.eps)));
     }
     if (t == 0) trace_put(p, pidx, 6);
+    float o[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float scale = __shfl_sync(0xffffffffu, hscale, (vec_elem(t, i) >> 8) & 31);
         if (i < per) {
             const float gv = v[i];
             const float normalized = __fmul_rn(__fmul_rn(v[8 + i], scale), wv[i]);
-            sm_xs()[xs_pos(vec_elem(t, i))] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv), sigmoid_ref(gv)));
+            o[i] = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv), sigmoid_ref(gv)));
         }
     }
+    store_input<MODE>(o, per);
     return ok;
 }
 
@@ -990,7 +1086,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     nw = aux + p.H + kHeadDim;
                     break;
                 case PH_DOWN:
-                    in_ok = xread_to_xs(p, p.m, p.I, tag_base + PH_GU);
+                    in_ok = xread_to_xs<MODE>(p, p.m, p.I, tag_base + PH_GU);
                     if (threadIdx.x == 0) trace_put(p, pidx, 1);
                     break;
                 default:
@@ -1008,7 +1104,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                 named_sync(1, kConsumerThreads);
                 if (*sm_decision() == 0) { ok = false; break; }
                 if (threadIdx.x == 0) trace_put(p, pidx, 2);
-
                 const uint32_t tag_out = tag_base + (uint32_t)ph;
                 /* chunks of this phase: warp w takes every 8th. A warp that
                  * gives up (abort) skips its remaining chunks but keeps walking
