@@ -334,38 +334,45 @@ __device__ __forceinline__ Geom geom(const DecodeParams &p, int l, int ph) {
     return g;
 }
 
-/* Start the bulk copy of chunk q of the CTA's schedule (each layer's phases
- * A..E, then the LM head) into ring slot q % kSlots; nothing past the end of
- * the schedule. One lane calls this, once the slot's previous chunk has been
- * read. Weights stream with L2 evict_first, the recurrent state with
- * evict_last (it is written back right after). */
-__device__ __forceinline__ void issue_chunk(const DecodeParams &p, uint32_t q) {
+/* A ring refill: chunk `idx` of layer `l` of the CTA's schedule (each layer's
+ * phases A..E, then the LM head as layer L; idx may run past the end of the
+ * layer and is carried into the next), into ring slot `slot`, whose
+ * `count`-th copy it is (1-based). */
+struct Refill {
+    uint32_t l, idx, slot, count;
+};
+
+/* Start the bulk copy of a refill; nothing past the end of the schedule. One
+ * lane calls this, once the slot's previous chunk has been read. Weights
+ * stream with L2 evict_first, the recurrent state with evict_last (it is
+ * written back right after). */
+__device__ __forceinline__ void issue_chunk(const DecodeParams &p, Refill f) {
     const uint32_t *sh = sm_shape();
     const uint32_t per_layer = sh[PH_LM * 8 + 7];
-    int l, ph;
-    uint32_t r;
-    if (q < (uint32_t)p.L * per_layer) {
-        l = (int)(q / per_layer);
-        r = q - (uint32_t)l * per_layer;
-        ph = 0;
-        while (ph < kPhasesPerLayer - 1 && r >= sh[(ph + 1) * 8 + 5]) ++ph;
-        r -= sh[ph * 8 + 5];
-    } else {
-        l = 0;
+    uint32_t l = f.l, i = f.idx;
+    while (l < (uint32_t)p.L && i >= per_layer) {
+        i -= per_layer;
+        ++l;
+    }
+    int ph;
+    if (l >= (uint32_t)p.L) {
+        if (i >= sh[PH_LM * 8 + 4]) return;
         ph = PH_LM;
-        r = q - (uint32_t)p.L * per_layer;
-        if (r >= sh[PH_LM * 8 + 4]) return;
+        l = 0;
+    } else {
+        ph = (int)(i >= sh[1 * 8 + 5]) + (int)(i >= sh[2 * 8 + 5]) + (int)(i >= sh[3 * 8 + 5]) +
+             (int)(i >= sh[4 * 8 + 5]);
+        i -= sh[ph * 8 + 5];
     }
     const uint32_t *t = sh + ph * 8;
-    const uint32_t u = t[2] + r * t[1];
+    const uint32_t u = t[2] + i * t[1];
     const uint32_t n = (t[3] - u) < t[1] ? (t[3] - u) : t[1];
     const uint32_t bytes = n * t[0];
-    const uint32_t slot = q % kSlots;
-    const uint32_t fb = smem_u32(&sm_full()[slot]);
-    atomicAdd(&sm_issued()[slot], 1u);
+    const uint32_t fb = smem_u32(&sm_full()[f.slot]);
+    *reinterpret_cast<volatile uint32_t *>(sm_issued() + f.slot) = f.count;
     mbar_expect_tx(fb, bytes);
-    bulk_g2s(smem_u32(sm_ring() + (size_t)slot * kSlotBytes), phase_src(p, l, ph) + (size_t)u * t[0], bytes, fb,
-             ph == PH_STATE ? policy_evict_last() : policy_evict_first());
+    bulk_g2s(smem_u32(sm_ring() + (size_t)f.slot * kSlotBytes), phase_src(p, (int)l, ph) + (size_t)u * t[0], bytes,
+             fb, ph == PH_STATE ? policy_evict_last() : policy_evict_first());
 }
 
 /* --------------------------------------------------- block-level helpers */
@@ -662,7 +669,7 @@ __device__ __forceinline__ float tree16_mx(const uint4 &w0, const uint4 &w1, con
  * Every lane returns all row sums. */
 template <int MODE>
 __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, unsigned tiny, const float *xs,
-                                         float *chain, const DecodeParams &p, uint32_t refill_q, float (&out)[4]) {
+                                         float *chain, const DecodeParams &p, Refill refill, float (&out)[4]) {
     const int lane = threadIdx.x & 31;
     const int G = K >> 9;           /* 512-column groups */
     const int C = K >> 6;           /* halves per bank of one row */
@@ -709,7 +716,7 @@ __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, 
     /* the weights have been read: refill the ring slot before the bank
      * chains and the epilogue */
     __syncwarp();
-    if (lane == 0) issue_chunk(p, refill_q);
+    if (lane == 0) issue_chunk(p, refill);
     const int r = lane >> 2, b = lane & 3;
     float acc = 0.0f;
     const bool is_tiny = r < nrows && ((tiny >> r) & 1u);
@@ -1013,7 +1020,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
         }
         sm_shape()[PH_LM * 8 + 5] = 0;
         sm_shape()[PH_LM * 8 + 7] = acc;
-        for (uint32_t q = 0; q < (uint32_t)kSlots; ++q) issue_chunk(p, q);
+        for (uint32_t q = 0; q < (uint32_t)kSlots; ++q) issue_chunk(p, Refill{0u, q, q, 1u});
     }
     __syncthreads();
 
@@ -1109,12 +1116,18 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                  * gives up (abort) skips its remaining chunks but keeps walking
                  * the schedule, so all consumer warps meet the same named
                  * barriers; the stop is taken uniformly at the next phase. */
+                /* chunk kk of this phase is chunk first + kk of layer l's
+                 * schedule (the LM head is layer L) */
+                const uint32_t first = (ph == PH_LM) ? 0u : sm_shape()[ph * 8 + 5];
+                uint32_t kk = 0;
 #pragma unroll 1
-                for (uint32_t u = g.u0; u < g.u1; u += g.upc, ++seq) {
+                for (uint32_t u = g.u0; u < g.u1; u += g.upc, ++seq, ++kk) {
                     if ((int)(seq % kConsumerWarps) != warp) continue;
                     if (*sm_abort_flag()) continue;
                     const uint32_t n = (g.u1 - u) < g.upc ? (g.u1 - u) : g.upc;
                     const uint32_t slot = seq % kSlots;
+                    /* the slot's next chunk, kSlots further on */
+                    const Refill refill{(uint32_t)l, first + kk + kSlots, slot, seq / kSlots + 2u};
                     const uint8_t *buf = sm_ring() + (size_t)slot * kSlotBytes;
 
                     /* per-row side inputs, fetched before waiting for the chunk */
@@ -1207,7 +1220,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                                 if (u + j >= 4u * p.H) tiny |= 1u << j;
                         }
                         warp_dot<MODE>(buf, K, (int)((ph == PH_GU) ? 2 * n : n), tiny, sm_xs(),
-                                       sm_chain() + warp * 512, p, seq + kSlots, out);
+                                       sm_chain() + warp * 512, p, refill, out);
                         float y = out[0];
                         if (lane == 1) y = out[1];
                         if (lane == 2) y = out[2];
@@ -1262,7 +1275,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                         }
                     }
                     __syncwarp();
-                    if (ph == PH_STATE && lane == 0) issue_chunk(p, seq + kSlots);
+                    if (ph == PH_STATE && lane == 0) issue_chunk(p, refill);
                 }
                 if (threadIdx.x == 0) trace_put(p, pidx, 3);
             }
