@@ -42,9 +42,8 @@ sys.path.insert(0, REPO)
 
 METRIC = "GDN-1.3B batch-1 decode ms/token (inner+outer) & % HBM roofline; streams tok/s"
 FPGA_INNER_MS = 8.141  # reference-published inner ms/token (Alveo U55C)
-SHAPE = dict(vocab=32000, hidden=2048, layers=24, heads=8, head_dim=256, inter=5632, conv=4)
-SEED = 1234
-STREAM_SEED = 99
+from gateddeltanet_b200.workload import (PROMPT_OFFSET, SEED, SHAPE, STREAM_SEED, job_tokens_per_s,  # noqa: E402
+                                         max_over_ranks, rank_streams, token_stream)
 
 
 def algorithmic_bytes_per_token(s=SHAPE) -> int:
@@ -196,7 +195,6 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
 
-    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -220,20 +218,13 @@ def main():
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     model = gdn.Model(header=gdn.make_header(**SHAPE), seed=SEED)
     rs = gdn.RunState(model)
-    # token streams: rank r decodes stream r (independent sequences)
-    sys.path.insert(0, os.path.join(REPO, "tests"))
+    # token streams: each rank decodes its own independent stream
+    stream = rank_streams(rank, world)[0]
     V = SHAPE["vocab"]
-    prompt = [tok for tok in _stream(rank, args.prompt, V, offset=1 << 20)]
-    teacher = _stream(rank, 4096, V, offset=0)
+    prompt = token_stream(stream, args.prompt, V, offset=PROMPT_OFFSET)
+    teacher = token_stream(stream, 4096, V)
     if args.prompt:
         rs.decode(prompt)
     n_w = args.warmup
@@ -246,24 +237,23 @@ def main():
     barrier()
     picks, kernel_ms = rs.decode(timed)
     barrier()
-    kernel_ms = max_over_ranks(kernel_ms)
+    kernel_ms = max_over_ranks(kernel_ms, device="cuda")
 
     # e2e through the C ABI (gdn_decode_step_host), host buffers
     e2e_n = min(args.e2e_steps, max(args.steps, 1))
     barrier()
     t0 = time.perf_counter()
-    tok = timed[0]
     for i in range(e2e_n):
         rs.step(teacher[(n_w + args.steps + i) % 4096])
     torch.cuda.synchronize()
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, device="cuda")
     barrier()
     sampler.stop()
 
     ms_per_tok = kernel_ms / args.steps
-    value = world * args.steps / (kernel_ms / 1000.0)
+    value = job_tokens_per_s(world, args.steps, kernel_ms / 1000.0)
     e2e_ms = e2e_s * 1000.0 / e2e_n
-    e2e_value = world * e2e_n / e2e_s
+    e2e_value = job_tokens_per_s(world, e2e_n, e2e_s)
     alg = algorithmic_bytes_per_token()
     peak, peak_kind = peaks()
     achieved = alg / (ms_per_tok / 1000.0) / 1e9
@@ -304,31 +294,6 @@ def main():
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     return 0
-
-
-def _stream(stream: int, n: int, vocab: int, offset: int = 0):
-    """Seeded uniform token ids (gateddeltanet_b200/csrc/gdn_synth.h, via the
-    same counter-based generator re-stated here in numpy-free Python)."""
-    key = _key(STREAM_SEED, 0x70000000 + stream)
-    out = []
-    for i in range(offset, offset + n):
-        r = _mix64((key + (i + 1) * 0x9E3779B97F4A7C15) & MASK)
-        out.append(((r >> 32) * vocab) >> 32)
-    return out
-
-
-MASK = (1 << 64) - 1
-
-
-def _mix64(z: int) -> int:
-    z = (z + 0x9E3779B97F4A7C15) & MASK
-    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & MASK
-    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & MASK
-    return z ^ (z >> 31)
-
-
-def _key(seed: int, stream: int) -> int:
-    return _mix64(seed ^ _mix64((stream * 0xD1B54A32D192ED03 + 0x1234567) & MASK))
 
 
 if __name__ == "__main__":
