@@ -107,6 +107,9 @@ EXPORTS = [
     ("gdn_b200_decode_tokens", ctypes.c_int,
      [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32,
       ctypes.c_int, ctypes.POINTER(ctypes.c_int32), _FP]),
+    ("gdn_b200_decode_tokens_noalloc", ctypes.c_int,
+     [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32,
+      ctypes.c_int, ctypes.POINTER(ctypes.c_int32), _FP]),
     ("gdn_b200_trace_step", ctypes.c_int,
      [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64),
       ctypes.c_size_t]),
@@ -228,6 +231,20 @@ class RunState:
                                               tok.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n, int(greedy),
                                               out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ctypes.byref(ms)),
               "gdn_b200_decode_tokens")
+        return out, float(ms.value)
+
+    def decode_noalloc(self, tokens: Sequence[int], greedy: bool = False):
+        """decode() through gdn_b200_decode_tokens_noalloc (no device allocation,
+        at most 4096 tokens per call)."""
+        tok = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        n = len(tok)
+        out = np.empty(n, dtype=np.int32)
+        ms = ctypes.c_float(0.0)
+        check(self.lib.gdn_b200_decode_tokens_noalloc(ctypes.byref(self.model.m), ctypes.byref(self.s),
+                                                      tok.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n,
+                                                      int(greedy), out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                                      ctypes.byref(ms)),
+              "gdn_b200_decode_tokens_noalloc")
         return out, float(ms.value)
 
     def trace(self, token: int) -> np.ndarray:

@@ -791,6 +791,73 @@ int gdn_b200_decode_tokens(const GDNModel *model, GDNRunState *state, const int3
     return 0;
 }
 
+/* ------------------------------------------- allocation-free decode loop */
+
+/* Scratch of gdn_b200_decode_tokens_noalloc: the step token ids in
+ * [0, kNoAllocMaxTokens) and the per-step argmax in [kNoAllocMaxTokens,
+ * 2 kNoAllocMaxTokens), 32 KB. A __device__ variable has one instance per
+ * device, so every device has its own copy; all run states of a device share
+ * it. Nothing in it has to start at zero: a call writes every entry it reads
+ * (the token ids by its host-to-device copy, the argmax of step i by step i)
+ * before reading it. */
+constexpr uint32_t kNoAllocMaxTokens = 4096;
+static __device__ __align__(256) int32_t g_noalloc_scratch[2 * kNoAllocMaxTokens];
+
+/* Device address of the scratch on `device`, looked up once per device with
+ * cudaGetSymbolAddress and cached; nullptr (error in *err) if unavailable. */
+static int32_t *noalloc_scratch(int device, cudaError_t *err) {
+    static std::mutex mu;
+    static int32_t *addr[256] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    *err = cudaSuccess;
+    if (device < 0 || device >= 256) {
+        *err = cudaErrorInvalidDevice;
+        return nullptr;
+    }
+    if (addr[device] == nullptr) {
+        void *p = nullptr;
+        *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (*err != cudaSuccess) return nullptr;
+        addr[device] = static_cast<int32_t *>(p);
+    }
+    return addr[device];
+}
+
+int gdn_b200_decode_tokens_noalloc(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n,
+                                   int greedy, int32_t *argmax_out, float *kernel_ms) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    if (n == 0) return 0;
+    if (n > kNoAllocMaxTokens)
+        return fail("gdn_b200_decode_tokens_noalloc: at most %u tokens per call (got %u); split the sequence",
+                    kNoAllocMaxTokens, n);
+    const uint32_t V = model->config.vocab_size;
+    for (uint32_t i = 0; i < (greedy ? 1u : n); ++i)
+        if (tokens[i] < 0 || (uint32_t)tokens[i] >= V) return fail("token id out of range");
+    CUDA_OK(cudaSetDevice(s->device));
+    cudaError_t serr = cudaSuccess;
+    int32_t *scratch = noalloc_scratch(s->device, &serr);
+    if (scratch == nullptr)
+        return fail("gdn_b200_decode_tokens_noalloc: scratch address unavailable: %s", cudaGetErrorString(serr));
+    int32_t *dtok = scratch, *dmax = scratch + kNoAllocMaxTokens;
+    CUDA_OK(cudaMemcpyAsync(dtok, tokens, (greedy ? 1u : n) * sizeof(int32_t), cudaMemcpyHostToDevice, s->stream));
+    gdn::DecodeParams p = make_params(*s);
+    CUDA_OK(cudaEventRecord(s->ev0, s->stream));
+    for (uint32_t i = 0; i < n; ++i) {
+        p.token_src = (greedy && i > 0) ? dmax + (i - 1) : dtok + i;
+        p.token_out = dmax + i;
+        if (launch(*s, p) != 0) return -1;
+    }
+    CUDA_OK(cudaEventRecord(s->ev1, s->stream));
+    if (argmax_out != nullptr)
+        CUDA_OK(cudaMemcpyAsync(argmax_out, dmax, n * sizeof(int32_t), cudaMemcpyDeviceToHost, s->stream));
+    CUDA_OK(cudaMemcpyAsync(s->ws + GDN_WS_OFF_X_NORM, s->status->token_line, 64, cudaMemcpyDeviceToHost, s->stream));
+    const int rc = sync_and_check(*s);
+    if (rc != 0) return rc;
+    if (kernel_ms != nullptr) CUDA_OK(cudaEventElapsedTime(kernel_ms, s->ev0, s->ev1));
+    return 0;
+}
+
 int gdn_b200_trace_step(const GDNModel *model, GDNRunState *state, int32_t token, uint64_t *trace_out,
                         size_t capacity) {
     Stream *s = find_stream(state);

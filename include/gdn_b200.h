@@ -75,6 +75,27 @@ int gdn_b200_fetch_outputs(GDNRunState *state, float *logits, float *final_hidde
 int gdn_b200_decode_tokens(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n,
                            int greedy, int32_t *argmax_out, float *kernel_ms);
 
+/* gdn_b200_decode_tokens without any device memory allocation: same
+ * arguments, same results. No counterpart in the reference.
+ *
+ * For callers that must not allocate device memory while they decode -- a
+ * server that has handed the rest of HBM to its own pool, or a loop that
+ * cannot afford cudaMalloc/cudaFree synchronising the device. (The plain
+ * gdn_b200_decode_tokens grows a per-run-state device buffer with cudaMalloc
+ * whenever a call is longer than any before it.) The token ids and per-step
+ * argmax live instead in a fixed 32 KB array in the library's device memory,
+ * one per device.
+ *
+ * Limits: at most 4096 tokens per call (longer calls fail with an error
+ * naming the limit; split the sequence). The first call on a device looks up
+ * the array's address (cudaGetSymbolAddress); make that first call before
+ * any stream capture begins on that device. All run states of a device share
+ * the array, so calls that overlap in time on one device -- from several
+ * threads, or on run states whose streams run concurrently -- race on it and
+ * may read each other's tokens: issue them one at a time per device. */
+int gdn_b200_decode_tokens_noalloc(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n,
+                                   int greedy, int32_t *argmax_out, float *kernel_ms);
+
 /* One decode step of `token` with the kernel's phase trace enabled: for every
  * CTA and phase (layer * 5 + {QKVG, state, O, gate/up, down}, then the LM
  * head) eight %globaltimer stamps in ns -- consumers done with the previous
