@@ -346,7 +346,19 @@ struct Refill {
  * lane calls this, once the slot's previous chunk has been read. Weights
  * stream with L2 evict_first, the recurrent state with evict_last (it is
  * written back right after). */
-__device__ __forceinline__ void issue_chunk(const DecodeParams &p, Refill f) {
+/* A resolved refill: what issue_refill copies (bytes == 0: nothing). */
+struct RefillDesc {
+    const uint8_t *src;
+    uint32_t bytes, slot, count, state;
+};
+
+/* Resolve a refill against the shape table (shared-memory reads; done before
+ * the chunk's own work so their latency overlaps it). */
+__device__ __forceinline__ RefillDesc prepare_refill(const DecodeParams &p, Refill f) {
+    RefillDesc d;
+    d.bytes = 0;
+    d.slot = f.slot;
+    d.count = f.count;
     const uint32_t *sh = sm_shape();
     const uint32_t per_layer = sh[PH_LM * 8 + 7];
     uint32_t l = f.l, i = f.idx;
@@ -356,7 +368,7 @@ __device__ __forceinline__ void issue_chunk(const DecodeParams &p, Refill f) {
     }
     int ph;
     if (l >= (uint32_t)p.L) {
-        if (i >= sh[PH_LM * 8 + 4]) return;
+        if (i >= sh[PH_LM * 8 + 4]) return d;
         ph = PH_LM;
         l = 0;
     } else {
@@ -367,13 +379,22 @@ __device__ __forceinline__ void issue_chunk(const DecodeParams &p, Refill f) {
     const uint32_t *t = sh + ph * 8;
     const uint32_t u = t[2] + i * t[1];
     const uint32_t n = (t[3] - u) < t[1] ? (t[3] - u) : t[1];
-    const uint32_t bytes = n * t[0];
-    const uint32_t fb = smem_u32(&sm_full()[f.slot]);
-    *reinterpret_cast<volatile uint32_t *>(sm_issued() + f.slot) = f.count;
-    mbar_expect_tx(fb, bytes);
-    bulk_g2s(smem_u32(sm_ring() + (size_t)f.slot * kSlotBytes), phase_src(p, (int)l, ph) + (size_t)u * t[0], bytes,
-             fb, ph == PH_STATE ? policy_evict_last() : policy_evict_first());
+    d.bytes = n * t[0];
+    d.src = phase_src(p, (int)l, ph) + (size_t)u * t[0];
+    d.state = ph == PH_STATE;
+    return d;
 }
+
+__device__ __forceinline__ void issue_refill(const RefillDesc &d) {
+    if (d.bytes == 0) return;
+    const uint32_t fb = smem_u32(&sm_full()[d.slot]);
+    *reinterpret_cast<volatile uint32_t *>(sm_issued() + d.slot) = d.count;
+    mbar_expect_tx(fb, d.bytes);
+    bulk_g2s(smem_u32(sm_ring() + (size_t)d.slot * kSlotBytes), d.src, d.bytes, fb,
+             d.state ? policy_evict_last() : policy_evict_first());
+}
+
+__device__ __forceinline__ void issue_chunk(const DecodeParams &p, Refill f) { issue_refill(prepare_refill(p, f)); }
 
 /* --------------------------------------------------- block-level helpers */
 
@@ -653,6 +674,52 @@ __device__ __forceinline__ float tree16_mx(const uint4 &w0, const uint4 &w1, con
  * land on the same shared-memory banks; the XOR keeps every aligned run of 8
  * positions contiguous (stage 2 reads float4). */
 
+/* Stage 1 for a compile-time shape (G groups, NR rows, MODE 1): every
+ * address folds to an immediate and each group's loads are issued before its
+ * products, the same arithmetic as the general loop of warp_dot. */
+template <int G, int NR>
+__device__ __forceinline__ void dot_fixed(const uint8_t *slot, const float *xs, float *chain, int lane) {
+    constexpr int K = G * 512, C = G * 8;
+    constexpr bool kSwizzle = (G % 4) == 0;
+    const int b_own = lane & 3;
+    float *park = chain + b_own * C + (lane >> 2);
+    const uint4 *xsp4 = reinterpret_cast<const uint4 *>(xs);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const uint4 x0 = xsp4[(g << 6) + lane], x1 = xsp4[(g << 6) + 32 + lane];
+        uint4 wa[NR], wb[NR];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            const uint4 *wr = reinterpret_cast<const uint4 *>(slot + (size_t)r * K * 2) + (g << 6);
+            wa[r] = wr[lane];
+            wb[r] = wr[32 + lane];
+        }
+#pragma unroll
+        for (int r = 0; r < NR; ++r)
+            park[r * 4 * C + ((kSwizzle ? (g ^ b_own) : g) << 3)] = tree16_mx(wa[r], wb[r], x0, x1);
+    }
+}
+
+/* Stage 2 for a compile-time chain length C: the bank's C partials (XOR
+ * layout of dot_fixed when C % 32 == 0) are loaded first, then summed in
+ * position order from 0.0f. */
+template <int C>
+__device__ __forceinline__ float chain_sum_fixed(const float *c, int b) {
+    const int sw = (C % 32 == 0) ? (b << 3) : 0;
+    float4 v[C / 4];
+#pragma unroll
+    for (int k = 0; k < C / 4; ++k) v[k] = *reinterpret_cast<const float4 *>(c + ((4 * k) ^ sw));
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < C / 4; ++k) {
+        acc = __fadd_rn(acc, v[k].x);
+        acc = __fadd_rn(acc, v[k].y);
+        acc = __fadd_rn(acc, v[k].z);
+        acc = __fadd_rn(acc, v[k].w);
+    }
+    return acc;
+}
+
 /* Dot products of up to 4 BF16 rows (contiguous in a ring slot, columns
  * permuted per 512-column group) with the shared input, summed in the
  * reference's order (c_impl/gdn_model.cpp:4444-4586):
@@ -669,7 +736,7 @@ __device__ __forceinline__ float tree16_mx(const uint4 &w0, const uint4 &w1, con
  * Every lane returns all row sums. */
 template <int MODE>
 __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, unsigned tiny, const float *xs,
-                                         float *chain, const DecodeParams &p, Refill refill, float (&out)[4]) {
+                                         float *chain, const RefillDesc &refill, float (&out)[4]) {
     const int lane = threadIdx.x & 31;
     const int G = K >> 9;           /* 512-column groups */
     const int C = K >> 6;           /* halves per bank of one row */
@@ -678,7 +745,11 @@ __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, 
      * the group index XOR-ed by the bank when G % 4 == 0 (chain_pos) */
     const int sw = (G & 3) ? 0 : b_own;
     float *park = chain + b_own * C + (lane >> 2);
-    if (MODE == 1) {
+    if (MODE == 1 && K == 2048 && nrows == 4 && tiny == 0) {
+        dot_fixed<4, 4>(slot, xs, chain, lane); /* the K = H = 2048 phases, full chunks */
+    } else if (MODE == 1 && K == 5632 && nrows == 1) {
+        dot_fixed<11, 1>(slot, xs, chain, lane); /* the down projection, I = 5632 */
+    } else if (MODE == 1) {
         /* packed BF16 input in shared memory */
         const uint4 *xsp4 = reinterpret_cast<const uint4 *>(xs);
 #pragma unroll 2
@@ -716,11 +787,15 @@ __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, 
     /* the weights have been read: refill the ring slot before the bank
      * chains and the epilogue */
     __syncwarp();
-    if (lane == 0) issue_chunk(p, refill);
+    if (lane == 0) issue_refill(refill);
     const int r = lane >> 2, b = lane & 3;
     float acc = 0.0f;
     const bool is_tiny = r < nrows && ((tiny >> r) & 1u);
-    if (r < nrows) {
+    if (MODE == 1 && K == 2048 && nrows == 4 && tiny == 0) {
+        if (r < 4) acc = chain_sum_fixed<32>(chain + (r * 4 + b) * 32, b);
+    } else if (MODE == 1 && K == 5632 && nrows == 1) {
+        if (r == 0) acc = chain_sum_fixed<88>(chain + b * 88, b);
+    } else if (r < nrows) {
         if (!is_tiny) {
             const float *c = chain + (r * 4 + b) * C;
             const int swb = (G & 3) ? 0 : (b << 3);
@@ -1126,8 +1201,11 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     if (*sm_abort_flag()) continue;
                     const uint32_t n = (g.u1 - u) < g.upc ? (g.u1 - u) : g.upc;
                     const uint32_t slot = seq % kSlots;
-                    /* the slot's next chunk, kSlots further on */
-                    const Refill refill{(uint32_t)l, first + kk + kSlots, slot, seq / kSlots + 2u};
+                    /* the slot's next chunk, kSlots further on (resolved by lane 0
+                     * now, issued once the slot has been read) */
+                    RefillDesc refill;
+                    refill.bytes = 0;
+                    if (lane == 0) refill = prepare_refill(p, Refill{(uint32_t)l, first + kk + kSlots, slot, seq / kSlots + 2u});
                     const uint8_t *buf = sm_ring() + (size_t)slot * kSlotBytes;
 
                     /* per-row side inputs, fetched before waiting for the chunk */
@@ -1220,7 +1298,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                                 if (u + j >= 4u * p.H) tiny |= 1u << j;
                         }
                         warp_dot<MODE>(buf, K, (int)((ph == PH_GU) ? 2 * n : n), tiny, sm_xs(),
-                                       sm_chain() + warp * 512, p, refill, out);
+                                       sm_chain() + warp * 512, refill, out);
                         float y = out[0];
                         if (lane == 1) y = out[1];
                         if (lane == 2) y = out[2];
@@ -1275,7 +1353,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                         }
                     }
                     __syncwarp();
-                    if (ph == PH_STATE && lane == 0) issue_chunk(p, refill);
+                    if (ph == PH_STATE && lane == 0) issue_refill(refill);
                 }
                 if (threadIdx.x == 0) trace_put(p, pidx, 3);
             }
