@@ -468,9 +468,9 @@ __device__ __forceinline__ void xget2(const xword *p, xword &a, xword &b) {
  * lay the words out so that a warp's loads are coalesced (consecutive lanes
  * at consecutive addresses): per-thread contiguous runs cost several times
  * more. Every load is issued at once, so data that is already there costs
- * one round trip. While words are missing, one lane of the warp polls a
- * missing word (no flood of loads while producers are still busy), then the
- * warp re-reads everything still missing. All 32 lanes must call; lanes
+ * one round trip. While words are missing, every lane re-reads its own
+ * missing words, so the read completes one round trip after the last word
+ * lands. All 32 lanes must call; lanes
  * that use no word take part in the protocol only. With PAIRS, use(2k) must
  * equal use(2k + 1). */
 template <int N, bool PAIRS, class Addr, class TagOf, class Use>
@@ -492,26 +492,32 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, c
     for (int i = 0; i < N; ++i)
         if (use(i) && xtag(w[i]) != tagof(i)) missing |= 1u << i;
     uint64_t t0 = 0;
+    uint32_t rounds = 0;
     while (__any_sync(0xffffffffu, missing != 0)) {
-        /* the lowest lane with a missing word polls it until it lands */
-        const uint32_t ballot = __ballot_sync(0xffffffffu, missing != 0);
-        const int leader = __ffs(ballot) - 1;
-        int ok = 1;
-        if (lane == leader) {
-            const int i = __ffs(missing) - 1;
-            ok = xtag(xwait(p, addr(i), tagof(i))) == tagof(i);
-        }
-        if (!__shfl_sync(0xffffffffu, ok, leader)) return false;
+        /* every lane re-reads its own missing words, so the read completes one
+         * round trip after the last word lands; the words still missing after
+         * the first read are the few of the slowest producers */
 #pragma unroll
         for (int i = 0; i < N; ++i)
             if ((missing >> i) & 1u) w[i] = xget(addr(i));
 #pragma unroll
         for (int i = 0; i < N; ++i)
             if (((missing >> i) & 1u) && xtag(w[i]) == tagof(i)) missing &= ~(1u << i);
-        if (t0 == 0) t0 = gtimer();
-        else if (gtimer() - t0 > kWaitNs) {
-            if (missing) raise_error(p, kErrExchangeTimeout, tagof(__ffs(missing) - 1));
-            return false;
+        if ((++rounds & 15u) == 0) {
+            /* lane 0 decides for the warp: abort raised elsewhere, or timeout */
+            int stop = 0;
+            if (lane == 0) {
+                if (*sm_abort_flag() != 0 || ld_volatile_i32(&p.status->err) != 0) stop = 1;
+                else if (t0 == 0) t0 = gtimer();
+                else if (gtimer() - t0 > kWaitNs) stop = 2;
+            }
+            stop = __shfl_sync(0xffffffffu, stop, 0);
+            if (stop) {
+                const uint32_t any = __ballot_sync(0xffffffffu, missing != 0);
+                if (stop == 2 && lane == __ffs(any) - 1) raise_error(p, kErrExchangeTimeout, tagof(__ffs(missing) - 1));
+                *sm_abort_flag() = 1;
+                return false;
+            }
         }
     }
 #pragma unroll
