@@ -1066,6 +1066,97 @@ __device__ __forceinline__ bool prologue_state(const DecodeParams &p, int l, int
     return ok;
 }
 
+/* Four sequential steps of the state read pass (c_impl/gdn_model.cpp:2184-2210):
+ * r += S[k][v] k_n[k], p += S[k][v] q_n[k], each product rounded, then added. */
+__device__ __forceinline__ void state_acc(float &r, float &pp, const float4 &sv, const float4 &kv, const float4 &qv) {
+    r = __fadd_rn(r, __fmul_rn(sv.x, kv.x));
+    pp = __fadd_rn(pp, __fmul_rn(sv.x, qv.x));
+    r = __fadd_rn(r, __fmul_rn(sv.y, kv.y));
+    pp = __fadd_rn(pp, __fmul_rn(sv.y, qv.y));
+    r = __fadd_rn(r, __fmul_rn(sv.z, kv.z));
+    pp = __fadd_rn(pp, __fmul_rn(sv.z, qv.z));
+    r = __fadd_rn(r, __fmul_rn(sv.w, kv.w));
+    pp = __fadd_rn(pp, __fmul_rn(sv.w, qv.w));
+}
+
+/* One chunk of the recurrence (phase B): columns u .. u + n - 1 of the layer's
+ * state in ring slot `buf`; lane j < n reads column u + j. A separate,
+ * non-inlined function: its long add chains get their own register
+ * allocation instead of competing with the GEMV path of the chunk loop. */
+template <int MODE>
+__device__ __noinline__ void state_chunk(const DecodeParams &p, const uint8_t *buf, uint32_t u, uint32_t n, int h0,
+                                         int l, float vv, uint32_t tag_out) {
+    const int lane = threadIdx.x & 31;
+    /* read pass, sequential over k for each column (lane j owns
+     * column u + j), c_impl/gdn_model.cpp:2184-2210 */
+    float r = 0.0f, pp = 0.0f;
+    if (lane < (int)n) {
+        const int hs = (int)((u + lane) >> 8) - h0;
+        const float4 *col = reinterpret_cast<const float4 *>(buf) + lane * (kHeadDim / 4);
+        const float4 *kn4 = reinterpret_cast<const float4 *>(sm_kn() + hs * kHeadDim);
+        const float4 *qn4 = reinterpret_cast<const float4 *>(sm_qn() + hs * kHeadDim);
+        /* the add chains are the critical path: loads run two
+         * batches of 2 float4 ahead (ping-pong, no register copies) */
+        float4 s0 = col[0], s1 = col[1], k0 = kn4[0], k1 = kn4[1], q0 = qn4[0], q1 = qn4[1];
+#pragma unroll 1
+        for (int k = 0; k < kHeadDim / 4; k += 4) {
+            const float4 s2 = col[k + 2], s3 = col[k + 3];
+            const float4 k2 = kn4[k + 2], k3 = kn4[k + 3], q2 = qn4[k + 2], q3 = qn4[k + 3];
+            state_acc(r, pp, s0, k0, q0);
+            state_acc(r, pp, s1, k1, q1);
+            const int kn = (k + 4 < kHeadDim / 4) ? k + 4 : 0;
+            s0 = col[kn];
+            s1 = col[kn + 1];
+            k0 = kn4[kn];
+            k1 = kn4[kn + 1];
+            q0 = qn4[kn];
+            q1 = qn4[kn + 1];
+            state_acc(r, pp, s2, k2, q2);
+            state_acc(r, pp, s3, k3, q3);
+        }
+    }
+    for (uint32_t j = 0; j < n; ++j) {
+        const uint32_t c = u + j;
+        const int hs = (int)(c >> 8) - h0;
+        const float rj = __shfl_sync(0xffffffffu, r, j);
+        const float pj = __shfl_sync(0xffffffffu, pp, j);
+        const float vj = __shfl_sync(0xffffffffu, vv, j);
+        const float alpha = sm_hscal()[hs * 4 + 0];
+        const float beta = sm_hscal()[hs * 4 + 1];
+        const float decay = sm_hscal()[hs * 4 + 2];
+        /* c_impl/gdn_model.cpp:2214-2243 */
+        const float delta = __fmul_rn(beta, __fsub_rn(vj, __fmul_rn(decay, rj)));
+        const float o =
+            __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pj), __fmul_rn(alpha, delta)));
+        if (lane == 0) xput(p.attn + c, bnd<MODE>(o), tag_out);
+        /* update, c_impl/gdn_model.cpp:2268-2300 */
+        const float *colp = reinterpret_cast<const float *>(buf) + j * kHeadDim + lane * 8;
+        const float *knp = sm_kn() + hs * kHeadDim + lane * 8;
+        const float4 s0 = *reinterpret_cast<const float4 *>(colp);
+        const float4 s1 = *reinterpret_cast<const float4 *>(colp + 4);
+        const float4 k0 = *reinterpret_cast<const float4 *>(knp);
+        const float4 k1 = *reinterpret_cast<const float4 *>(knp + 4);
+        float4 n0, n1;
+        n0.x = __fadd_rn(__fmul_rn(decay, s0.x), __fmul_rn(k0.x, delta));
+        n0.y = __fadd_rn(__fmul_rn(decay, s0.y), __fmul_rn(k0.y, delta));
+        n0.z = __fadd_rn(__fmul_rn(decay, s0.z), __fmul_rn(k0.z, delta));
+        n0.w = __fadd_rn(__fmul_rn(decay, s0.w), __fmul_rn(k0.w, delta));
+        n1.x = __fadd_rn(__fmul_rn(decay, s1.x), __fmul_rn(k1.x, delta));
+        n1.y = __fadd_rn(__fmul_rn(decay, s1.y), __fmul_rn(k1.y, delta));
+        n1.z = __fadd_rn(__fmul_rn(decay, s1.z), __fmul_rn(k1.z, delta));
+        n1.w = __fadd_rn(__fmul_rn(decay, s1.w), __fmul_rn(k1.w, delta));
+        if (p.bf16_state) {
+            n0.x = bf16_round(n0.x); n0.y = bf16_round(n0.y);
+            n0.z = bf16_round(n0.z); n0.w = bf16_round(n0.w);
+            n1.x = bf16_round(n1.x); n1.y = bf16_round(n1.y);
+            n1.z = bf16_round(n1.z); n1.w = bf16_round(n1.w);
+        }
+        float *dst = p.S + ((size_t)l * p.nh * kHeadDim + c) * kHeadDim + lane * 8;
+        __stcg(reinterpret_cast<float4 *>(dst), n0);
+        __stcg(reinterpret_cast<float4 *>(dst + 4), n1);
+    }
+}
+
 /* ------------------------------------------------------------ the kernel */
 
 template <int MODE>
@@ -1234,67 +1325,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     if (!wait_full(p, seq)) continue;
 
                     if (ph == PH_STATE) {
-                        /* read pass, sequential over k for each column (lane j owns
-                         * column u + j), c_impl/gdn_model.cpp:2184-2210 */
-                        float r = 0.0f, pp = 0.0f;
-                        if (lane < (int)n) {
-                            const int hs = (int)((u + lane) >> 8) - h0;
-                            const float4 *col = reinterpret_cast<const float4 *>(buf) + lane * (kHeadDim / 4);
-                            const float4 *kn4 = reinterpret_cast<const float4 *>(sm_kn() + hs * kHeadDim);
-                            const float4 *qn4 = reinterpret_cast<const float4 *>(sm_qn() + hs * kHeadDim);
-#pragma unroll 4
-                            for (int k = 0; k < kHeadDim / 4; ++k) {
-                                const float4 sv = col[k], kv = kn4[k], qv = qn4[k];
-                                r = __fadd_rn(r, __fmul_rn(sv.x, kv.x));
-                                pp = __fadd_rn(pp, __fmul_rn(sv.x, qv.x));
-                                r = __fadd_rn(r, __fmul_rn(sv.y, kv.y));
-                                pp = __fadd_rn(pp, __fmul_rn(sv.y, qv.y));
-                                r = __fadd_rn(r, __fmul_rn(sv.z, kv.z));
-                                pp = __fadd_rn(pp, __fmul_rn(sv.z, qv.z));
-                                r = __fadd_rn(r, __fmul_rn(sv.w, kv.w));
-                                pp = __fadd_rn(pp, __fmul_rn(sv.w, qv.w));
-                            }
-                        }
-                        for (uint32_t j = 0; j < n; ++j) {
-                            const uint32_t c = u + j;
-                            const int hs = (int)(c >> 8) - h0;
-                            const float rj = __shfl_sync(0xffffffffu, r, j);
-                            const float pj = __shfl_sync(0xffffffffu, pp, j);
-                            const float vj = __shfl_sync(0xffffffffu, vv, j);
-                            const float alpha = sm_hscal()[hs * 4 + 0];
-                            const float beta = sm_hscal()[hs * 4 + 1];
-                            const float decay = sm_hscal()[hs * 4 + 2];
-                            /* c_impl/gdn_model.cpp:2214-2243 */
-                            const float delta = __fmul_rn(beta, __fsub_rn(vj, __fmul_rn(decay, rj)));
-                            const float o =
-                                __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pj), __fmul_rn(alpha, delta)));
-                            if (lane == 0) xput(p.attn + c, bnd<MODE>(o), tag_out);
-                            /* update, c_impl/gdn_model.cpp:2268-2300 */
-                            const float *colp = reinterpret_cast<const float *>(buf) + j * kHeadDim + lane * 8;
-                            const float *knp = sm_kn() + hs * kHeadDim + lane * 8;
-                            const float4 s0 = *reinterpret_cast<const float4 *>(colp);
-                            const float4 s1 = *reinterpret_cast<const float4 *>(colp + 4);
-                            const float4 k0 = *reinterpret_cast<const float4 *>(knp);
-                            const float4 k1 = *reinterpret_cast<const float4 *>(knp + 4);
-                            float4 n0, n1;
-                            n0.x = __fadd_rn(__fmul_rn(decay, s0.x), __fmul_rn(k0.x, delta));
-                            n0.y = __fadd_rn(__fmul_rn(decay, s0.y), __fmul_rn(k0.y, delta));
-                            n0.z = __fadd_rn(__fmul_rn(decay, s0.z), __fmul_rn(k0.z, delta));
-                            n0.w = __fadd_rn(__fmul_rn(decay, s0.w), __fmul_rn(k0.w, delta));
-                            n1.x = __fadd_rn(__fmul_rn(decay, s1.x), __fmul_rn(k1.x, delta));
-                            n1.y = __fadd_rn(__fmul_rn(decay, s1.y), __fmul_rn(k1.y, delta));
-                            n1.z = __fadd_rn(__fmul_rn(decay, s1.z), __fmul_rn(k1.z, delta));
-                            n1.w = __fadd_rn(__fmul_rn(decay, s1.w), __fmul_rn(k1.w, delta));
-                            if (p.bf16_state) {
-                                n0.x = bf16_round(n0.x); n0.y = bf16_round(n0.y);
-                                n0.z = bf16_round(n0.z); n0.w = bf16_round(n0.w);
-                                n1.x = bf16_round(n1.x); n1.y = bf16_round(n1.y);
-                                n1.z = bf16_round(n1.z); n1.w = bf16_round(n1.w);
-                            }
-                            float *dst = p.S + ((size_t)l * p.nh * kHeadDim + c) * kHeadDim + lane * 8;
-                            __stcg(reinterpret_cast<float4 *>(dst), n0);
-                            __stcg(reinterpret_cast<float4 *>(dst + 4), n1);
-                        }
+                        state_chunk<MODE>(p, buf, u, n, h0, l, vv, tag_out);
                     } else {
                         const int K = (ph == PH_DOWN) ? p.I : p.H;
                         float out[4];
