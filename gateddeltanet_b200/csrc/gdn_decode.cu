@@ -40,6 +40,7 @@
 #include "gdn_math.h"
 
 #include <cuda_runtime.h>
+#include <type_traits>
 #include <stdint.h>
 
 namespace gdn {
@@ -249,17 +250,68 @@ __device__ __forceinline__ const uint8_t *phase_src(const DecodeParams &p, int l
 
 /* ------------------------------------------------------ exchange words */
 
-__device__ __forceinline__ void xput(xword *p, float v, uint32_t tag) {
-    const xword w = ((xword)tag << 32) | (xword)__float_as_uint(v);
+/* Exchange words. The BF16-boundary contracts (MODE & 1) only ever exchange
+ * BF16-exact values, so their word is 32 bits: the value's upper half and a
+ * 16-bit tag (the low half of epoch + phase; a word always holds either this
+ * launch's tag or the previous launch's, which differs by the epoch stride).
+ * The FP32 contract uses 64-bit words {FP32 value, 32-bit tag}. Either way one
+ * aligned store publishes value and tag together. The buffers are sized for
+ * 64-bit words; a 32-bit-word contract uses the first half of each. */
+template <int MODE>
+struct XW {
+    typedef unsigned long long T;
+};
+template <>
+struct XW<1> {
+    typedef uint32_t T;
+};
+template <>
+struct XW<3> {
+    typedef uint32_t T;
+};
+
+template <int MODE>
+__device__ __forceinline__ typename XW<MODE>::T *xw(xword *base) {
+    return reinterpret_cast<typename XW<MODE>::T *>(base);
+}
+template <int MODE>
+__device__ __forceinline__ const typename XW<MODE>::T *xw(const xword *base) {
+    return reinterpret_cast<const typename XW<MODE>::T *>(base);
+}
+
+__device__ __forceinline__ void xput_w(uint32_t *p, float v, uint32_t tag) {
+    const uint32_t w = (__float_as_uint(v) & 0xffff0000u) | (tag & 0xffffu);
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
+}
+__device__ __forceinline__ void xput_w(unsigned long long *p, float v, uint32_t tag) {
+    const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ xword xget(const xword *p) {
-    xword w;
+/* store element i of exchange buffer `base` */
+template <int MODE>
+__device__ __forceinline__ void xput(xword *base, size_t i, float v, uint32_t tag) {
+    xput_w(xw<MODE>(base) + i, v, tag);
+}
+__device__ __forceinline__ uint32_t xget(const uint32_t *p) {
+    uint32_t w;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ unsigned long long xget(const unsigned long long *p) {
+    unsigned long long w;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
-__device__ __forceinline__ uint32_t xtag(xword w) { return (uint32_t)(w >> 32); }
-__device__ __forceinline__ float xval(xword w) { return __uint_as_float((uint32_t)w); }
+__device__ __forceinline__ void xget2(const uint32_t *p, uint32_t &a, uint32_t &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ void xget2(const unsigned long long *p, unsigned long long &a, unsigned long long &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ bool xtag_is(uint32_t w, uint32_t tag) { return (w & 0xffffu) == (tag & 0xffffu); }
+__device__ __forceinline__ bool xtag_is(unsigned long long w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+__device__ __forceinline__ float xval(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ float xval(unsigned long long w) { return __uint_as_float((uint32_t)w); }
 
 /* ------------------------------------------------------- shared memory */
 
@@ -438,12 +490,13 @@ __device__ __forceinline__ void raise_error(const DecodeParams &p, int code, uin
 
 /* Spin on one exchange word until it carries `tag`; returns the last word
  * read, whose tag differs from `tag` on abort/timeout. */
-__device__ __noinline__ xword xwait(const DecodeParams &p, const xword *a, uint32_t tag) {
+template <class W>
+__device__ __noinline__ W xwait(const DecodeParams &p, const W *a, uint32_t tag) {
     const uint64_t t0 = gtimer();
     uint32_t spins = 0;
     while (true) {
-        const xword w = xget(a);
-        if (xtag(w) == tag) return w;
+        const W w = xget(a);
+        if (xtag_is(w, tag)) return w;
         if (*sm_abort_flag()) return w;
         if ((++spins & 63u) == 0) {
             if (ld_volatile_i32(&p.status->err) != 0) {
@@ -456,10 +509,6 @@ __device__ __noinline__ xword xwait(const DecodeParams &p, const xword *a, uint3
             }
         }
     }
-}
-
-__device__ __forceinline__ void xget2(const xword *p, xword &a, xword &b) {
-    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
 /* Warp-wide read of exchange words: lane word i (i < N, where use(i)) lives
@@ -476,8 +525,9 @@ __device__ __forceinline__ void xget2(const xword *p, xword &a, xword &b) {
 template <int N, bool PAIRS, class Addr, class TagOf, class Use>
 __device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, const TagOf &tagof, const Use &use,
                                       float (&v)[N]) {
+    typedef typename std::remove_const<typename std::remove_pointer<decltype(addr(0))>::type>::type W;
     const int lane = threadIdx.x & 31;
-    xword w[N];
+    W w[N];
     if (PAIRS) {
 #pragma unroll
         for (int i = 0; i < N; i += 2)
@@ -490,7 +540,7 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, c
     uint32_t missing = 0;
 #pragma unroll
     for (int i = 0; i < N; ++i)
-        if (use(i) && xtag(w[i]) != tagof(i)) missing |= 1u << i;
+        if (use(i) && !xtag_is(w[i], tagof(i))) missing |= 1u << i;
     uint64_t t0 = 0;
     uint32_t rounds = 0;
     while (__any_sync(0xffffffffu, missing != 0)) {
@@ -502,7 +552,7 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, c
             if ((missing >> i) & 1u) w[i] = xget(addr(i));
 #pragma unroll
         for (int i = 0; i < N; ++i)
-            if (((missing >> i) & 1u) && xtag(w[i]) == tagof(i)) missing &= ~(1u << i);
+            if (((missing >> i) & 1u) && xtag_is(w[i], tagof(i))) missing &= ~(1u << i);
         if ((++rounds & 15u) == 0) {
             /* lane 0 decides for the warp: abort raised elsewhere, or timeout */
             int stop = 0;
@@ -552,7 +602,8 @@ __device__ __forceinline__ bool xread_to_xs(const DecodeParams &p, const xword *
     const int per = n >> 8;
     float v[kMaxWordsPerThread];
     const bool ok = xread<kMaxWordsPerThread, true>(
-        p, [&](int i) { return src + vec_elem(t, i); }, [&](int) { return tag; }, [&](int i) { return i < per; }, v);
+        p, [&](int i) { return xw<MODE>(src) + vec_elem(t, i); }, [&](int) { return tag; },
+        [&](int i) { return i < per; }, v);
     if (MODE == 1) {
         uint32_t *xsp = reinterpret_cast<uint32_t *>(sm_xs());
 #pragma unroll
@@ -584,12 +635,12 @@ __device__ __forceinline__ void store_input(const float (&o)[8], int per) {
 }
 
 /* Single-lane read of one exchange word. */
-__device__ __forceinline__ bool xread1(const DecodeParams &p, const xword *src, uint32_t tag,
-                                       float &v) {
-    xword w = xget(src);
-    if (xtag(w) != tag) w = xwait(p, src, tag);
+template <class W>
+__device__ __forceinline__ bool xread1(const DecodeParams &p, const W *src, uint32_t tag, float &v) {
+    W w = xget(src);
+    if (!xtag_is(w, tag)) w = xwait(p, src, tag);
     v = xval(w);
-    return xtag(w) == tag;
+    return xtag_is(w, tag);
 }
 
 /* Wait until chunk q of the schedule sits in its ring slot; false on abort.
@@ -884,7 +935,7 @@ __device__ __forceinline__ bool prologue_norm(const DecodeParams &p, const xword
         }
     } else {
         float yv[8];
-        ok = xread<8, true>(p, [&](int i) { return y + vec_elem(t, i); }, [&](int) { return tag; },
+        ok = xread<8, true>(p, [&](int i) { return xw<MODE>(y) + vec_elem(t, i); }, [&](int) { return tag; },
                             [&](int i) { return i < per; }, yv);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -948,7 +999,7 @@ __device__ __forceinline__ bool prologue_norm_gate(const DecodeParams &p, const 
     /* words [0, per): gate; [8, 8 + per): attention output */
     float v[16];
     const bool ok = xread<16, true>(
-        p, [&](int i) { return i < 8 ? p.gate + vec_elem(t, i) : p.attn + vec_elem(t, i - 8); },
+        p, [&](int i) { return i < 8 ? xw<MODE>(p.gate) + vec_elem(t, i) : xw<MODE>(p.attn) + vec_elem(t, i - 8); },
         [&](int i) { return i < 8 ? tag_a : tag_b; }, [&](int i) { return (i & 7) < per; }, v);
     if (t == 0) trace_put(p, pidx, 1);
 #pragma unroll
@@ -994,6 +1045,7 @@ __device__ __forceinline__ bool prologue_norm_gate(const DecodeParams &p, const 
 /* q/k L2 norms (balanced tree order of gdn_tree_reduce_256), alpha, beta
  * and decay for the CTA's heads (c_impl/gdn_model.cpp:2059-2124); all reads
  * are issued before any reduction. */
+template <int MODE>
 __device__ __forceinline__ bool prologue_state(const DecodeParams &p, int l, int h0, int h1,
                                             uint32_t tag) {
     const int t = threadIdx.x;
@@ -1012,7 +1064,7 @@ __device__ __forceinline__ bool prologue_state(const DecodeParams &p, int l, int
     {
         /* words: q h0, k h0 [, q h1, k h1] at stride H between q and k */
         float v4[4];
-        const xword *base = p.qkv + h0 * kHeadDim + t;
+        const typename XW<MODE>::T *base = xw<MODE>(p.qkv) + h0 * kHeadDim + t;
         float vq[2], vk[2];
         ok = xread<2, false>(p, [&](int i) { return base + i * kHeadDim; }, [&](int) { return tag; },
                              [&](int i) { return i < nhl; }, vq) &&
@@ -1029,7 +1081,7 @@ __device__ __forceinline__ bool prologue_state(const DecodeParams &p, int l, int
     }
     if (t < 2 * nhl) {
         const int h = h0 + (t >> 1);
-        ok = xread1(p, p.ab + ((t & 1) ? p.nh + h : h), tag, (t & 1) ? bv : av) && ok;
+        ok = xread1(p, xw<MODE>(p.ab) + ((t & 1) ? p.nh + h : h), tag, (t & 1) ? bv : av) && ok;
     }
     float sq[4];
 #pragma unroll
@@ -1128,7 +1180,7 @@ __device__ __noinline__ void state_chunk(const DecodeParams &p, const uint8_t *b
         const float delta = __fmul_rn(beta, __fsub_rn(vj, __fmul_rn(decay, rj)));
         const float o =
             __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pj), __fmul_rn(alpha, delta)));
-        if (lane == 0) xput(p.attn + c, bnd<MODE>(o), tag_out);
+        if (lane == 0) xput<MODE>(p.attn, c, bnd<MODE>(o), tag_out);
         /* update, c_impl/gdn_model.cpp:2268-2300 */
         const float *colp = reinterpret_cast<const float *>(buf) + j * kHeadDim + lane * 8;
         const float *knp = sm_kn() + hs * kHeadDim + lane * 8;
@@ -1251,7 +1303,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     if (g.u1 > g.u0) {
                         h0 = (int)(g.u0 >> 8);
                         h1 = (int)((g.u1 - 1) >> 8);
-                        in_ok = prologue_state(p, l, h0, h1, tag_base + PH_QKVG);
+                        in_ok = prologue_state<MODE>(p, l, h0, h1, tag_base + PH_QKVG);
                         if (threadIdx.x == 0) trace_put(p, pidx, 1);
                     }
                     break;
@@ -1320,7 +1372,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                         }
                     }
                     float vv = 0.0f;
-                    if (ph == PH_STATE && lane < (int)n) xread1(p, p.qkv + 2 * p.H + u + lane, tag_base + PH_QKVG, vv);
+                    if (ph == PH_STATE && lane < (int)n)
+                        xread1(p, xw<MODE>(p.qkv) + 2 * p.H + u + lane, tag_base + PH_QKVG, vv);
 
                     if (!wait_full(p, seq)) continue;
 
@@ -1352,29 +1405,29 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                                         __fadd_rn(__fadd_rn(__fmul_rn(tail.x, cw.x), __fmul_rn(tail.y, cw.y)),
                                                   __fmul_rn(tail.z, cw.z)),
                                         __fmul_rn(raw, cw.w));
-                                    xput(p.qkv + r, bnd<MODE>(silu_ref(sum)), tag_out);
+                                    xput<MODE>(p.qkv, r, bnd<MODE>(silu_ref(sum)), tag_out);
                                     const uint32_t d = r - (uint32_t)row_kind * p.H;
                                     __stcg(reinterpret_cast<float4 *>(
                                                p.tails + (((size_t)l * 3 + row_kind) * p.H + d) * 4),
                                            make_float4(tail.y, tail.z, raw, 0.0f));
                                 } else if (r < 4u * p.H) {
-                                    xput(p.gate + (r - 3u * p.H), raw, tag_out);
+                                    xput<MODE>(p.gate, r - 3u * p.H, raw, tag_out);
                                 } else {
-                                    xput(p.ab + (r - 4u * p.H), raw, tag_out);
+                                    xput<MODE>(p.ab, r - 4u * p.H, raw, tag_out);
                                 }
                             }
                             break;
                         case PH_O:
-                            if (lane < (int)n) xput(p.y_o + u + lane, bnd<MODE>(y), tag_out);
+                            if (lane < (int)n) xput<MODE>(p.y_o, u + lane, bnd<MODE>(y), tag_out);
                             break;
                         case PH_DOWN:
-                            if (lane < (int)n) xput(p.y_down + u + lane, bnd<MODE>(y), tag_out);
+                            if (lane < (int)n) xput<MODE>(p.y_down, u + lane, bnd<MODE>(y), tag_out);
                             break;
                         case PH_GU: {
                             /* rows [g_u, u_u, g_u+1, u_u+1]; SwiGLU as c_impl/gdn_model.cpp:4751-4770 */
                             const float gv = bnd<MODE>(lane == 0 ? out[0] : out[2]);
                             const float uv = bnd<MODE>(lane == 0 ? out[1] : out[3]);
-                            if (lane < (int)n) xput(p.m + u + lane, bnd<MODE>(__fmul_rn(silu_ref(gv), uv)), tag_out);
+                            if (lane < (int)n) xput<MODE>(p.m, u + lane, bnd<MODE>(__fmul_rn(silu_ref(gv), uv)), tag_out);
                             break;
                         }
                         default:

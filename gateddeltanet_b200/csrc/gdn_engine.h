@@ -21,12 +21,14 @@
  *          is 1 KB contiguous, so a CTA's share of columns is one range
  *   tails  FP32 [L][3 (q,k,v)][H][4]       -- rows 0..2 of the conv window
  *          (row 2 newest) plus one pad lane, one 16-byte vector per channel
- *   exchange buffers (qkv, gate, ab, attn, y_o, m, y_down): 64-bit words
- *          {FP32 bits (low), tag (high)}. A phase's producer CTAs store each
- *          word once with a single 64-bit store; consumer CTAs poll the words
- *          until every tag equals the phase's tag (epoch + phase index), so a
- *          phase boundary costs one round trip instead of a grid barrier plus
- *          a load.
+ *   exchange buffers (qkv, gate, ab, attn, y_o, m, y_down): one word per
+ *          element carrying the value and the phase's tag (epoch + phase
+ *          index) -- 32 bits {BF16 value, 16-bit tag} in the BF16-boundary
+ *          contracts, 64 bits {FP32 value, 32-bit tag} in the FP32 one. A
+ *          phase's producer CTAs store each word once with a single store;
+ *          consumer CTAs poll the words until every tag matches, so a phase
+ *          boundary costs one round trip instead of a grid barrier plus a
+ *          load.
  */
 #ifndef GDN_ENGINE_H
 #define GDN_ENGINE_H

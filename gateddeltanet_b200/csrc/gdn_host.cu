@@ -314,6 +314,7 @@ struct Stream {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float *S = nullptr, *tails = nullptr, *acts = nullptr;
     gdn::xword *xbuf = nullptr;  /* exchange words: qkv | gate | ab | attn | y_o | m | y_down */
+    size_t xwords = 0;
     gdn::xword *qkv, *gate, *ab, *attn, *y_o, *m, *y_down;
     float *logits, *hidden, *x_embed, *cand_val;
     int32_t *cand_idx = nullptr;
@@ -643,6 +644,7 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
     const size_t t_bytes = L * 3 * H * 4 * sizeof(float);
     const size_t act_floats = V + H + H + 2 * (size_t)s->grid + 64;
     const size_t xwords = 3 * H + H + 64 + H + H + I + H;
+    s->xwords = xwords;
     if (cudaMalloc(&s->S, s_bytes) != cudaSuccess || cudaMalloc(&s->tails, t_bytes) != cudaSuccess ||
         cudaMalloc(&s->acts, act_floats * sizeof(float)) != cudaSuccess ||
         cudaMalloc(&s->xbuf, xwords * sizeof(gdn::xword)) != cudaSuccess ||
@@ -726,7 +728,16 @@ int gdn_b200_set_numerics(GDNRunState *state, int bf16_boundary, int bf16_produc
     Stream *s = find_stream(state);
     if (s == nullptr) return fail("gdn_b200: unknown run state");
     if (bf16_products && !bf16_boundary) return fail("gdn_b200: BF16-rounded products need BF16 boundaries");
-    s->bf16_boundary = bf16_boundary ? 1 : 0;
+    const int boundary = bf16_boundary ? 1 : 0;
+    if (boundary != s->bf16_boundary) {
+        /* the exchange word width follows the boundary contract (32-bit words
+         * for BF16 boundaries, 64-bit for FP32): start the buffers over with
+         * the tag no launch uses rather than reinterpret the other width */
+        CUDA_OK(cudaSetDevice(s->device));
+        CUDA_OK(cudaMemsetAsync(s->xbuf, 0xff, s->xwords * sizeof(gdn::xword), s->stream));
+        CUDA_OK(cudaStreamSynchronize(s->stream));
+    }
+    s->bf16_boundary = boundary;
     s->native_product = bf16_products ? 1 : 0;
     s->bf16_state = bf16_state ? 1 : 0;
     return 0;
