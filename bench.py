@@ -276,7 +276,7 @@ def main():
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(),
                      "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg,
-                     "kernel": "gdn_decode_kernel<true> (one launch per token)"},
+                     "kernel": "gdn_decode_kernel<1> (BF16-boundary contract; one launch per token)"},
         "gpu_launches": args.steps,
         "clocks": sampler.summary(),
     }
