@@ -182,6 +182,46 @@ def run_reference(args):
     return 0
 
 
+def run_delta_rule(args):
+    """--workload delta_rule: BASELINE config[1], the gated delta rule alone on
+    24 x 8 FP32 256x256 states (inputs as in tests/test_gpu_delta_rule.py),
+    L2 flushed before every step; value = state GB/s of one step."""
+    import numpy as np
+    import gateddeltanet_b200 as gdn
+    from gateddeltanet_b200 import build
+    build.build()
+    L = gdn.lib()
+    gdn.check(L.gdn_b200_set_device(int(os.environ.get("LOCAL_RANK", "0"))), "gdn_b200_set_device")
+    slices = SHAPE["layers"] * SHAPE["heads"]
+    rng = np.random.default_rng(SEED)
+    S = rng.normal(0, 0.1, (slices, 256, 256)).astype(np.float32)
+    q = rng.normal(0, 1, (slices, 256)).astype(np.float32)
+    k = rng.normal(0, 1, (slices, 256)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    k /= np.linalg.norm(k, axis=1, keepdims=True)
+    v = rng.normal(0, 1, (slices, 256)).astype(np.float32)
+    decay = np.exp(-np.log1p(np.exp(rng.normal(-4, 1, slices)))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.normal(0, 1, slices)))).astype(np.float32)
+    gdn.delta_rule_step(S, q, k, v, decay, beta, steps=max(args.warmup, 1))
+    _, _, ms = gdn.delta_rule_step(S, q, k, v, decay, beta, steps=args.steps)
+    state_bytes = 2 * slices * 256 * 256 * 4
+    io_bytes = slices * (3 * 256 * 4 + 256 * 4 + 8)
+    gbs = (state_bytes + io_bytes) / (ms / 1000.0) / 1e9
+    peak, peak_kind = peaks()
+    print(json.dumps({
+        "metric": "gated delta-rule step: state GB/s (BASELINE config[1])", "value": round(gbs, 1), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "BASELINE config[1]: 24 layers x 8 heads, S 256x256 fp32 N(0,0.1), q/k/v N(0,1) "
+                               "with q,k L2-normalised, decay=exp(-softplus(N(-4,1))), beta=sigmoid(N(0,1))",
+                   "l2": "flushed (256 MB write) before every step"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": state_bytes + io_bytes, "kernel": "delta_rule_kernel"},
+        "gpu_launches": args.steps}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -191,7 +231,11 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "delta_rule"],
+                    help="decode: the headline batch-1 decode (default); delta_rule: BASELINE config[1]")
     args = ap.parse_args()
+    if args.workload == "delta_rule" and args.impl == "b200":
+        return run_delta_rule(args)
     if args.impl == "reference":
         return run_reference(args)
 

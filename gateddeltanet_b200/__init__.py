@@ -113,6 +113,8 @@ EXPORTS = [
     ("gdn_b200_trace_step", ctypes.c_int,
      [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.c_int32, ctypes.POINTER(ctypes.c_uint64),
       ctypes.c_size_t]),
+    ("gdn_b200_delta_rule_step", ctypes.c_int,
+     [ctypes.c_uint32, _FP, _FP, _FP, _FP, _FP, _FP, _FP, ctypes.c_uint32, _FP]),
     ("gdn_b200_grid_size", ctypes.c_int, []),
 ]
 
@@ -296,3 +298,20 @@ class RunState:
             self.free()
         except Exception:
             pass
+
+
+def delta_rule_step(S: np.ndarray, q: np.ndarray, k: np.ndarray, v: np.ndarray, decay: np.ndarray,
+                    beta: np.ndarray, steps: int = 1):
+    """gdn_b200_delta_rule_step on host arrays: S [slices, 256, 256] (v, k),
+    q/k/v [slices, 256], decay/beta [slices], all float32. Returns
+    (S after `steps` steps, o of the last step, mean device ms per step)."""
+    L = lib()
+    S = np.ascontiguousarray(S, dtype=np.float32).copy()
+    slices = S.shape[0]
+    arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v, decay, beta)]
+    o = np.empty((slices, 256), dtype=np.float32)
+    ms = ctypes.c_float(0.0)
+    check(L.gdn_b200_delta_rule_step(slices, _fptr(S), *[_fptr(a) for a in arrs], _fptr(o), int(steps),
+                                     ctypes.byref(ms)), "gdn_b200_delta_rule_step")
+    return S, o, float(ms.value)
+

@@ -111,6 +111,21 @@ struct DecodeParams {
     unsigned long long *trace;
 };
 
+/* The isolated gated-delta-rule step (gdn_recurrence.cu): `slices` (layer,
+ * head) states S [256 (v)][256 (k)] FP32 updated in place from L2-normalised
+ * q, k and v ([slices][256] each), decay and beta ([slices]); o [slices][256]
+ * receives the unrounded outputs. status: set to 1 by a CTA whose state copy
+ * did not land within its wait limit. */
+struct DeltaRuleParams {
+    float *S;
+    const float *q, *k, *v, *decay, *beta;
+    float *o;
+    int *status;
+    uint32_t slices;
+};
+size_t delta_rule_smem_bytes();
+cudaError_t launch_delta_rule(const DeltaRuleParams &p, cudaStream_t stream);
+
 /* Tags one launch consumes; the host advances DecodeParams.epoch by this. */
 inline uint32_t epoch_stride(int L) { return (uint32_t)(L * kPhasesPerLayer + 1); }
 

@@ -869,6 +869,69 @@ int gdn_b200_decode_tokens_noalloc(const GDNModel *model, GDNRunState *state, co
     return 0;
 }
 
+int gdn_b200_delta_rule_step(uint32_t slices, float *S, const float *q, const float *k, const float *v,
+                             const float *decay, const float *beta, float *o, uint32_t steps, float *ms_per_step) {
+    if (slices == 0 || steps == 0 || S == nullptr || q == nullptr || k == nullptr || v == nullptr ||
+        decay == nullptr || beta == nullptr || o == nullptr)
+        return fail("gdn_b200_delta_rule_step: empty or missing argument");
+    CUDA_OK(cudaSetDevice(g_device));
+    const size_t s_bytes = (size_t)slices * 256 * 256 * sizeof(float), vec_bytes = (size_t)slices * 256 * sizeof(float);
+    const size_t flush_bytes = (size_t)256 << 20; /* twice the L2 */
+    float *dS = nullptr, *dvec = nullptr;
+    int *dstatus = nullptr;
+    void *dflush = nullptr;
+    cudaStream_t st = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = 0;
+    auto release = [&]() {
+        cudaFree(dS);
+        cudaFree(dvec);
+        cudaFree(dstatus);
+        cudaFree(dflush);
+        if (e0) cudaEventDestroy(e0);
+        if (e1) cudaEventDestroy(e1);
+        if (st) cudaStreamDestroy(st);
+    };
+    if (cudaMalloc(&dS, s_bytes) != cudaSuccess || cudaMalloc(&dvec, 4 * vec_bytes + 2 * slices * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&dstatus, sizeof(int)) != cudaSuccess || cudaMalloc(&dflush, flush_bytes) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess || cudaEventCreate(&e0) != cudaSuccess ||
+        cudaEventCreate(&e1) != cudaSuccess) {
+        release();
+        return fail("gdn_b200_delta_rule_step: allocation failed");
+    }
+    float *dq = dvec, *dk = dq + slices * 256, *dv = dk + slices * 256, *dout = dv + slices * 256;
+    float *ddecay = dout + slices * 256, *dbeta = ddecay + slices;
+    gdn::DeltaRuleParams prm{dS, dq, dk, dv, ddecay, dbeta, dout, dstatus, slices};
+    double total_ms = 0.0;
+    if (cudaMemcpyAsync(dS, S, s_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(dq, q, vec_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(dk, k, vec_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(dv, v, vec_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(ddecay, decay, slices * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(dbeta, beta, slices * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemsetAsync(dstatus, 0, sizeof(int), st) != cudaSuccess)
+        rc = fail("gdn_b200_delta_rule_step: upload failed");
+    for (uint32_t i = 0; rc == 0 && i < steps; ++i) {
+        float ms = 0.0f;
+        if (cudaMemsetAsync(dflush, (int)(i & 0xff), flush_bytes, st) != cudaSuccess ||
+            cudaEventRecord(e0, st) != cudaSuccess || gdn::launch_delta_rule(prm, st) != cudaSuccess ||
+            cudaEventRecord(e1, st) != cudaSuccess || cudaEventSynchronize(e1) != cudaSuccess ||
+            cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess)
+            rc = fail("gdn_b200_delta_rule_step: step %u failed: %s", i, cudaGetErrorString(cudaGetLastError()));
+        total_ms += ms;
+    }
+    int status = 0;
+    if (rc == 0 && (cudaMemcpyAsync(S, dS, s_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                    cudaMemcpyAsync(o, dout, vec_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                    cudaMemcpyAsync(&status, dstatus, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                    cudaStreamSynchronize(st) != cudaSuccess))
+        rc = fail("gdn_b200_delta_rule_step: download failed");
+    if (rc == 0 && status != 0) rc = fail("gdn_b200_delta_rule_step: a state copy did not land in time");
+    if (rc == 0 && ms_per_step != nullptr) *ms_per_step = (float)(total_ms / steps);
+    release();
+    return rc;
+}
+
 int gdn_b200_trace_step(const GDNModel *model, GDNRunState *state, int32_t token, uint64_t *trace_out,
                         size_t capacity) {
     Stream *s = find_stream(state);

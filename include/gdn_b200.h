@@ -106,6 +106,22 @@ int gdn_b200_decode_tokens_noalloc(const GDNModel *model, GDNRunState *state, co
 int gdn_b200_trace_step(const GDNModel *model, GDNRunState *state, int32_t token, uint64_t *trace_out,
                         size_t capacity);
 
+/* The gated delta rule alone (BASELINE config[1] microbench): `slices`
+ * (layer, head) recurrent states S [slices][256 (v)][256 (k)] FP32 (the
+ * engine's layout: column v of the reference's S[k][v] is contiguous) are
+ * advanced `steps` times in place from
+ * L2-normalised q and k, v ([slices][256] each), decay and beta ([slices]),
+ * as c_impl/gdn_model.cpp:2119-2300 does for one head: alpha = tree256(q.k),
+ * r and p by sequential sums over k, delta = beta (v - decay r),
+ * o = (decay p + alpha delta) / 16, S' = decay S + k delta^T (no rounding of
+ * S). o receives the last step's FP32 outputs. All buffers are host memory;
+ * the call uploads them, runs the steps (L2 flushed before each, so every
+ * step streams S from HBM) and downloads S and o. ms_per_step, if not NULL,
+ * receives the mean device time of one step (CUDA events around each kernel
+ * only). */
+int gdn_b200_delta_rule_step(uint32_t slices, float *S, const float *q, const float *k, const float *v,
+                             const float *decay, const float *beta, float *o, uint32_t steps, float *ms_per_step);
+
 /* Number of SMs (CTAs) the decode kernel uses on the current device. */
 int gdn_b200_grid_size(void);
 
