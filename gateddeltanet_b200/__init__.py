@@ -115,6 +115,7 @@ EXPORTS = [
       ctypes.c_size_t]),
     ("gdn_b200_delta_rule_step", ctypes.c_int,
      [ctypes.c_uint32, _FP, _FP, _FP, _FP, _FP, _FP, _FP, ctypes.c_uint32, _FP]),
+    ("gdn_b200_test_drop_outputs", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int, ctypes.c_int]),
     ("gdn_b200_grid_size", ctypes.c_int, []),
 ]
 

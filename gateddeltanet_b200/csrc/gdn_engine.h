@@ -109,6 +109,10 @@ struct DecodeParams {
      * chunks done (warp 0), 6 input reduction (norm sums, head scalars) done;
      * 4, 5 and 7 unused. */
     unsigned long long *trace;
+    /* test hook: CTA test_drop_cta stores none of its outputs of phase
+     * test_drop_phase (layer * 5 + {A, C, D, E}), so the consumers' bounded
+     * waits run out; -1: off */
+    int test_drop_cta, test_drop_phase;
 };
 
 /* The isolated gated-delta-rule step (gdn_recurrence.cu): `slices` (layer,

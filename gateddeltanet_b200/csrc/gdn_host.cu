@@ -323,6 +323,7 @@ struct Stream {
     int32_t *tokens = nullptr, *argmax = nullptr;
     size_t tokens_cap = 0;
     uint32_t epoch = 0;   /* exchange tag base of the next launch */
+    int test_drop_cta = -1, test_drop_phase = -1;
     float *ws = nullptr;  /* pinned ABI workspace (host) */
 };
 
@@ -378,6 +379,8 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.token_out = nullptr;
     p.status = s.status;
     p.epoch = s.epoch;
+    p.test_drop_cta = s.test_drop_cta;
+    p.test_drop_phase = s.test_drop_phase;
     return p;
 }
 
@@ -740,6 +743,17 @@ int gdn_b200_set_numerics(GDNRunState *state, int bf16_boundary, int bf16_produc
     s->bf16_boundary = boundary;
     s->native_product = bf16_products ? 1 : 0;
     s->bf16_state = bf16_state ? 1 : 0;
+    return 0;
+}
+
+int gdn_b200_test_drop_outputs(GDNRunState *state, int cta, int phase) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    if (cta >= s->grid) return fail("gdn_b200_test_drop_outputs: cta %d out of range", cta);
+    if (cta >= 0 && (phase < 0 || phase % gdn::kPhasesPerLayer == 1))
+        return fail("gdn_b200_test_drop_outputs: phase %d is not a GEMV phase (layer * 5 + {0, 2, 3, 4})", phase);
+    s->test_drop_cta = cta < 0 ? -1 : cta;
+    s->test_drop_phase = cta < 0 ? -1 : phase;
     return 0;
 }
 

@@ -122,6 +122,15 @@ int gdn_b200_trace_step(const GDNModel *model, GDNRunState *state, int32_t token
 int gdn_b200_delta_rule_step(uint32_t slices, float *S, const float *q, const float *k, const float *v,
                              const float *decay, const float *beta, float *o, uint32_t steps, float *ms_per_step);
 
+/* Test hook for the failure path (no counterpart in the reference): until
+ * called again with cta = -1, every decode step of `state` has CTA `cta`
+ * leave out its outputs of phase `phase` (layer * 5 + 0 for QKVGAB, + 2 for O,
+ * + 3 for gate/up, + 4 for down). The CTAs waiting for them give up after
+ * their wait limit (2 s), the step returns -1 with the kernel's error, and
+ * the run state stays usable (its recurrent state is then partly updated:
+ * reload it). Nothing faults or hangs on the GPU. */
+int gdn_b200_test_drop_outputs(GDNRunState *state, int cta, int phase);
+
 /* Number of SMs (CTAs) the decode kernel uses on the current device. */
 int gdn_b200_grid_size(void);
 
