@@ -1118,19 +1118,6 @@ __device__ __forceinline__ bool prologue_state(const DecodeParams &p, int l, int
     return ok;
 }
 
-/* Four sequential steps of the state read pass (c_impl/gdn_model.cpp:2184-2210):
- * r += S[k][v] k_n[k], p += S[k][v] q_n[k], each product rounded, then added. */
-__device__ __forceinline__ void state_acc(float &r, float &pp, const float4 &sv, const float4 &kv, const float4 &qv) {
-    r = __fadd_rn(r, __fmul_rn(sv.x, kv.x));
-    pp = __fadd_rn(pp, __fmul_rn(sv.x, qv.x));
-    r = __fadd_rn(r, __fmul_rn(sv.y, kv.y));
-    pp = __fadd_rn(pp, __fmul_rn(sv.y, qv.y));
-    r = __fadd_rn(r, __fmul_rn(sv.z, kv.z));
-    pp = __fadd_rn(pp, __fmul_rn(sv.z, qv.z));
-    r = __fadd_rn(r, __fmul_rn(sv.w, kv.w));
-    pp = __fadd_rn(pp, __fmul_rn(sv.w, qv.w));
-}
-
 /* One chunk of the recurrence (phase B): columns u .. u + n - 1 of the layer's
  * state in ring slot `buf`; lane j < n reads column u + j. A separate,
  * non-inlined function: its long add chains get their own register
@@ -1139,39 +1126,30 @@ template <int MODE>
 __device__ __noinline__ void state_chunk(const DecodeParams &p, const uint8_t *buf, uint32_t u, uint32_t n, int h0,
                                          int l, float vv, uint32_t tag_out) {
     const int lane = threadIdx.x & 31;
-    /* read pass, sequential over k for each column (lane j owns
-     * column u + j), c_impl/gdn_model.cpp:2184-2210 */
-    float r = 0.0f, pp = 0.0f;
-    if (lane < (int)n) {
-        const int hs = (int)((u + lane) >> 8) - h0;
-        const float4 *col = reinterpret_cast<const float4 *>(buf) + lane * (kHeadDim / 4);
-        const float4 *kn4 = reinterpret_cast<const float4 *>(sm_kn() + hs * kHeadDim);
-        const float4 *qn4 = reinterpret_cast<const float4 *>(sm_qn() + hs * kHeadDim);
-        /* the add chains are the critical path: loads run two
-         * batches of 2 float4 ahead (ping-pong, no register copies) */
-        float4 s0 = col[0], s1 = col[1], k0 = kn4[0], k1 = kn4[1], q0 = qn4[0], q1 = qn4[1];
-#pragma unroll 1
-        for (int k = 0; k < kHeadDim / 4; k += 4) {
-            const float4 s2 = col[k + 2], s3 = col[k + 3];
-            const float4 k2 = kn4[k + 2], k3 = kn4[k + 3], q2 = qn4[k + 2], q3 = qn4[k + 3];
-            state_acc(r, pp, s0, k0, q0);
-            state_acc(r, pp, s1, k1, q1);
-            const int kn = (k + 4 < kHeadDim / 4) ? k + 4 : 0;
-            s0 = col[kn];
-            s1 = col[kn + 1];
-            k0 = kn4[kn];
-            k1 = kn4[kn + 1];
-            q0 = qn4[kn];
-            q1 = qn4[kn + 1];
-            state_acc(r, pp, s2, k2, q2);
-            state_acc(r, pp, s3, k3, q3);
+    /* read pass, sequential over k for each column, c_impl/gdn_model.cpp:
+     * 2184-2210: lane j < n runs the r chain of column u + j (sum S k_n),
+     * lane 16 + j its p chain (sum S q_n) -- one chain per lane */
+    static_assert(kColsPerChunk <= 16, "a state chunk's columns map to lanes j and 16 + j");
+    float acc = 0.0f;
+    const int cj = lane & 15;
+    if (cj < (int)n) {
+        const int hs = (int)((u + cj) >> 8) - h0;
+        const float4 *col = reinterpret_cast<const float4 *>(buf) + cj * (kHeadDim / 4);
+        const float4 *vec4 = reinterpret_cast<const float4 *>((lane < 16 ? sm_kn() : sm_qn()) + hs * kHeadDim);
+#pragma unroll 8
+        for (int k = 0; k < kHeadDim / 4; ++k) {
+            const float4 sv = col[k], xv = vec4[k];
+            acc = __fadd_rn(acc, __fmul_rn(sv.x, xv.x));
+            acc = __fadd_rn(acc, __fmul_rn(sv.y, xv.y));
+            acc = __fadd_rn(acc, __fmul_rn(sv.z, xv.z));
+            acc = __fadd_rn(acc, __fmul_rn(sv.w, xv.w));
         }
     }
     for (uint32_t j = 0; j < n; ++j) {
         const uint32_t c = u + j;
         const int hs = (int)(c >> 8) - h0;
-        const float rj = __shfl_sync(0xffffffffu, r, j);
-        const float pj = __shfl_sync(0xffffffffu, pp, j);
+        const float rj = __shfl_sync(0xffffffffu, acc, j);
+        const float pj = __shfl_sync(0xffffffffu, acc, 16 + j);
         const float vj = __shfl_sync(0xffffffffu, vv, j);
         const float alpha = sm_hscal()[hs * 4 + 0];
         const float beta = sm_hscal()[hs * 4 + 1];
