@@ -222,6 +222,110 @@ def run_delta_rule(args):
     return 0
 
 
+def step_bytes_streams(b: int, s=SHAPE) -> int:
+    """HBM bytes of one multi-stream step: every weight byte once, plus per
+    stream its FP32 state read and written, conv tails, embedding row, logits."""
+    H, I, V, L, nh = s["hidden"], s["inter"], s["vocab"], s["layers"], s["heads"]
+    weights = 2 * (L * (4 * H * H + 2 * nh * H + H * H + 2 * I * H + I * H) + V * H)
+    aux = 4 * (L * (H + 256 + H + 12 * H + 2 * nh) + H)
+    per_stream = 2 * L * nh * 256 * 256 * 4 + 2 * L * 9 * H * 4 + 2 * H + 4 * V + 4
+    return weights + aux + b * per_stream
+
+
+def run_streams(args):
+    """--workload streams: BASELINE config[3], B independent streams from zero
+    state, sharded over the ranks (B / N per GPU, no collective); one step
+    advances every stream by one token (gdn_b200_batch_*)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=600))
+    if args.streams % world:
+        raise SystemExit("--streams must be a multiple of the GPU count")
+    per_rank = args.streams // world
+
+    import gateddeltanet_b200 as gdn
+    from gateddeltanet_b200 import build
+    build.build()
+    L = gdn.lib()
+    gdn.check(L.gdn_b200_set_device(local), "gdn_b200_set_device")
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    model = gdn.Model(header=gdn.make_header(**SHAPE), seed=SEED)
+    batch = gdn.Batch(model, per_rank)
+    V = SHAPE["vocab"]
+    ids = rank_streams(rank, world, per_rank)
+    n_all = args.warmup + args.steps + args.e2e_steps
+    toks = np.array([token_stream(i, n_all, V) for i in ids], dtype=np.int32).T.copy()  # [n_all, per_rank]
+    if args.warmup:
+        batch.decode(toks[:args.warmup])
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    _, dev_ms = batch.decode(toks[args.warmup:args.warmup + args.steps])
+    barrier()
+    dev_ms = max_over_ranks(dev_ms, device="cuda")
+    # e2e: host tokens in, argmax out, every step through gdn_b200_batch_step_host
+    e2e_n = max(1, min(args.e2e_steps, args.steps))
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_n):
+        batch.step(toks[args.warmup + args.steps + i % max(args.e2e_steps, 1)])
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, device="cuda")
+    barrier()
+    sampler.stop()
+    launches = batch.launches_per_step
+    ms_step = dev_ms / args.steps
+    value = args.streams * args.steps / (dev_ms / 1000.0)
+    e2e_value = args.streams * e2e_n / e2e_s
+    alg = step_bytes_streams(per_rank)
+    peak, peak_kind = peaks()
+    achieved = alg / (ms_step / 1000.0) / 1e9
+    line = {
+        "metric": "GDN-1.3B multi-stream decode tokens/s (BASELINE config[3])", "value": round(value, 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"BASELINE config[3]: {args.streams} independent GDN-1.3B streams from zero fp32 "
+                               "state, seeded uniform teacher-forced tokens per stream, sharded over the GPUs",
+                   "streams": args.streams, "streams_per_gpu": per_rank, "state": "fp32", "boundaries": "fp32",
+                   "projections": "tcgen05 tile GEMM, activations as three BF16 terms, FP32 accumulation",
+                   "l2": "no flush: 2.8 GB of weights plus the streams' state per step exceed the 126 MB L2",
+                   "parallelism": f"stream-dp{world}"},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * per_rank,
+                "d2h_bytes_per_step": 4 * per_rank + 8,
+                "api": "gdn_b200_batch_step_host (C ABI), synchronous per step"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": alg,
+                     "kernel": f"whole step ({launches} launches: tile GEMMs, recurrence, norms; one CUDA graph)"},
+        "gpu_launches": launches * args.steps,
+        "clocks": sampler.summary(),
+    }
+    batch.free()
+    model.free()
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -231,11 +335,15 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "delta_rule"],
-                    help="decode: the headline batch-1 decode (default); delta_rule: BASELINE config[1]")
+    ap.add_argument("--workload", default="decode", choices=["decode", "delta_rule", "streams"],
+                    help="decode: the headline batch-1 decode (default); delta_rule: BASELINE config[1]; "
+                         "streams: BASELINE config[3] multi-stream decode")
+    ap.add_argument("--streams", type=int, default=64, help="total streams of --workload streams")
     args = ap.parse_args()
     if args.workload == "delta_rule" and args.impl == "b200":
         return run_delta_rule(args)
+    if args.workload == "streams" and args.impl == "b200":
+        return run_streams(args)
     if args.impl == "reference":
         return run_reference(args)
 

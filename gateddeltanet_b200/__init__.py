@@ -117,6 +117,22 @@ EXPORTS = [
      [ctypes.c_uint32, _FP, _FP, _FP, _FP, _FP, _FP, _FP, ctypes.c_uint32, _FP]),
     ("gdn_b200_test_drop_outputs", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int, ctypes.c_int]),
     ("gdn_b200_grid_size", ctypes.c_int, []),
+    ("gdn_b200_batch_create", ctypes.c_void_p, [ctypes.POINTER(GDNModel), ctypes.c_uint32]),
+    ("gdn_b200_batch_free", None, [ctypes.c_void_p]),
+    ("gdn_b200_batch_launches_per_step", ctypes.c_uint32, [ctypes.c_void_p]),
+    ("gdn_b200_batch_reset", ctypes.c_int, [ctypes.c_void_p]),
+    ("gdn_b200_batch_state_upload", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_uint32, _FP, ctypes.c_size_t, _FP, ctypes.c_size_t]),
+    ("gdn_b200_batch_state_download", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_uint32, _FP, ctypes.c_size_t, _FP, ctypes.c_size_t]),
+    ("gdn_b200_batch_step_host", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32), _FP]),
+    ("gdn_b200_batch_decode_tokens", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32, ctypes.c_int,
+      ctypes.POINTER(ctypes.c_int32), _FP]),
+    ("gdn_b200_batch_fetch_logits", ctypes.c_int, [ctypes.c_void_p, _FP]),
+    ("gdn_b200_test_tile_gemm", ctypes.c_int,
+     [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, _FP, _FP, _FP]),
 ]
 
 
@@ -299,6 +315,94 @@ class RunState:
             self.free()
         except Exception:
             pass
+
+
+class Batch:
+    """Several decode streams of a Model advanced together (gdn_b200_batch_*):
+    each step reads every weight byte once for all streams; projections on
+    the tensor cores, FP32-boundary numerics."""
+
+    def __init__(self, model: Model, streams: int):
+        self.model = model
+        self.lib = model.lib
+        self.streams = int(streams)
+        self.b = self.lib.gdn_b200_batch_create(ctypes.byref(model.m), self.streams)
+        if not self.b:
+            raise RuntimeError(f"gdn_b200_batch_create failed: {last_error()}")
+        c = model.config
+        self.rec_floats = c.num_layers * c.num_heads * c.head_dim * c.head_dim
+        self.conv_floats = c.num_layers * 3 * (c.conv_size - 1) * c.hidden_size
+
+    @property
+    def launches_per_step(self) -> int:
+        return int(self.lib.gdn_b200_batch_launches_per_step(self.b))
+
+    def reset(self) -> None:
+        check(self.lib.gdn_b200_batch_reset(self.b), "gdn_b200_batch_reset")
+
+    def step(self, tokens: Sequence[int], with_logits: bool = False):
+        """One step from host memory; returns argmax [streams] (and logits [streams, vocab])."""
+        tok = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        assert tok.size == self.streams
+        am = np.empty(self.streams, dtype=np.int32)
+        lg = np.empty((self.streams, self.model.config.vocab_size), dtype=np.float32) if with_logits else None
+        check(self.lib.gdn_b200_batch_step_host(self.b, tok.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                                am.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                                _fptr(lg) if lg is not None else None), "gdn_b200_batch_step_host")
+        return (am, lg) if with_logits else am
+
+    def decode(self, tokens: np.ndarray, greedy: bool = False):
+        """tokens [n, streams] (greedy: row 0 only is read); returns (argmax [n, streams], device ms)."""
+        tok = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        n = tok.shape[0]
+        out = np.empty((n, self.streams), dtype=np.int32)
+        ms = ctypes.c_float(0.0)
+        check(self.lib.gdn_b200_batch_decode_tokens(self.b, tok.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n,
+                                                    int(greedy), out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                                    ctypes.byref(ms)), "gdn_b200_batch_decode_tokens")
+        return out, float(ms.value)
+
+    def logits(self) -> np.ndarray:
+        lg = np.empty((self.streams, self.model.config.vocab_size), dtype=np.float32)
+        check(self.lib.gdn_b200_batch_fetch_logits(self.b, _fptr(lg)), "gdn_b200_batch_fetch_logits")
+        return lg
+
+    def load_state(self, stream: int, rec: np.ndarray, conv: np.ndarray) -> None:
+        rec = np.ascontiguousarray(rec, dtype=np.float32)
+        conv = np.ascontiguousarray(conv, dtype=np.float32)
+        check(self.lib.gdn_b200_batch_state_upload(self.b, int(stream), _fptr(rec), rec.size, _fptr(conv), conv.size),
+              "gdn_b200_batch_state_upload")
+
+    def read_state(self, stream: int):
+        rec = np.empty(self.rec_floats, dtype=np.float32)
+        conv = np.empty(self.conv_floats, dtype=np.float32)
+        check(self.lib.gdn_b200_batch_state_download(self.b, int(stream), _fptr(rec), rec.size, _fptr(conv),
+                                                     conv.size), "gdn_b200_batch_state_download")
+        return rec, conv
+
+    def free(self) -> None:
+        if self.b:
+            self.lib.gdn_b200_batch_free(self.b)
+            self.b = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def tile_gemm(w: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """gdn_b200_test_tile_gemm: y [n, m] = x [n, k] . w [m, k]^T through one
+    tensor-core tile-GEMM launch (w BF16-exact float32)."""
+    L = lib()
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m, k = w.shape
+    n = x.shape[0]
+    y = np.empty((n, m), dtype=np.float32)
+    check(L.gdn_b200_test_tile_gemm(m, k, n, _fptr(w), _fptr(x), _fptr(y)), "gdn_b200_test_tile_gemm")
+    return y
 
 
 def delta_rule_step(S: np.ndarray, q: np.ndarray, k: np.ndarray, v: np.ndarray, decay: np.ndarray,

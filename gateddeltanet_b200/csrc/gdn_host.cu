@@ -445,6 +445,13 @@ uint16_t bf16_rne_bits(float v) {
 
 }  // namespace
 
+/* Shared with the multi-stream layer (gdn_batch_host.cu): one error string and
+ * one device selection per thread for the whole library. */
+namespace gdn {
+int host_fail(const char *msg) { return fail("%s", msg); }
+int host_device() { return g_device; }
+}  // namespace gdn
+
 /* ================================================================ C ABI */
 
 extern "C" {

@@ -134,6 +134,49 @@ int gdn_b200_test_drop_outputs(GDNRunState *state, int cta, int phase);
 /* Number of SMs (CTAs) the decode kernel uses on the current device. */
 int gdn_b200_grid_size(void);
 
+/* ---------------------------------------------------- multi-stream decode
+ * Several independent decode streams on one GPU (no
+ * counterpart in the reference, whose decode ABI is one stream per call):
+ * every step advances each stream by one token and reads each weight byte
+ * once for all of them. The projections run on the tensor cores (tcgen05)
+ * with FP32 accumulation, so the batch follows the FP32-boundary contract
+ * (FP32 activations and state, BF16 weights; every product exact, only the
+ * summation order differs from c_impl/gdn_model.cpp's bank chains). Streams
+ * start from zero state. The weight image (a tensor-core tile layout, 2.8 GB
+ * for GDN-1.3B) is built once per model and device and shared by batches.
+ * Functions return 0 / -1 (gdn_b200_last_error) unless stated. */
+typedef struct GdnB200Batch GdnB200Batch;
+
+/* NULL on error. streams: 1 .. 1024 (processed in passes of 128). */
+GdnB200Batch *gdn_b200_batch_create(const GDNModel *model, uint32_t streams);
+void gdn_b200_batch_free(GdnB200Batch *batch);
+/* Kernel launches in one step (the step is one CUDA graph replay). */
+uint32_t gdn_b200_batch_launches_per_step(const GdnB200Batch *batch);
+/* Zero every stream's recurrent state and conv tails. */
+int gdn_b200_batch_reset(GdnB200Batch *batch);
+/* One stream's state in the host layouts of gdn_b200_state_upload:
+ * rec [L][heads][K][V], conv tails [L][q,k,v][W-1][hidden]. */
+int gdn_b200_batch_state_upload(GdnB200Batch *batch, uint32_t stream, const float *rec, size_t rec_floats,
+                                const float *conv, size_t conv_floats);
+int gdn_b200_batch_state_download(GdnB200Batch *batch, uint32_t stream, float *rec, size_t rec_floats, float *conv,
+                                  size_t conv_floats);
+/* One step from host memory: tokens[streams] in; argmax[streams] and, if not
+ * NULL, logits[streams][vocab] (FP32) out. */
+int gdn_b200_batch_step_host(GdnB200Batch *batch, const int32_t *tokens, int32_t *argmax, float *logits);
+/* n steps with the token ids on the device: tokens[n][streams] (teacher
+ * forced), or with greedy != 0 only tokens[0][streams] and then each
+ * stream's own argmax. argmax_out[n][streams] may be NULL; device_ms, if not
+ * NULL, receives the device time of the steps (CUDA events around the graph
+ * replays). */
+int gdn_b200_batch_decode_tokens(GdnB200Batch *batch, const int32_t *tokens, uint32_t n, int greedy,
+                                 int32_t *argmax_out, float *device_ms);
+/* Logits [streams][vocab] of the last step. */
+int gdn_b200_batch_fetch_logits(GdnB200Batch *batch, float *logits);
+/* Test hook: y[n][m] = sum_k w[m][k] x[n][k] through one tensor-core tile-GEMM
+ * launch (w BF16-exact FP32 words, x FP32 entering as three BF16 terms;
+ * k a multiple of 64, n <= 128). */
+int gdn_b200_test_tile_gemm(uint32_t m, uint32_t k, uint32_t n, const float *w, const float *x, float *y);
+
 #ifdef __cplusplus
 }
 #endif
