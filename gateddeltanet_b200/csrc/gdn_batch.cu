@@ -23,14 +23,18 @@
  * tile split over several CTAs is summed by the last CTA to finish it, in
  * k order (deterministic). Warp roles: one thread streams the weight blocks
  * (16 KB bulk copies, L2 evict-first) through an 8-10 slot ring, one streams
- * the activation blocks, one issues the MMAs (three per 16-column step: one
- * per BF16 term of the activations), and four warps drain TMEM and run the
- * epilogue while the next segment accumulates. Every wait is bounded (2 s) and
+ * the activation blocks, one issues the MMAs (one per 16-column step, N =
+ * three BF16 terms x streams), and four warps drain TMEM (summing the terms)
+ * while the next segment accumulates. Every wait is bounded (2 s) and
  * reports through the status word.
  */
 #include "gdn_batch.h"
 
 #include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <utility>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -90,9 +94,6 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
-__device__ __forceinline__ void named_sync(int id, int n) {
-    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 /* AND of v over the n threads of named barrier id (every one of them gets it) */
 __device__ __forceinline__ bool named_all(int id, int n, bool v) {
     uint32_t r;
@@ -108,6 +109,13 @@ __device__ __forceinline__ bool named_all(int id, int n, bool v) {
         : "memory");
     return r != 0;
 }
+
+/* Programmatic dependent launch: every kernel of the step lets the next one
+ * start (launch_dependents) and waits for the previous one (wait) only where
+ * it first needs that kernel's results, so weight copies and state loads that
+ * depend on nothing overlap the previous kernel's tail. */
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 /* ---- tcgen05 ---- */
 
@@ -192,15 +200,6 @@ __device__ __forceinline__ void split3(float v, uint16_t &h0, uint16_t &h1, uint
     h1 = __bfloat16_as_ushort(b1);
     h2 = __bfloat16_as_ushort(b2);
 }
-__device__ __forceinline__ void put_act(uint8_t *tiles, uint32_t npad, uint32_t n, uint32_t k, float v) {
-    uint16_t h0, h1, h2;
-    split3(v, h0, h1, h2);
-    uint8_t *p = tiles + tile_off(npad, n, k);
-    const size_t term = (size_t)npad * 128u;
-    *reinterpret_cast<uint16_t *>(p) = h0;
-    *reinterpret_cast<uint16_t *>(p + term) = h1;
-    *reinterpret_cast<uint16_t *>(p + 2 * term) = h2;
-}
 /* eight consecutive k (k % 8 == 0) of stream n: one 16-byte chunk per term */
 __device__ __forceinline__ void put_act8(uint8_t *tiles, uint32_t npad, uint32_t n, uint32_t k, const float (&v)[8]) {
     uint32_t w0[4], w1[4], w2[4];
@@ -233,16 +232,6 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t row) 
     return ((unsigned long long)b << 32) | (unsigned long long)(0xFFFFFFFFu - row);
 }
 
-/* ---- unit partition of one projection ---- */
-
-__host__ __device__ __forceinline__ uint32_t unit_start(uint32_t c, uint32_t units, uint32_t grid) {
-    return (uint32_t)(((uint64_t)c * units) / grid);
-}
-/* the CTA whose range holds unit u: the largest c with unit_start(c) <= u */
-__host__ __device__ __forceinline__ uint32_t unit_owner(uint32_t u, uint32_t units, uint32_t grid) {
-    return (uint32_t)((((uint64_t)(u + 1) * grid) + units - 1) / units) - 1u;
-}
-
 /* shared-memory layout of the GEMM */
 struct GemmSmem {
     uint32_t a0, b0, bblock;                 /* ring bases (shared addresses), B block bytes */
@@ -257,61 +246,6 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
         if (mbar_try(bar, parity)) return true;
         if (*abort) return false;
         if (gtimer() - t0 > kWaitNs) return false;
-    }
-}
-
-/* The epilogue of y = D[row][n] of the pass; called by all 32 lanes of a warp
- * with the same n (rows r .. r + 31). */
-__device__ __forceinline__ void epilogue(const GemmParams &p, float y, uint32_t n, uint32_t row, bool valid) {
-    const float partner = __shfl_xor_sync(0xffffffffu, y, 1);
-    const bool live = valid && n < p.nvalid;
-    if (p.epi == kEpiLogits) {
-        unsigned long long key = live ? argmax_key(y, row) : 0ull;
-        if (live) p.out[(size_t)n * p.out_stride + row] = y;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-            key = other > key ? other : key;
-        }
-        if ((threadIdx.x & 31u) == 0 && n < p.nvalid && key != 0ull) atomicMax(p.keys + p.stream0 + n, key);
-        return;
-    }
-    if (!live) return;
-    switch (p.epi) {
-        case kEpiStore:
-            p.out[(size_t)n * p.out_stride + row] = y;
-            break;
-        case kEpiResid: {
-            float *r = p.out + (size_t)n * p.out_stride + row;
-            *r = __fadd_rn(*r, y);
-            break;
-        }
-        case kEpiQKV: {
-            const uint32_t H = p.hidden;
-            float v = y;
-            if (row < 3 * H) {
-                /* window = [t0, t1, t2, new], summed left to right (:1543-1660) */
-                const uint32_t kind = row / H, ch = row - kind * H;
-                const float4 w = reinterpret_cast<const float4 *>(p.conv_w)[(size_t)kind * H + ch];
-                float *t = p.tails + (size_t)n * p.tails_stride + (size_t)kind * 3 * H + ch;
-                const float t0 = t[0], t1 = t[H], t2 = t[2 * H];
-                float sum = __fadd_rn(__fmul_rn(t0, w.x), __fmul_rn(t1, w.y));
-                sum = __fadd_rn(sum, __fmul_rn(t2, w.z));
-                sum = __fadd_rn(sum, __fmul_rn(y, w.w));
-                v = silu_ref(sum);
-                t[0] = t1;
-                t[H] = t2;
-                t[2 * H] = y;
-            }
-            p.out[(size_t)n * p.out_stride + row] = v;
-            break;
-        }
-        case kEpiSwiGLU:
-            /* row 2i = gate_i, row 2i + 1 = up_i (:4751-4770) */
-            if ((row & 1u) == 0) put_act(p.next_b, p.npad, n, row >> 1, __fmul_rn(silu_ref(y), partner));
-            break;
-        default:
-            break;
     }
 }
 
@@ -340,12 +274,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tile_gemm_kernel(const __grid
     s.flag = reinterpret_cast<uint32_t *>(tail + 8);
     volatile uint32_t *abort = s.abort;
 
+    pdl_trigger();
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t units = p.mtiles * p.kblocks, G = gridDim.x, c = blockIdx.x;
     const uint32_t u0 = unit_start(c, units, G), u1 = unit_start(c + 1, units, G);
     const uint32_t KB = p.kblocks;
-    uint32_t acc_cols = 32;  /* a power of two >= npad: both buffers start aligned */
-    while (acc_cols < p.npad) acc_cols <<= 1;
+    /* TMEM: one accumulator holds the three term columns of every stream
+     * (3 * npad <= 240 columns); two of them, a power of two apart, so the
+     * next segment accumulates while the epilogue drains the last one */
+    uint32_t acc_cols = 32;
+    while (acc_cols < kTerms * p.npad) acc_cols <<= 1;
     const uint32_t ncols = 2 * acc_cols;
 
     if (tid == 0) {
@@ -401,8 +339,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tile_gemm_kernel(const __grid
             }
         }
     } else if (warp == 5) {
-        /* activation blocks: k-block u % KB of the pass's tiles */
+        /* activation blocks: k-block u % KB of the pass's tiles, written by
+         * the previous kernel */
         if (lane == 0) {
+            pdl_wait();
             const uint64_t pol = policy_evict_last();
             uint32_t i = 0;
             for (uint32_t u = u0; u < u1; ++u, ++i) {
@@ -424,8 +364,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tile_gemm_kernel(const __grid
         }
     } else if (warp == 6) {
         if (lane == 0) {
-            const uint32_t idesc = instr_desc(kTileM, p.npad);
-            const uint32_t term_bytes = p.npad * 128u;
+            /* N = 3 * npad: the three BF16 terms of the activations are 3 * npad
+             * consecutive rows of the activation block, so one MMA per 16
+             * columns covers them all and reads the weight tile once */
+            const uint32_t idesc = instr_desc(kTileM, kTerms * p.npad);
             uint32_t i = 0, seg = 0;
             bool ok = true;
             for (uint32_t t = u0 / KB; ok && t * KB < u1; ++t, ++seg) {
@@ -450,14 +392,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tile_gemm_kernel(const __grid
                     tc_fence_after();
                     const uint32_t abase = s.a0 + sa * kABlockBytes, bbase = s.b0 + sb * s.bblock;
 #pragma unroll
-                    for (uint32_t term = 0; term < kTerms; ++term) {
-#pragma unroll
-                        for (uint32_t kk = 0; kk < kTileK / 16; ++kk) {
-                            const uint64_t ad = smem_desc(abase + kk * 32u);
-                            const uint64_t bd = smem_desc(bbase + term * term_bytes + kk * 32u);
-                            tc_mma(d, ad, bd, idesc, (u == ua && term == 0 && kk == 0) ? 0u : 1u);
-                        }
-                    }
+                    for (uint32_t kk = 0; kk < kTileK / 16; ++kk)
+                        tc_mma(d, smem_desc(abase + kk * 32u), smem_desc(bbase + kk * 32u), idesc,
+                               (u == ua && kk == 0) ? 0u : 1u);
                     tc_commit(s.empty_a + 8 * sa);
                     tc_commit(s.empty_b + 8 * sb);
                 }
@@ -470,15 +407,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tile_gemm_kernel(const __grid
             }
         }
     } else {
-        /* warps 0-3: TMEM lanes 32w .. 32w + 31 = rows of the tile */
+        /* warps 0-3: TMEM lanes 32w .. 32w + 31 = rows of the tile; each
+         * segment's accumulator goes to its partial slot (the projection's
+         * consumer sums the slots of a tile) */
         const uint32_t r = tid;  /* 0..127 */
+        pdl_wait();  /* the partial slots may still be read by the previous kernel */
         uint32_t seg = 0;
         for (uint32_t t = u0 / KB; t * KB < u1; ++t, ++seg) {
-            const uint32_t ua = max(u0, t * KB), ub = min(u1, (t + 1) * KB);
             const uint32_t acc = seg & 1u;
-            const bool whole = (ua == t * KB) && (ub == (t + 1) * KB);
-            const uint32_t row = t * kTileM + r;
-            const bool valid = row < p.m;
             /* the 128 epilogue threads leave together or not at all */
             const bool got = wait_bar(s.acc_full + 8 * acc, (seg >> 1) & 1u, abort);
             if (!named_all(1, 128, got)) {
@@ -488,46 +424,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tile_gemm_kernel(const __grid
             }
             tc_fence_after();
             const uint32_t taddr = tmem + acc * acc_cols + ((warp * 32u) << 16);
-            const uint32_t local = t - u0 / KB;
-            float *slot = p.partial + ((size_t)c * p.max_local + local) * p.npad * kTileM;
+            float *slot = p.partial + ((size_t)c * p.max_local + (t - u0 / KB)) * p.npad * kTileM + r;
             for (uint32_t c0 = 0; c0 < p.npad; c0 += 16) {
-                float v[16];
-                tc_ld16(taddr + c0, v);
-                if (whole) {
+                float v0[16], v1[16], v2[16];
+                tc_ld16(taddr + c0, v0);
+                tc_ld16(taddr + p.npad + c0, v1);
+                tc_ld16(taddr + 2 * p.npad + c0, v2);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) epilogue(p, v[j], c0 + j, row, valid);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) slot[(size_t)(c0 + j) * kTileM + r] = v[j];
-                }
+                for (int j = 0; j < 16; ++j)
+                    __stcg(slot + (size_t)(c0 + j) * kTileM, __fadd_rn(v0[j], __fadd_rn(v1[j], v2[j])));
             }
             tc_fence_before();
             mbar_arrive(s.acc_empty + 8 * acc);
-            if (whole) continue;
-            /* split tile: the last of its CTAs sums the segments in k order */
-            __threadfence();
-            named_sync(1, 128);
-            if (r == 0) {
-                const uint32_t cf = unit_owner(t * KB, units, G), cl = unit_owner(t * KB + KB - 1, units, G);
-                const uint32_t prev = atomicAdd(p.counters + t, 1u);
-                *s.flag = (prev + 1 == cl - cf + 1) ? 1u : 0u;
-            }
-            named_sync(1, 128);
-            if (*s.flag) {
-                __threadfence();
-                const uint32_t cf = unit_owner(t * KB, units, G), cl = unit_owner(t * KB + KB - 1, units, G);
-                for (uint32_t n = 0; n < p.npad; ++n) {
-                    float y = 0.0f;
-                    for (uint32_t cc = cf; cc <= cl; ++cc) {
-                        const uint32_t lc = t - unit_start(cc, units, G) / KB;
-                        const float *sl = p.partial + ((size_t)cc * p.max_local + lc) * p.npad * kTileM;
-                        y = (cc == cf) ? __ldcg(sl + (size_t)n * kTileM + r) : __fadd_rn(y, __ldcg(sl + (size_t)n * kTileM + r));
-                    }
-                    epilogue(p, y, n, row, valid);
-                }
-                if (r == 0) p.counters[t] = 0;
-            }
-            named_sync(1, 128);
         }
     }
     tc_fence_before();
@@ -549,42 +457,95 @@ __device__ __forceinline__ uint8_t *pass_tiles(const TileOut &o, uint32_t s, uin
     return o.base + (size_t)pass * o.pass_stride;
 }
 
+/* Rows row0 .. row0 + 7 (row0 % 8 == 0) of stream s of a projection: the sum
+ * of the tile's partial slots in k order. The loads of up to four segments
+ * are in flight together. */
+__device__ __forceinline__ void psum8(const Partials &v, uint32_t s, uint32_t row0, float (&out)[8]) {
+    const uint32_t pass = s / kMaxPassStreams, n = s - pass * kMaxPassStreams;
+    const uint32_t npad = (pass + 1 == v.passes) ? v.npad_last : (uint32_t)kMaxPassStreams;
+    const uint32_t KB = v.kblocks, t = row0 / kTileM, r = row0 - t * kTileM;
+    const uint32_t cf = unit_owner(t * KB, v.units, v.grid), cl = unit_owner(t * KB + KB - 1, v.units, v.grid);
+    const uint32_t ns = cl - cf + 1;
+    const float *base = v.base + pass * v.pass_stride + (size_t)n * kTileM + r;
+    const size_t slot = (size_t)npad * kTileM;
+    for (uint32_t k0 = 0; k0 < ns; k0 += 4) {
+        float4 x[4][2];
+#pragma unroll
+        for (uint32_t k = 0; k < 4; ++k) {
+            if (k0 + k < ns) {
+                const uint32_t cc = cf + k0 + k;
+                const uint32_t lc = t - unit_start(cc, v.units, v.grid) / KB;
+                const float4 *q = reinterpret_cast<const float4 *>(base + ((size_t)cc * v.max_local + lc) * slot);
+                x[k][0] = __ldcg(q);
+                x[k][1] = __ldcg(q + 1);
+            }
+        }
+#pragma unroll
+        for (uint32_t k = 0; k < 4; ++k) {
+            if (k0 + k < ns) {
+                const float e[8] = {x[k][0].x, x[k][0].y, x[k][0].z, x[k][0].w,
+                                    x[k][1].x, x[k][1].y, x[k][1].z, x[k][1].w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) out[i] = (k0 + k == 0) ? e[i] : __fadd_rn(out[i], e[i]);
+            }
+        }
+    }
+}
+
 /* RMSNorm of the residual of stream blockIdx.x (c_impl/gdn_model.cpp:1394-1476):
- * per 16-element half a sequential sum of squares, the halves summed in
- * order; scale = 1/sqrtf(sum/H + eps); out = (x * scale) * w, written as the
- * activation tiles of the next projection. At layer 0 the residual is first
- * loaded with the token's embedding row (:3719-3731). */
-__global__ void __launch_bounds__(256) input_kernel(const StepParams p, const float *__restrict__ norm_w, int embed,
-                                                    TileOut out) {
-    __shared__ float half_sum[256];
+ * sums of squares per 8 elements, then per 16-element half, the halves summed
+ * in order; scale = 1/sqrtf(sum/H + eps); out = (x * scale) * w, written as the
+ * activation tiles of the next projection. Mode 0 (layer 0) loads the residual
+ * with the token's embedding row (:3719-3731); mode 1 first adds the sums of
+ * the previous projection (the residual add of :3351-3452, :3836-3842). */
+__global__ void __launch_bounds__(256) input_kernel(const StepParams p, const float *__restrict__ norm_w, int mode,
+                                                    const Partials add, TileOut out) {
+    __shared__ float chunk_sum[512];
     __shared__ float scale_s;
+    pdl_trigger();
+    pdl_wait();
     const uint32_t s = blockIdx.x, H = p.hidden, t = threadIdx.x;
     float *x = p.resid + (size_t)s * H;
-    if (embed) {
-        const uint32_t step = *p.step;
-        int32_t tok = (p.greedy && step > 0) ? p.argmax_out[(size_t)(step - 1) * p.streams + s]
-                                             : p.tokens[(size_t)step * p.streams + s];
+    int32_t tok = 0;
+    if (mode == 0) {
+        const uint32_t step = __ldcg(p.step);
+        tok = (p.greedy && step > 0) ? __ldcg(p.argmax_out + (size_t)(step - 1) * p.streams + s)
+                                     : __ldcg(p.tokens + (size_t)step * p.streams + s);
         if (tok < 0 || (uint32_t)tok >= p.vocab) {
             if (t == 0) report(p.status, kErrBadToken, s);
             tok = 0;
         }
-        const uint16_t *e = p.emb + (size_t)tok * H;
-        for (uint32_t j = t; j < H; j += 256) x[j] = __uint_as_float((uint32_t)e[j] << 16);
-        __syncthreads();
     }
-    for (uint32_t hf = t; hf < H / 16; hf += 256) {
+    float v[8];
+    for (uint32_t c8 = t; c8 < H / 8; c8 += 256) {
+        if (mode == 0) {
+            const uint4 e = *reinterpret_cast<const uint4 *>(p.emb + (size_t)tok * H + c8 * 8);
+            const uint32_t w[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[2 * i] = __uint_as_float(w[i] << 16);
+                v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+            }
+        } else {
+            float y[8];
+            psum8(add, s, c8 * 8, y);
+            const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(x) + 2 * c8);
+            const float4 a1 = __ldcg(reinterpret_cast<const float4 *>(x) + 2 * c8 + 1);
+            const float xa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(xa[i], y[i]);
+        }
+        reinterpret_cast<float4 *>(x)[2 * c8] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4 *>(x)[2 * c8 + 1] = make_float4(v[4], v[5], v[6], v[7]);
         float acc = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const float v = x[hf * 16 + k];
-            acc = __fadd_rn(acc, __fmul_rn(v, v));
-        }
-        half_sum[hf] = acc;
+        for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(v[i], v[i]));
+        chunk_sum[c8] = acc;
     }
     __syncthreads();
     if (t == 0) {
         float sum = 0.0f;
-        for (uint32_t hf = 0; hf < H / 16; ++hf) sum = __fadd_rn(sum, half_sum[hf]);
+        for (uint32_t hf = 0; hf < H / 16; ++hf) sum = __fadd_rn(sum, __fadd_rn(chunk_sum[2 * hf], chunk_sum[2 * hf + 1]));
         scale_s = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(sum, (float)H), p.eps)));
     }
     __syncthreads();
@@ -592,38 +553,86 @@ __global__ void __launch_bounds__(256) input_kernel(const StepParams p, const fl
     uint32_t n, npad;
     uint8_t *tiles = pass_tiles(out, s, n, npad);
     for (uint32_t c8 = t; c8 < H / 8; c8 += 256) {
-        float v[8];
+        const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(x) + 2 * c8);
+        const float4 a1 = __ldcg(reinterpret_cast<const float4 *>(x) + 2 * c8 + 1);
+        const float xa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        float o[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t j = c8 * 8 + i;
-            v[i] = __fmul_rn(__fmul_rn(x[j], scale), norm_w[j]);
-        }
-        put_act8(tiles, npad, n, c8 * 8, v);
+        for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(xa[i], scale), norm_w[c8 * 8 + i]);
+        put_act8(tiles, npad, n, c8 * 8, o);
     }
 }
 
-/* The gated delta rule for 64 state columns of one head of one stream
- * (c_impl/gdn_model.cpp:1932-2340 in the FP32 contract): q, k L2-normalised
- * (tree256 sums, :2059-2092), beta = sigmoid(b), decay = exp(-exp(a_log) *
- * softplus(a + dt_bias)) (:2101-2105), alpha = tree256(qn . kn) (:2119-2124);
- * per column v: r = S[:, v] . kn, p = S[:, v] . qn, delta = beta (v - decay r),
- * o = (decay p + alpha delta) / 16, S'[:, v] = decay S[:, v] + kn delta. A warp
- * owns eight columns; lane l holds k = 4l .. 4l+3 and 128+4l .. 128+4l+3 of a
- * column, the two dot products are warp sums. */
-constexpr uint32_t kRecurCols = 64;
-__global__ void __launch_bounds__(256) recur_kernel(const StepParams p, uint32_t layer) {
-    __shared__ __align__(16) float qn[256], kn[256];
-    __shared__ float red[2][8];
-    __shared__ float scal[3];
+/* Causal conv + SiLU of 8 channels (:1543-1660): window [t0, t1, t2, new]
+ * summed left to right; the new window [t1, t2, new] goes to the other tail
+ * buffer when `write` is set. */
+__device__ __forceinline__ void conv8(const float *__restrict__ tr, float *__restrict__ tw, uint32_t H,
+                                      const float *__restrict__ w4, const float (&y)[8], bool write, float (&o)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float t0 = __ldcg(tr + i), t1 = __ldcg(tr + H + i), t2 = __ldcg(tr + 2 * H + i);
+        const float4 w = reinterpret_cast<const float4 *>(w4)[i];
+        float sum = __fadd_rn(__fmul_rn(t0, w.x), __fmul_rn(t1, w.y));
+        sum = __fadd_rn(sum, __fmul_rn(t2, w.z));
+        sum = __fadd_rn(sum, __fmul_rn(y[i], w.w));
+        o[i] = silu_ref(sum);
+        if (write) {
+            tw[i] = t1;
+            tw[H + i] = t2;
+            tw[2 * H + i] = y[i];
+        }
+    }
+}
+
+/* Per (stream, head), the inputs of the gated delta rule (c_impl/gdn_model.cpp:
+ * 1932-2124 in the FP32 contract): q, k, v of the head after the causal conv +
+ * SiLU (new tails to the other buffer), q and k L2-normalised (tree256 sums,
+ * :2059-2092), alpha = tree256(qn . kn) (:2119-2124), beta = sigmoid(b) and
+ * decay = exp(-exp(a_log) * softplus(a + dt_bias)) (:2101-2105). Output
+ * prep[s][h] = {alpha, beta, decay, 0, qn[256], kn[256], v[256]}. */
+constexpr uint32_t kPrepFloats = 4 + 3 * 256;
+__global__ void __launch_bounds__(128) prep_kernel(const StepParams p, uint32_t layer, const Partials qkv,
+                                                   float *__restrict__ prep) {
+    __shared__ __align__(16) float qs[256], ks[256];
+    __shared__ float red[3][4];
+    __shared__ float scal[2];
+    pdl_trigger();
+    pdl_wait();
     const uint32_t nh = p.heads, H = p.hidden;
-    const uint32_t cb = blockIdx.x % (256 / kRecurCols);
-    const uint32_t h = (blockIdx.x / (256 / kRecurCols)) % nh;
-    const uint32_t s = blockIdx.x / ((256 / kRecurCols) * nh);
-    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const uint32_t qkv_stride = 4 * H + 2 * nh;
-    const float *row = p.qkv + (size_t)s * qkv_stride;
-    const float q = row[h * 256 + t], k = row[H + h * 256 + t];
-    float sq = __fmul_rn(q, q), sk = __fmul_rn(k, k);
+    const uint32_t h = blockIdx.x % nh, s = blockIdx.x / nh, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const float *aux = p.aux + (size_t)layer * p.aux_stride;
+    float *out = prep + ((size_t)s * nh + h) * kPrepFloats;
+    if (t < 96) {
+        const uint32_t kind = t >> 5, ch = h * 256 + (t & 31) * 8;
+        float y[8], o[8];
+        psum8(qkv, s, kind * H + ch, y);
+        const uint32_t par = __ldcg(p.tails_parity);
+        const size_t toff = (size_t)s * p.tails_stride + ((size_t)layer * 3 + kind) * 3 * H + ch;
+        conv8(p.tails + par * p.tails_buf + toff, p.tails + (par ^ 1u) * p.tails_buf + toff, H,
+              aux + 2 * H + 256 + ((size_t)kind * H + ch) * 4, y, true, o);
+        float *dst = kind == 0 ? qs + (t & 31) * 8 : (kind == 1 ? ks + (t & 31) * 8 : out + 4 + 512 + (t & 31) * 8);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = o[i];
+    } else if (t == 96) {
+        float ya[8], yb[8];
+        psum8(qkv, s, 4 * H + (h & ~7u), ya);
+        psum8(qkv, s, 4 * H + ((nh + h) & ~7u), yb);
+        float av = 0.0f, bv = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            av = ((uint32_t)i == (h & 7u)) ? ya[i] : av;
+            bv = ((uint32_t)i == ((nh + h) & 7u)) ? yb[i] : bv;
+        }
+        const float *a_log = aux + 14 * H + 256, *dt_bias = a_log + nh;
+        scal[0] = sigmoid_ref(bv);
+        scal[1] = expf(__fmul_rn(-expf(a_log[h]), softplus_ref(__fadd_rn(av, dt_bias[h]))));
+    }
+    __syncthreads();
+    /* tree256: thread t holds elements 2t, 2t+1 (first level), the warp
+     * butterfly the next five levels, then (w0 + w1) + (w2 + w3) */
+    const float2 q2 = reinterpret_cast<const float2 *>(qs)[t], k2 = reinterpret_cast<const float2 *>(ks)[t];
+    float sq = __fadd_rn(__fmul_rn(q2.x, q2.x), __fmul_rn(q2.y, q2.y));
+    float sk = __fadd_rn(__fmul_rn(k2.x, k2.x), __fmul_rn(k2.y, k2.y));
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
@@ -634,44 +643,61 @@ __global__ void __launch_bounds__(256) recur_kernel(const StepParams p, uint32_t
         red[1][warp] = sk;
     }
     __syncthreads();
-    const float tq = __fadd_rn(__fadd_rn(__fadd_rn(red[0][0], red[0][1]), __fadd_rn(red[0][2], red[0][3])),
-                               __fadd_rn(__fadd_rn(red[0][4], red[0][5]), __fadd_rn(red[0][6], red[0][7])));
-    const float tk = __fadd_rn(__fadd_rn(__fadd_rn(red[1][0], red[1][1]), __fadd_rn(red[1][2], red[1][3])),
-                               __fadd_rn(__fadd_rn(red[1][4], red[1][5]), __fadd_rn(red[1][6], red[1][7])));
+    const float tq = __fadd_rn(__fadd_rn(red[0][0], red[0][1]), __fadd_rn(red[0][2], red[0][3]));
+    const float tk = __fadd_rn(__fadd_rn(red[1][0], red[1][1]), __fadd_rn(red[1][2], red[1][3]));
     const float q_inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(tq, 1e-6f)));
     const float k_inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(tk, 1e-6f)));
-    const float qv = __fmul_rn(q, q_inv), kv = __fmul_rn(k, k_inv);
-    qn[t] = qv;
-    kn[t] = kv;
-    float a = __fmul_rn(qv, kv);
+    const float2 qn = make_float2(__fmul_rn(q2.x, q_inv), __fmul_rn(q2.y, q_inv));
+    const float2 kn = make_float2(__fmul_rn(k2.x, k_inv), __fmul_rn(k2.y, k_inv));
+    reinterpret_cast<float2 *>(out + 4)[t] = qn;
+    reinterpret_cast<float2 *>(out + 4 + 256)[t] = kn;
+    float a = __fadd_rn(__fmul_rn(qn.x, kn.x), __fmul_rn(qn.y, kn.y));
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (lane == 0) red[2][warp] = a;
     __syncthreads();
-    if (lane == 0) red[0][warp] = a;
     if (t == 0) {
-        const float *aux = p.aux + (size_t)layer * p.aux_stride;
-        const float *a_log = aux + 14 * H + 256, *dt_bias = a_log + nh;
-        const float av = row[4 * H + h], bv = row[4 * H + nh + h];
-        scal[1] = sigmoid_ref(bv);
-        const float dv = __fmul_rn(-expf(a_log[h]), softplus_ref(__fadd_rn(av, dt_bias[h])));
-        scal[2] = expf(dv);
+        out[0] = __fadd_rn(__fadd_rn(red[2][0], red[2][1]), __fadd_rn(red[2][2], red[2][3]));
+        out[1] = scal[0];
+        out[2] = scal[1];
+        out[3] = 0.0f;
     }
-    __syncthreads();
-    const float alpha = __fadd_rn(__fadd_rn(__fadd_rn(red[0][0], red[0][1]), __fadd_rn(red[0][2], red[0][3])),
-                                  __fadd_rn(__fadd_rn(red[0][4], red[0][5]), __fadd_rn(red[0][6], red[0][7])));
-    const float beta = scal[1], decay = scal[2];
-    const float4 k0 = reinterpret_cast<const float4 *>(kn)[lane], k1 = reinterpret_cast<const float4 *>(kn)[32 + lane];
-    const float4 q0 = reinterpret_cast<const float4 *>(qn)[lane], q1 = reinterpret_cast<const float4 *>(qn)[32 + lane];
+}
+
+/* The gated delta rule for 64 state columns of one head of one stream
+ * (c_impl/gdn_model.cpp:2184-2300 in the FP32 contract), from prep_kernel's
+ * inputs: per column v, r = S[:, v] . kn, p = S[:, v] . qn, delta = beta (v -
+ * decay r), o = (decay p + alpha delta) / 16, S'[:, v] = decay S[:, v] +
+ * kn delta. A warp owns eight columns; lane l holds k = 4l .. 4l+3 and
+ * 128+4l .. 128+4l+3 of a column, the two dot products are warp sums. S is
+ * read and written once, with streaming (evict-first) accesses. */
+constexpr uint32_t kRecurCols = 64;
+__global__ void __launch_bounds__(256) recur_kernel(const StepParams p, uint32_t layer, const float *prep) {
+    const uint32_t nh = p.heads, H = p.hidden;
+    const uint32_t cb = blockIdx.x % (256 / kRecurCols);
+    const uint32_t h = (blockIdx.x / (256 / kRecurCols)) % nh;
+    const uint32_t s = blockIdx.x / ((256 / kRecurCols) * nh);
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t c0 = cb * kRecurCols + warp * 8;
     float *S = p.state + (size_t)s * p.state_stride + (((size_t)layer * nh + h) * 256 + c0) * 256;
+    pdl_trigger();
+    /* S was last written by this layer's recurrence one step earlier: it is
+     * loaded before waiting for prep_kernel */
     float4 a0[8], a1[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        a0[i] = __ldcs(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + lane);
-        a1[i] = __ldcs(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + 32 + lane);
+        a0[i] = __ldcg(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + lane);
+        a1[i] = __ldcg(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + 32 + lane);
     }
+    pdl_wait();
+    const float *in = prep + ((size_t)s * nh + h) * kPrepFloats;
+    const float alpha = __ldcg(in), beta = __ldcg(in + 1), decay = __ldcg(in + 2);
+    const float4 q0 = __ldcg(reinterpret_cast<const float4 *>(in + 4) + lane);
+    const float4 q1 = __ldcg(reinterpret_cast<const float4 *>(in + 4) + 32 + lane);
+    const float4 k0 = __ldcg(reinterpret_cast<const float4 *>(in + 4 + 256) + lane);
+    const float4 k1 = __ldcg(reinterpret_cast<const float4 *>(in + 4 + 256) + 32 + lane);
+    const float vv = lane < 8 ? __ldcg(in + 4 + 512 + c0 + lane) : 0.0f;
     float *attn = p.attn + (size_t)s * H + h * 256;
-    const float *vrow = row + 2 * H + h * 256;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         float r = __fmul_rn(a0[i].x, k0.x), pp = __fmul_rn(a0[i].x, q0.x);
@@ -687,9 +713,9 @@ __global__ void __launch_bounds__(256) recur_kernel(const StepParams p, uint32_t
             r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, o));
             pp = __fadd_rn(pp, __shfl_xor_sync(0xffffffffu, pp, o));
         }
-        const uint32_t col = c0 + i;
-        const float delta = __fmul_rn(beta, __fsub_rn(vrow[col], __fmul_rn(decay, r)));
-        if (lane == 0) attn[col] = __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pp), __fmul_rn(alpha, delta)));
+        const float v = __shfl_sync(0xffffffffu, vv, i);
+        const float delta = __fmul_rn(beta, __fsub_rn(v, __fmul_rn(decay, r)));
+        if (lane == 0) attn[c0 + i] = __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pp), __fmul_rn(alpha, delta)));
         float4 n0, n1;
         n0.x = __fadd_rn(__fmul_rn(decay, a0[i].x), __fmul_rn(k0.x, delta));
         n0.y = __fadd_rn(__fmul_rn(decay, a0[i].y), __fmul_rn(k0.y, delta));
@@ -705,58 +731,114 @@ __global__ void __launch_bounds__(256) recur_kernel(const StepParams p, uint32_t
 }
 
 /* Output RMSNorm x swish gate of one head of one stream (c_impl/gdn_model.cpp:
- * 3226-3349): per 16-element half a sequential sum of squares, halves summed
- * in order; scale = 1/sqrtf(sum/256 + eps); out = ((a * scale) * w) * g *
- * sigmoid(g), written as activation tiles of the O projection. */
-__global__ void __launch_bounds__(256) gate_norm_kernel(const StepParams p, uint32_t layer, TileOut out) {
-    __shared__ float half_sum[16];
-    __shared__ float scale_s;
+ * 3226-3349): sums of squares per 8 elements, then per 16-element half, the
+ * halves summed in order; scale = 1/sqrtf(sum/256 + eps); out = ((a * scale)
+ * * w) * g * sigmoid(g), written as activation tiles of the O projection. */
+__global__ void __launch_bounds__(32) gate_norm_kernel(const StepParams p, uint32_t layer, const Partials qkv,
+                                                       TileOut out) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t nh = p.heads, H = p.hidden;
     const uint32_t h = blockIdx.x % nh, s = blockIdx.x / nh, t = threadIdx.x;
-    const float *a = p.attn + (size_t)s * H + h * 256;
-    if (t < 16) {
-        float acc = 0.0f;
+    const float *a = p.attn + (size_t)s * H + h * 256 + t * 8;
+    const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(a)), a1 = __ldcg(reinterpret_cast<const float4 *>(a) + 1);
+    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    float g[8];
+    psum8(qkv, s, 3 * H + h * 256 + t * 8, g);
+    float acc = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const float v = a[t * 16 + k];
-            acc = __fadd_rn(acc, __fmul_rn(v, v));
-        }
-        half_sum[t] = acc;
+    for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(av[i], av[i]));
+    /* halves: lanes (2j, 2j+1); then the 16 halves in order */
+    const float half = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, half, 2 * j));
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(sum, 256.0f), p.eps)));
+    const float *w = p.aux + (size_t)layer * p.aux_stride + H + t * 8; /* o_norm */
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float nrm = __fmul_rn(__fmul_rn(av[i], scale), w[i]);
+        v[i] = __fmul_rn(__fmul_rn(nrm, g[i]), sigmoid_ref(g[i]));
     }
-    __syncthreads();
-    if (t == 0) {
-        float sum = 0.0f;
-        for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, half_sum[i]);
-        scale_s = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(sum, 256.0f), p.eps)));
-    }
-    __syncthreads();
-    if (t < 32) {
-        const float *w = p.aux + (size_t)layer * p.aux_stride + H;  /* o_norm */
-        const float *g = p.qkv + (size_t)s * (4 * H + 2 * nh) + 3 * H + h * 256;
-        float v[8];
+    uint32_t n, npad;
+    uint8_t *tiles = pass_tiles(out, s, n, npad);
+    put_act8(tiles, npad, n, h * 256 + t * 8, v);
+}
+
+/* m_i = silu(gate_i) * up_i (c_impl/gdn_model.cpp:4751-4770; gate row i at 2i,
+ * up at 2i + 1), eight m per thread, as activation tiles of the down projection. */
+__global__ void __launch_bounds__(256) swiglu_kernel(const StepParams p, const Partials gu, TileOut out) {
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t chunks = p.inter / 8;
+    const uint32_t s = blockIdx.x % p.streams, part = blockIdx.x / p.streams;
+    const uint32_t c8 = part * 256 + threadIdx.x;
+    if (c8 >= chunks) return;
+    float lo[8], hi[8];
+    psum8(gu, s, c8 * 16, lo);
+    psum8(gu, s, c8 * 16 + 8, hi);
+    const float y[16] = {lo[0], lo[1], lo[2], lo[3], lo[4], lo[5], lo[6], lo[7],
+                         hi[0], hi[1], hi[2], hi[3], hi[4], hi[5], hi[6], hi[7]};
+    float m[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = __fmul_rn(silu_ref(y[2 * i]), y[2 * i + 1]);
+    uint32_t n, npad;
+    uint8_t *tiles = pass_tiles(out, s, n, npad);
+    put_act8(tiles, npad, n, c8 * 8, m);
+}
+
+/* FP32 logits (not rounded) and the per-stream argmax: largest value, lowest
+ * row on ties (c_impl/gdn_model.cpp:4775-4925), as a packed key. */
+__global__ void __launch_bounds__(256) logits_kernel(const StepParams p, const Partials lm) {
+    __shared__ unsigned long long best[8];
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t s = blockIdx.x % p.streams, part = blockIdx.x / p.streams;
+    const uint32_t c8 = part * 256 + threadIdx.x;
+    unsigned long long key = 0ull;
+    if (c8 * 8 < p.vocab) {
+        float y[8];
+        psum8(lm, s, c8 * 8, y);
+        float *dst = p.logits + (size_t)s * p.vocab + c8 * 8;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const uint32_t j = t * 8 + i;
-            const float gv = g[j];
-            const float nrm = __fmul_rn(__fmul_rn(a[j], scale_s), w[j]);
-            v[i] = __fmul_rn(__fmul_rn(nrm, gv), sigmoid_ref(gv));
+            if (c8 * 8 + i < p.vocab) {
+                dst[i] = y[i];
+                const unsigned long long kk = argmax_key(y[i], c8 * 8 + i);
+                key = kk > key ? kk : key;
+            }
         }
-        uint32_t n, npad;
-        uint8_t *tiles = pass_tiles(out, s, n, npad);
-        put_act8(tiles, npad, n, h * 256 + t * 8, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+    }
+    if ((threadIdx.x & 31) == 0) best[threadIdx.x >> 5] = key;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long b = best[0];
+        for (int w = 1; w < 8; ++w) b = best[w] > b ? best[w] : b;
+        if (b != 0ull) atomicMax(p.keys + s, b);
     }
 }
 
-/* Tokens of the step from the argmax keys; keys cleared; step advanced. */
+/* Tokens of the step from the argmax keys; keys cleared; step and tail parity advanced. */
 __global__ void __launch_bounds__(256) finish_kernel(const StepParams p) {
-    const uint32_t step = *p.step;
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t step = __ldcg(p.step);
     for (uint32_t s = threadIdx.x; s < p.streams; s += 256) {
-        const unsigned long long key = p.keys[s];
+        const unsigned long long key = __ldcg(p.keys + s);
         p.argmax_out[(size_t)step * p.streams + s] = key ? (int32_t)(0xFFFFFFFFu - (uint32_t)key) : 0;
         p.keys[s] = 0ull;
     }
     __syncthreads();
-    if (threadIdx.x == 0) *p.step = step + 1;
+    if (threadIdx.x == 0) {
+        *p.step = step + 1;
+        *p.tails_parity ^= 1u;
+    }
 }
 
 }  // namespace
@@ -766,10 +848,14 @@ size_t gemm_smem_bytes(uint32_t npad, uint32_t a_slots, uint32_t b_slots) {
 }
 
 void gemm_slots(uint32_t npad, uint32_t *a_slots, uint32_t *b_slots) {
+    /* activation blocks come from L2 (a microsecond or more under load): up to
+     * 96 KB of them in flight, at least two; the weight ring takes the rest
+     * (at most 10 blocks) */
     const size_t bblock = (size_t)kTerms * npad * 128u;
-    const uint32_t sb = bblock >= 24576 ? 2u : 4u;
-    size_t room = kSmemLimit - kSmemAlign - kSmemTail - sb * bblock;
-    uint32_t sa = (uint32_t)(room / kABlockBytes);
+    const size_t budget = kSmemLimit - kSmemAlign - kSmemTail;
+    uint32_t sb = (uint32_t)std::max<size_t>(2, std::min<size_t>(8, (96 * 1024) / bblock));
+    while (sb > 2 && sb * bblock + 6 * (size_t)kABlockBytes > budget) --sb;
+    uint32_t sa = (uint32_t)((budget - sb * bblock) / kABlockBytes);
     if (sa > 10) sa = 10;
     *a_slots = sa;
     *b_slots = sb;
@@ -794,33 +880,62 @@ uint32_t gemm_max_local(uint32_t mtiles, uint32_t kblocks, uint32_t grid) {
 
 size_t tile_pass_bytes(uint32_t npad, uint32_t k) { return (size_t)(k / kTileK) * kTerms * npad * 128u; }
 
+/* Launch with programmatic stream serialization (see pdl_wait). */
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), uint32_t grid, uint32_t block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 cudaError_t launch_gemm(const GemmParams &p, uint32_t grid, cudaStream_t stream) {
     const size_t smem = gemm_smem_bytes(p.npad, p.a_slots, p.b_slots);
     cudaError_t e = cudaFuncSetAttribute(tile_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    tile_gemm_kernel<<<grid, kGemmThreads, smem, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(tile_gemm_kernel, grid, kGemmThreads, smem, stream, p);
 }
 
-
-cudaError_t launch_input(const StepParams &p, const float *norm_w, int embed, TileOut out, cudaStream_t stream) {
-    input_kernel<<<p.streams, 256, 0, stream>>>(p, norm_w, embed, out);
-    return cudaGetLastError();
+cudaError_t launch_input(const StepParams &p, const float *norm_w, int mode, const Partials &add, TileOut out,
+                         cudaStream_t stream) {
+    return launch_pdl(input_kernel, p.streams, 256, 0, stream, p, norm_w, mode, add, out);
 }
 
-cudaError_t launch_recur(const StepParams &p, uint32_t layer, cudaStream_t stream) {
-    recur_kernel<<<p.streams * p.heads * (256 / kRecurCols), 256, 0, stream>>>(p, layer);
-    return cudaGetLastError();
+cudaError_t launch_recur(const StepParams &p, uint32_t layer, const Partials &qkv, float *prep, cudaStream_t stream) {
+    cudaError_t e = launch_pdl(prep_kernel, p.streams * p.heads, 128, 0, stream, p, layer, qkv, prep);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(recur_kernel, p.streams * p.heads * (256 / kRecurCols), 256, 0, stream, p, layer,
+                      (const float *)prep);
 }
 
-cudaError_t launch_gate_norm(const StepParams &p, uint32_t layer, TileOut out, cudaStream_t stream) {
-    gate_norm_kernel<<<p.streams * p.heads, 256, 0, stream>>>(p, layer, out);
-    return cudaGetLastError();
+size_t prep_floats(uint32_t streams, uint32_t heads) { return (size_t)streams * heads * kPrepFloats; }
+
+cudaError_t launch_gate_norm(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out,
+                             cudaStream_t stream) {
+    return launch_pdl(gate_norm_kernel, p.streams * p.heads, 32, 0, stream, p, layer, qkv, out);
+}
+
+cudaError_t launch_swiglu(const StepParams &p, const Partials &gu, TileOut out, cudaStream_t stream) {
+    const uint32_t parts = (p.inter / 8 + 255) / 256;
+    return launch_pdl(swiglu_kernel, p.streams * parts, 256, 0, stream, p, gu, out);
+}
+
+cudaError_t launch_logits(const StepParams &p, const Partials &lm, cudaStream_t stream) {
+    const uint32_t parts = (p.vocab / 8 + 255) / 256 + 1;
+    return launch_pdl(logits_kernel, p.streams * parts, 256, 0, stream, p, lm);
 }
 
 cudaError_t launch_finish(const StepParams &p, cudaStream_t stream) {
-    finish_kernel<<<1, 256, 0, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(finish_kernel, 1, 256, 0, stream, p);
 }
 
 }  // namespace bt

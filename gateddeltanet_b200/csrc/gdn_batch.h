@@ -25,8 +25,9 @@
  *       kb * 3*N*128 + t * N*128 + n*128 + ((((k & 63) >> 3) ^ (n & 7)) << 4) + (k & 7)*2.
  *   per stream s: S FP32 [L][nh][v][k] (column v of a head's S[k][v] is 1 KB
  *     contiguous); conv tails FP32 [L][q,k,v][3][H] (row 2 newest, the
- *     reference's order); residual x FP32 [H]; the QKVGAB output FP32
- *     [4H + 2nh] (q, k, v after the short convolution and SiLU; g, a, b raw).
+ *     reference's order) in two buffers that alternate by step, so that the
+ *     CTAs sharing a head read the old window while others write the new
+ *     one; residual x FP32 [H].
  */
 #ifndef GDN_BATCH_H
 #define GDN_BATCH_H
@@ -42,16 +43,8 @@ constexpr int kTileM = 128;
 constexpr int kTileK = 64;
 constexpr int kTerms = 3;
 constexpr int kABlockBytes = kTileM * kTileK * 2;
-constexpr int kMaxPassStreams = 128;  /* streams per GEMM pass (TMEM: 2 x 128 columns) */
+constexpr int kMaxPassStreams = 80;   /* streams per GEMM pass: MMA N = 3 x 80 <= 256 */
 constexpr int kGemmThreads = 224;     /* warps 0-3 epilogue, 4 A copies, 5 B copies, 6 MMA */
-
-enum Epilogue : int {
-    kEpiStore = 0,   /* out[n * out_stride + row] = y */
-    kEpiQKV = 1,     /* rows < 3H: causal conv + SiLU with tail update; others stored raw */
-    kEpiResid = 2,   /* resid[n * out_stride + row] += y */
-    kEpiSwiGLU = 3,  /* rows (2i, 2i+1) = (gate_i, up_i): m_i = silu(g) * u as activation tiles */
-    kEpiLogits = 4,  /* out[n * out_stride + row] = y, and the per-stream argmax key */
-};
 
 enum Error : uint32_t {
     kErrNone = 0,
@@ -63,32 +56,39 @@ enum Error : uint32_t {
     kErrBadToken = 6,
 };
 
+/* Unit partition of one projection: CTA c of `grid` takes the contiguous
+ * (tile, k-block) units [unit_start(c), unit_start(c + 1)). */
+__host__ __device__ __forceinline__ uint32_t unit_start(uint32_t c, uint32_t units, uint32_t grid) {
+    return (uint32_t)(((uint64_t)c * units) / grid);
+}
+/* the CTA whose range holds unit u: the largest c with unit_start(c) <= u */
+__host__ __device__ __forceinline__ uint32_t unit_owner(uint32_t u, uint32_t units, uint32_t grid) {
+    return (uint32_t)((((uint64_t)(u + 1) * grid) + units - 1) / units) - 1u;
+}
+
+/* Split-K partial sums of one projection. The (tile, k-block) units are split
+ * over the launch's CTAs in contiguous ranges; CTA c writes, for each tile
+ * segment it covers (local index j = tile - its first tile), the FP32 block
+ * [npad][128] (stream-major, rows of the tile contiguous) at
+ *   base + pass * pass_stride + (c * max_local + j) * npad * 128
+ * floats. The consumer of the projection sums the segments of a row's tile in
+ * k order (deterministic), so no GEMM waits for another CTA. */
+struct Partials {
+    float *base;
+    size_t pass_stride;   /* floats per pass */
+    uint32_t units, grid, kblocks, max_local;
+    uint32_t npad_last, passes;
+};
+
 struct GemmParams {
     const uint8_t *a;      /* tile image, [m-tile][k-block] 16 KB blocks */
     const uint8_t *b;      /* activation tiles of this pass */
-    uint32_t m;            /* valid rows */
     uint32_t kblocks;      /* K / 64 */
     uint32_t mtiles;       /* ceil(M / 128) */
     uint32_t npad;         /* streams of this pass, padded to a multiple of 16 */
-    uint32_t nvalid;       /* streams of this pass */
-    uint32_t stream0;      /* first stream of this pass (argmax keys, tails) */
     uint32_t a_slots, b_slots;
-    float *partial;        /* [grid][max_local][npad][128] */
-    uint32_t max_local;    /* partial slots per CTA */
-    uint32_t *counters;    /* per m-tile arrival counters, zero between launches */
-    int epi;
-    float *out;            /* Store / Logits / Resid: [n][out_stride] (pass-relative n) */
-    uint32_t out_stride;
-    /* QKV: conv weights FP32 [3][H][4] of the layer; tails of stream 0 of the
-     * pass at tails, stream stride tails_stride floats, layout [3][3][H] */
-    const float *conv_w;
-    float *tails;
-    size_t tails_stride;
-    uint32_t hidden;
-    /* SwiGLU: activation tiles of the next GEMM (K = M / 2) */
-    uint8_t *next_b;
-    /* Logits: argmax keys, one per stream (absolute stream index) */
-    unsigned long long *keys;
+    float *partial;        /* this pass's slots */
+    uint32_t max_local;    /* slots per CTA */
     uint32_t *status;      /* [0] error code, [1] where */
 };
 
@@ -104,27 +104,30 @@ cudaError_t launch_gemm(const GemmParams &p, uint32_t grid, cudaStream_t stream)
 
 /* Per-stream kernels of one step. */
 struct StepParams {
-    uint32_t streams, npad_total;  /* all streams; npad of each pass is min(128, ...) */
+    uint32_t streams;
     uint32_t hidden, heads, inter, vocab, layers;
     float eps;
     const uint16_t *emb;           /* BF16 [V][H] */
     const float *aux;              /* per layer: attn_norm | o_norm | mlp_norm | conv_w | a_log | dt_bias */
     size_t aux_stride;
-    const float *final_norm;
     const int32_t *tokens;         /* [steps][streams] */
     uint32_t *step;                /* device step counter */
     int32_t *argmax_out;           /* [steps][streams] */
     int greedy;                    /* feed the previous argmax instead of tokens[step] (step > 0) */
     float *resid;                  /* [streams][H] */
-    float *qkv;                    /* [streams][4H + 2nh] */
     float *attn;                   /* [streams][H] */
     float *state;                  /* [streams][L][nh][256][256] */
     size_t state_stride;           /* floats per stream */
+    float *tails;                  /* [2][streams][L][3][3][H]: read buffer *tails_parity, write the other */
+    size_t tails_stride;           /* floats per stream */
+    size_t tails_buf;              /* floats per buffer */
+    uint32_t *tails_parity;
+    float *logits;                 /* [streams][V] */
     unsigned long long *keys;      /* [streams] */
     uint32_t *status;
 };
 
-/* Activation tiles for a set of passes: pass p covers streams [128p, 128p + 128)
+/* Activation tiles for a set of passes: pass p covers streams [80p, 80p + 80)
  * and its tiles start at base + p * pass_stride bytes. */
 struct TileOut {
     uint8_t *base;
@@ -133,13 +136,22 @@ struct TileOut {
     uint32_t passes;
 };
 
-/* x <- E[token] (layer 0) and RMSNorm(x) as activation tiles (K = H) */
-cudaError_t launch_input(const StepParams &p, const float *norm_w, int embed, TileOut out, cudaStream_t stream);
-/* recurrence of layer l: S, attn from the QKVGAB output */
-cudaError_t launch_recur(const StepParams &p, uint32_t layer, cudaStream_t stream);
+/* x <- E[token] (mode 0) or x <- x + the projection's sums (mode 1, then x is
+ * stored back); RMSNorm(x) with norm_w as activation tiles (K = H) */
+cudaError_t launch_input(const StepParams &p, const float *norm_w, int mode, const Partials &add, TileOut out,
+                         cudaStream_t stream);
+/* causal conv + SiLU of q, k, v, norms and gates (prep, two launches), then
+ * the recurrence of layer l; prep holds prep_floats() floats */
+cudaError_t launch_recur(const StepParams &p, uint32_t layer, const Partials &qkv, float *prep, cudaStream_t stream);
+size_t prep_floats(uint32_t streams, uint32_t heads);
 /* output norm x swish gate as activation tiles (K = H) */
-cudaError_t launch_gate_norm(const StepParams &p, uint32_t layer, TileOut out, cudaStream_t stream);
-/* argmax tokens of the step, step counter advance */
+cudaError_t launch_gate_norm(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out,
+                             cudaStream_t stream);
+/* m = silu(gate) * up as activation tiles (K = I) */
+cudaError_t launch_swiglu(const StepParams &p, const Partials &gu, TileOut out, cudaStream_t stream);
+/* FP32 logits and the per-stream argmax keys */
+cudaError_t launch_logits(const StepParams &p, const Partials &lm, cudaStream_t stream);
+/* argmax tokens of the step, step counter and tail parity advance */
 cudaError_t launch_finish(const StepParams &p, cudaStream_t stream);
 
 size_t tile_pass_bytes(uint32_t npad, uint32_t k);

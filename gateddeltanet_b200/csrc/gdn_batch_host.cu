@@ -6,7 +6,8 @@
  * A step advances every stream by one token: the per-layer kernel sequence of
  * gdn_batch.cu, captured once into a CUDA graph and replayed (the kernels read
  * the step index from a device counter, so one graph serves every step).
- * Streams are handled in passes of up to 128 (the tile GEMM's N); each
+ * Streams are handled in passes of up to 80 (the tile GEMM's N is three
+ * BF16 terms x streams <= 256); each
  * projection is one GEMM launch per pass.
  */
 #include "gdn_batch.h"
@@ -237,11 +238,13 @@ struct GdnB200Batch {
     uint32_t streams = 0, passes = 0, npad_last = 0, sms = 0;
     uint32_t cap_steps = 0;
     size_t state_stride = 0, tails_stride = 0;
-    float *state = nullptr, *tails = nullptr, *resid = nullptr, *qkv = nullptr, *attn = nullptr, *logits = nullptr;
+    float *state = nullptr, *tails = nullptr, *resid = nullptr, *attn = nullptr, *logits = nullptr;
     uint8_t *xb = nullptr, *mb = nullptr;
     size_t xb_stride = 0, mb_stride = 0;
     float *partial = nullptr;
-    uint32_t *counters = nullptr, *status = nullptr, *step = nullptr;
+    size_t partial_pass = 0;  /* floats per pass */
+    float *prep = nullptr;    /* recurrence inputs per (stream, head) */
+    uint32_t *status = nullptr, *step = nullptr, *parity = nullptr;
     unsigned long long *keys = nullptr;
     int32_t *tokens = nullptr, *argmax = nullptr;
     int greedy = 0;
@@ -255,10 +258,6 @@ namespace {
 uint32_t pass_npad(const GdnB200Batch *b, uint32_t pass) {
     return pass + 1 == b->passes ? b->npad_last : (uint32_t)kMaxPassStreams;
 }
-uint32_t pass_streams(const GdnB200Batch *b, uint32_t pass) {
-    return std::min<uint32_t>(kMaxPassStreams, b->streams - pass * kMaxPassStreams);
-}
-
 StepParams step_params(const GdnB200Batch *b, int greedy) {
     const GDNWeightHeader &c = b->tm->cfg;
     StepParams p;
@@ -273,103 +272,89 @@ StepParams step_params(const GdnB200Batch *b, int greedy) {
     p.emb = b->tm->emb;
     p.aux = b->tm->aux;
     p.aux_stride = b->tm->aux_stride;
-    p.final_norm = b->tm->aux + b->tm->aux_stride * c.num_layers;
     p.tokens = b->tokens;
     p.step = b->step;
     p.argmax_out = b->argmax;
     p.greedy = greedy;
     p.resid = b->resid;
-    p.qkv = b->qkv;
     p.attn = b->attn;
     p.state = b->state;
     p.state_stride = b->state_stride;
+    p.tails = b->tails;
+    p.tails_stride = b->tails_stride;
+    p.tails_buf = (size_t)b->streams * b->tails_stride;
+    p.tails_parity = b->parity;
+    p.logits = b->logits;
     p.keys = b->keys;
     p.status = b->status;
     return p;
 }
 
-/* One projection over every pass. */
-int gemm_all(GdnB200Batch *b, const Matrix &mx, const uint8_t *a, const uint8_t *bt, size_t bt_stride, int epi,
-             uint32_t layer, uint32_t *launches) {
-    const GDNWeightHeader &c = b->tm->cfg;
-    const uint32_t H = c.hidden_size, nh = c.num_heads, V = c.vocab_size;
+/* One projection over every pass; *view describes where its partial sums are. */
+int gemm_all(GdnB200Batch *b, const Matrix &mx, const uint8_t *a, const uint8_t *bt, size_t bt_stride, Partials *view,
+             uint32_t *launches) {
     const uint32_t grid = gemm_grid(mx.mtiles(), mx.kblocks(), b->sms);
+    const uint32_t max_local = gemm_max_local(mx.mtiles(), mx.kblocks(), grid);
     for (uint32_t ps = 0; ps < b->passes; ++ps) {
         GemmParams p;
         memset(&p, 0, sizeof(p));
         p.a = a;
         p.b = bt + ps * bt_stride;
-        p.m = mx.m;
         p.kblocks = mx.kblocks();
         p.mtiles = mx.mtiles();
         p.npad = pass_npad(b, ps);
-        p.nvalid = pass_streams(b, ps);
-        p.stream0 = ps * kMaxPassStreams;
         gemm_slots(p.npad, &p.a_slots, &p.b_slots);
-        p.partial = b->partial;
-        p.max_local = gemm_max_local(p.mtiles, p.kblocks, grid);
-        p.counters = b->counters;
-        p.epi = epi;
+        p.partial = b->partial + ps * b->partial_pass;
+        p.max_local = max_local;
         p.status = b->status;
-        p.hidden = H;
-        const size_t s0 = p.stream0;
-        switch (epi) {
-            case kEpiQKV:
-                p.out = b->qkv + s0 * (4 * H + 2 * nh);
-                p.out_stride = 4 * H + 2 * nh;
-                p.conv_w = b->tm->aux + (size_t)layer * b->tm->aux_stride + 2 * H + 256;
-                p.tails = b->tails + s0 * b->tails_stride + (size_t)layer * 9 * H;
-                p.tails_stride = b->tails_stride;
-                break;
-            case kEpiResid:
-                p.out = b->resid + s0 * H;
-                p.out_stride = H;
-                break;
-            case kEpiSwiGLU:
-                p.next_b = b->mb + ps * b->mb_stride;
-                break;
-            case kEpiLogits:
-                p.out = b->logits + s0 * V;
-                p.out_stride = V;
-                p.keys = b->keys;
-                break;
-            default:
-                break;
-        }
         BT_OK(launch_gemm(p, grid, b->stream));
         ++*launches;
     }
+    view->base = b->partial;
+    view->pass_stride = b->partial_pass;
+    view->units = mx.mtiles() * mx.kblocks();
+    view->grid = grid;
+    view->kblocks = mx.kblocks();
+    view->max_local = max_local;
+    view->npad_last = b->npad_last;
+    view->passes = b->passes;
     return 0;
 }
 
 int enqueue_step(GdnB200Batch *b, int greedy, uint32_t *launches) {
     const GDNWeightHeader &c = b->tm->cfg;
-    const uint32_t L = c.num_layers;
+    const uint32_t L = c.num_layers, H = c.hidden_size;
     const StepParams sp = step_params(b, greedy);
-    TileOut xo = {b->xb, b->xb_stride, b->npad_last, b->passes};
+    const TileOut xo = {b->xb, b->xb_stride, b->npad_last, b->passes};
+    const TileOut mo = {b->mb, b->mb_stride, b->npad_last, b->passes};
     const TileModel *tm = b->tm;
+    Partials none, qkv, o, gu, down, lm;
+    memset(&none, 0, sizeof(none));
     *launches = 0;
-    BT_OK(launch_input(sp, tm->aux, 1, xo, b->stream));
+    BT_OK(launch_input(sp, tm->aux, 0, none, xo, b->stream));
     ++*launches;
     for (uint32_t l = 0; l < L; ++l) {
         const uint8_t *w = tm->img + (size_t)l * tm->layer_bytes;
         const float *aux = tm->aux + (size_t)l * tm->aux_stride;
-        if (gemm_all(b, tm->qkv, w + tm->qkv.off, b->xb, b->xb_stride, kEpiQKV, l, launches)) return -1;
-        BT_OK(launch_recur(sp, l, b->stream));
-        BT_OK(launch_gate_norm(sp, l, xo, b->stream));
-        *launches += 2;
-        if (gemm_all(b, tm->o, w + tm->o.off, b->xb, b->xb_stride, kEpiResid, l, launches)) return -1;
-        BT_OK(launch_input(sp, aux + c.hidden_size + 256, 0, xo, b->stream));
+        if (gemm_all(b, tm->qkv, w + tm->qkv.off, b->xb, b->xb_stride, &qkv, launches)) return -1;
+        BT_OK(launch_recur(sp, l, qkv, b->prep, b->stream));
+        BT_OK(launch_gate_norm(sp, l, qkv, xo, b->stream));
+        *launches += 3;
+        if (gemm_all(b, tm->o, w + tm->o.off, b->xb, b->xb_stride, &o, launches)) return -1;
+        BT_OK(launch_input(sp, aux + H + 256, 1, o, xo, b->stream));
         ++*launches;
-        if (gemm_all(b, tm->gu, w + tm->gu.off, b->xb, b->xb_stride, kEpiSwiGLU, l, launches)) return -1;
-        if (gemm_all(b, tm->down, w + tm->down.off, b->mb, b->mb_stride, kEpiResid, l, launches)) return -1;
-        const float *next_norm = l + 1 < L ? tm->aux + (size_t)(l + 1) * tm->aux_stride : sp.final_norm;
-        BT_OK(launch_input(sp, next_norm, 0, xo, b->stream));
+        if (gemm_all(b, tm->gu, w + tm->gu.off, b->xb, b->xb_stride, &gu, launches)) return -1;
+        BT_OK(launch_swiglu(sp, gu, mo, b->stream));
+        ++*launches;
+        if (gemm_all(b, tm->down, w + tm->down.off, b->mb, b->mb_stride, &down, launches)) return -1;
+        const float *next_norm = l + 1 < L ? tm->aux + (size_t)(l + 1) * tm->aux_stride : tm->aux + tm->aux_stride * L;
+        BT_OK(launch_input(sp, next_norm, 1, down, xo, b->stream));
         ++*launches;
     }
-    if (gemm_all(b, tm->lm, tm->img + tm->lm.off, b->xb, b->xb_stride, kEpiLogits, 0, launches)) return -1;
+    if (gemm_all(b, tm->lm, tm->img + tm->lm.off, b->xb, b->xb_stride, &lm, launches)) return -1;
+    BT_OK(launch_logits(sp, lm, b->stream));
     BT_OK(launch_finish(sp, b->stream));
-    ++*launches;
+    *launches += 2;
     return 0;
 }
 
@@ -400,9 +385,8 @@ int check_status(GdnB200Batch *b) {
                                       "MMA operand wait timeout", "accumulator wait timeout", "drain timeout",
                                       "token out of range"};
         const char *nm = st[0] < sizeof(names) / sizeof(names[0]) ? names[st[0]] : "unknown";
-        /* a failed step can leave tile counters and argmax keys mid-count */
+        /* a failed step can leave argmax keys mid-count */
         cudaMemsetAsync(b->status, 0, 2 * sizeof(uint32_t), b->stream);
-        cudaMemsetAsync(b->counters, 0, 4096 * 4, b->stream);
         cudaMemsetAsync(b->keys, 0, (size_t)b->streams * 8, b->stream);
         cudaStreamSynchronize(b->stream);
         return bfail("gdn_b200 batch: step failed on the device: %s (at %u)", nm, st[1]);
@@ -417,8 +401,8 @@ void free_batch(GdnB200Batch *b) {
         if (g) cudaGraphExecDestroy(g);
     if (b->ev0) cudaEventDestroy(b->ev0);
     if (b->ev1) cudaEventDestroy(b->ev1);
-    void *ptrs[] = {b->state, b->tails, b->resid, b->qkv, b->attn, b->logits, b->xb, b->mb,
-                    b->partial, b->counters, b->status, b->step, b->keys, b->tokens, b->argmax};
+    void *ptrs[] = {b->state, b->tails, b->resid, b->attn, b->logits, b->xb, b->mb, b->prep,
+                    b->partial, b->status, b->step, b->parity, b->keys, b->tokens, b->argmax};
     for (void *p : ptrs) cudaFree(p);
     if (b->stream) cudaStreamDestroy(b->stream);
     if (b->tm) {
@@ -439,8 +423,8 @@ int batch_supports(const GDNWeightHeader &c, uint32_t streams) {
     if (streams == 0 || streams > 1024) return bfail("gdn_b200 batch: streams must be 1..1024 (got %u)", streams);
     if (c.head_dim != 256 || c.conv_size != 4 || c.hidden_size != c.num_heads * 256)
         return bfail("gdn_b200 batch: needs head_dim 256, conv 4, hidden = heads x 256");
-    if (c.hidden_size % 512 || c.intermediate_size % 64 || c.hidden_size > 8192)
-        return bfail("gdn_b200 batch: hidden must be a multiple of 512 (<= 8192), intermediate of 64");
+    if (c.hidden_size % 512 || c.intermediate_size % 64 || c.hidden_size > 4096)
+        return bfail("gdn_b200 batch: hidden must be a multiple of 512 (<= 4096), intermediate of 64");
     return 0;
 }
 
@@ -490,26 +474,27 @@ GdnB200Batch *gdn_b200_batch_create(const GDNModel *model, uint32_t streams) {
     b->tails_stride = (size_t)L * 9 * H;
     b->xb_stride = tile_pass_bytes(kMaxPassStreams, H);
     b->mb_stride = tile_pass_bytes(kMaxPassStreams, I);
-    /* partial slots: the largest grid x slots of any projection, 128 streams x 128 rows each */
+    /* partial slots: the largest grid x slots of any projection, 80 streams x 128 rows each, per pass */
     const TileModel *tm = b->tm;
-    uint32_t slots = 0;
+    size_t slots = 0;
     for (const Matrix *mx : {&tm->qkv, &tm->o, &tm->gu, &tm->down, &tm->lm}) {
         const uint32_t g = gemm_grid(mx->mtiles(), mx->kblocks(), b->sms);
-        slots = std::max(slots, g * gemm_max_local(mx->mtiles(), mx->kblocks(), g));
+        slots = std::max<size_t>(slots, (size_t)g * gemm_max_local(mx->mtiles(), mx->kblocks(), g));
     }
+    b->partial_pass = slots * kMaxPassStreams * kTileM;
     const size_t S = streams;
     bool ok = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking) == cudaSuccess &&
               cudaEventCreate(&b->ev0) == cudaSuccess && cudaEventCreate(&b->ev1) == cudaSuccess &&
               cudaMalloc(&b->state, S * b->state_stride * 4) == cudaSuccess &&
-              cudaMalloc(&b->tails, S * b->tails_stride * 4) == cudaSuccess &&
+              cudaMalloc(&b->tails, 2 * S * b->tails_stride * 4) == cudaSuccess &&
               cudaMalloc(&b->resid, S * H * 4) == cudaSuccess &&
-              cudaMalloc(&b->qkv, S * (4 * H + 2 * nh) * 4) == cudaSuccess &&
               cudaMalloc(&b->attn, S * H * 4) == cudaSuccess && cudaMalloc(&b->logits, S * V * 4) == cudaSuccess &&
+              cudaMalloc(&b->prep, prep_floats(streams, c.num_heads) * 4) == cudaSuccess &&
               cudaMalloc(&b->xb, b->passes * b->xb_stride) == cudaSuccess &&
               cudaMalloc(&b->mb, b->passes * b->mb_stride) == cudaSuccess &&
-              cudaMalloc(&b->partial, (size_t)slots * kMaxPassStreams * kTileM * 4) == cudaSuccess &&
-              cudaMalloc(&b->counters, 4096 * 4) == cudaSuccess && cudaMalloc(&b->status, 2 * 4) == cudaSuccess &&
-              cudaMalloc(&b->step, 4) == cudaSuccess && cudaMalloc(&b->keys, S * 8) == cudaSuccess &&
+              cudaMalloc(&b->partial, b->passes * b->partial_pass * 4) == cudaSuccess &&
+              cudaMalloc(&b->status, 2 * 4) == cudaSuccess && cudaMalloc(&b->step, 4) == cudaSuccess &&
+              cudaMalloc(&b->parity, 4) == cudaSuccess && cudaMalloc(&b->keys, S * 8) == cudaSuccess &&
               cudaMalloc(&b->tokens, (size_t)b->cap_steps * S * 4) == cudaSuccess &&
               cudaMalloc(&b->argmax, (size_t)b->cap_steps * S * 4) == cudaSuccess;
     if (!ok) {
@@ -518,20 +503,14 @@ GdnB200Batch *gdn_b200_batch_create(const GDNModel *model, uint32_t streams) {
         free_batch(b);
         return nullptr;
     }
-    const uint32_t max_tiles = std::max({tm->qkv.mtiles(), tm->gu.mtiles(), tm->lm.mtiles(), tm->o.mtiles()});
-    if (max_tiles > 4096) {
-        bfail("gdn_b200 batch: too many row tiles (%u)", max_tiles);
-        free_batch(b);
-        return nullptr;
-    }
     ok = cudaMemsetAsync(b->state, 0, S * b->state_stride * 4, b->stream) == cudaSuccess &&
-         cudaMemsetAsync(b->tails, 0, S * b->tails_stride * 4, b->stream) == cudaSuccess &&
+         cudaMemsetAsync(b->tails, 0, 2 * S * b->tails_stride * 4, b->stream) == cudaSuccess &&
          cudaMemsetAsync(b->xb, 0, b->passes * b->xb_stride, b->stream) == cudaSuccess &&
          cudaMemsetAsync(b->mb, 0, b->passes * b->mb_stride, b->stream) == cudaSuccess &&
-         cudaMemsetAsync(b->counters, 0, 4096 * 4, b->stream) == cudaSuccess &&
          cudaMemsetAsync(b->status, 0, 8, b->stream) == cudaSuccess &&
          cudaMemsetAsync(b->keys, 0, S * 8, b->stream) == cudaSuccess &&
          cudaMemsetAsync(b->step, 0, 4, b->stream) == cudaSuccess &&
+         cudaMemsetAsync(b->parity, 0, 4, b->stream) == cudaSuccess &&
          cudaStreamSynchronize(b->stream) == cudaSuccess;
     if (!ok || capture(b, 0) != 0 || capture(b, 1) != 0) {
         if (!ok) bfail("gdn_b200 batch: buffer initialisation failed");
@@ -551,8 +530,17 @@ int gdn_b200_batch_reset(GdnB200Batch *b) {
     if (b == nullptr) return bfail("gdn_b200 batch: null batch");
     BT_OK(cudaSetDevice(b->device));
     BT_OK(cudaMemsetAsync(b->state, 0, (size_t)b->streams * b->state_stride * 4, b->stream));
-    BT_OK(cudaMemsetAsync(b->tails, 0, (size_t)b->streams * b->tails_stride * 4, b->stream));
+    BT_OK(cudaMemsetAsync(b->tails, 0, 2 * (size_t)b->streams * b->tails_stride * 4, b->stream));
     BT_OK(cudaStreamSynchronize(b->stream));
+    return 0;
+}
+
+/* the tail buffer the next step reads */
+static int tails_read_buffer(GdnB200Batch *b, float **buf) {
+    uint32_t par = 0;
+    BT_OK(cudaMemcpyAsync(&par, b->parity, 4, cudaMemcpyDeviceToHost, b->stream));
+    BT_OK(cudaStreamSynchronize(b->stream));
+    *buf = b->tails + (size_t)(par & 1u) * b->streams * b->tails_stride;
     return 0;
 }
 
@@ -571,8 +559,10 @@ int gdn_b200_batch_state_upload(GdnB200Batch *b, uint32_t s, const float *rec, s
                 for (size_t v = 0; v < 256; ++v) S[(lh * 256 + v) * 256 + k] = rec[(lh * 256 + k) * 256 + v];
     });
     BT_OK(cudaSetDevice(b->device));
+    float *tails = nullptr;
+    if (tails_read_buffer(b, &tails) != 0) return -1;
     BT_OK(cudaMemcpyAsync(b->state + s * b->state_stride, S.data(), rec_floats * 4, cudaMemcpyHostToDevice, b->stream));
-    BT_OK(cudaMemcpyAsync(b->tails + s * b->tails_stride, conv, conv_floats * 4, cudaMemcpyHostToDevice, b->stream));
+    BT_OK(cudaMemcpyAsync(tails + s * b->tails_stride, conv, conv_floats * 4, cudaMemcpyHostToDevice, b->stream));
     BT_OK(cudaStreamSynchronize(b->stream));
     return 0;
 }
@@ -586,8 +576,10 @@ int gdn_b200_batch_state_download(GdnB200Batch *b, uint32_t s, float *rec, size_
         return bfail("gdn_b200 batch: state sizes do not match the model");
     std::vector<float> S(rec_floats);
     BT_OK(cudaSetDevice(b->device));
+    float *tails = nullptr;
+    if (tails_read_buffer(b, &tails) != 0) return -1;
     BT_OK(cudaMemcpyAsync(S.data(), b->state + s * b->state_stride, rec_floats * 4, cudaMemcpyDeviceToHost, b->stream));
-    BT_OK(cudaMemcpyAsync(conv, b->tails + s * b->tails_stride, conv_floats * 4, cudaMemcpyDeviceToHost, b->stream));
+    BT_OK(cudaMemcpyAsync(conv, tails + s * b->tails_stride, conv_floats * 4, cudaMemcpyDeviceToHost, b->stream));
     BT_OK(cudaStreamSynchronize(b->stream));
     parallel_for(L * nh, [&](size_t lo, size_t hi) {
         for (size_t lh = lo; lh < hi; ++lh)
@@ -664,7 +656,7 @@ int gdn_b200_batch_fetch_logits(GdnB200Batch *b, float *logits) {
 
 /* Test hook: Y[n][m] = sum_k W[m][k] X[n][k] through one tile-GEMM launch
  * (W BF16-exact FP32 words [m][k], X FP32 [n][k] split into three BF16 terms
- * as the engine does; k a multiple of 64, n <= 128). */
+ * as the engine does; k a multiple of 64, n <= 80). */
 int gdn_b200_test_tile_gemm(uint32_t m, uint32_t k, uint32_t n, const float *w, const float *x, float *y) {
     if (m == 0 || k == 0 || k % kTileK || n == 0 || n > (uint32_t)kMaxPassStreams || !w || !x || !y)
         return bfail("gdn_b200 batch: bad tile-GEMM test shape");
@@ -715,51 +707,58 @@ int gdn_b200_test_tile_gemm(uint32_t m, uint32_t k, uint32_t n, const float *w, 
         }
     const uint32_t grid = gemm_grid(mx.mtiles(), mx.kblocks(), (uint32_t)sms);
     const uint32_t max_local = gemm_max_local(mx.mtiles(), mx.kblocks(), grid);
+    const size_t part_floats = (size_t)grid * max_local * npad * kTileM;
     uint8_t *d_img = nullptr, *d_act = nullptr;
-    float *d_y = nullptr, *d_part = nullptr;
-    uint32_t *d_cnt = nullptr, *d_status = nullptr;
+    float *d_part = nullptr;
+    uint32_t *d_status = nullptr;
     int rc = 0;
     if (cudaMalloc(&d_img, img.size()) != cudaSuccess || cudaMalloc(&d_act, act.size()) != cudaSuccess ||
-        cudaMalloc(&d_y, (size_t)n * m * 4) != cudaSuccess ||
-        cudaMalloc(&d_part, (size_t)grid * max_local * npad * kTileM * 4) != cudaSuccess ||
-        cudaMalloc(&d_cnt, (size_t)mx.mtiles() * 4) != cudaSuccess || cudaMalloc(&d_status, 8) != cudaSuccess) {
+        cudaMalloc(&d_part, part_floats * 4) != cudaSuccess || cudaMalloc(&d_status, 8) != cudaSuccess) {
         rc = bfail("gdn_b200 batch: test allocation failed");
     } else {
         cudaMemcpy(d_img, img.data(), img.size(), cudaMemcpyHostToDevice);
         cudaMemcpy(d_act, act.data(), act.size(), cudaMemcpyHostToDevice);
-        cudaMemset(d_cnt, 0, (size_t)mx.mtiles() * 4);
         cudaMemset(d_status, 0, 8);
-        cudaMemset(d_y, 0, (size_t)n * m * 4);
         GemmParams p;
         memset(&p, 0, sizeof(p));
         p.a = d_img;
         p.b = d_act;
-        p.m = m;
         p.kblocks = mx.kblocks();
         p.mtiles = mx.mtiles();
         p.npad = npad;
-        p.nvalid = n;
         gemm_slots(npad, &p.a_slots, &p.b_slots);
         p.partial = d_part;
         p.max_local = max_local;
-        p.counters = d_cnt;
-        p.epi = kEpiStore;
-        p.out = d_y;
-        p.out_stride = m;
         p.status = d_status;
+        std::vector<float> part(part_floats);
         cudaError_t e = launch_gemm(p, grid, nullptr);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         uint32_t st[2] = {0, 0};
         if (e == cudaSuccess) e = cudaMemcpy(st, d_status, 8, cudaMemcpyDeviceToHost);
-        if (e == cudaSuccess) e = cudaMemcpy(y, d_y, (size_t)n * m * 4, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(part.data(), d_part, part_floats * 4, cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) rc = bfail("gdn_b200 batch: test GEMM failed: %s", cudaGetErrorString(e));
         else if (st[0] != 0) rc = bfail("gdn_b200 batch: test GEMM reported error %u at CTA %u", st[0], st[1]);
+        else {
+            /* the consumers' sum: segments of a tile in k order */
+            const uint32_t units = mx.mtiles() * mx.kblocks(), KB = mx.kblocks();
+            for (uint32_t row = 0; row < m; ++row) {
+                const uint32_t t = row / kTileM, r = row % kTileM;
+                const uint32_t cf = unit_owner(t * KB, units, grid), cl = unit_owner(t * KB + KB - 1, units, grid);
+                for (uint32_t s = 0; s < n; ++s) {
+                    float acc = 0.0f;
+                    for (uint32_t cc = cf; cc <= cl; ++cc) {
+                        const uint32_t lc = t - unit_start(cc, units, grid) / KB;
+                        const float v = part[((size_t)cc * max_local + lc) * npad * kTileM + (size_t)s * kTileM + r];
+                        acc = cc == cf ? v : acc + v;
+                    }
+                    y[(size_t)s * m + row] = acc;
+                }
+            }
+        }
     }
     cudaFree(d_img);
     cudaFree(d_act);
-    cudaFree(d_y);
     cudaFree(d_part);
-    cudaFree(d_cnt);
     cudaFree(d_status);
     return rc;
 }

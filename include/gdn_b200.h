@@ -147,7 +147,7 @@ int gdn_b200_grid_size(void);
  * Functions return 0 / -1 (gdn_b200_last_error) unless stated. */
 typedef struct GdnB200Batch GdnB200Batch;
 
-/* NULL on error. streams: 1 .. 1024 (processed in passes of 128). */
+/* NULL on error. streams: 1 .. 1024 (processed in passes of 80). */
 GdnB200Batch *gdn_b200_batch_create(const GDNModel *model, uint32_t streams);
 void gdn_b200_batch_free(GdnB200Batch *batch);
 /* Kernel launches in one step (the step is one CUDA graph replay). */
@@ -174,7 +174,7 @@ int gdn_b200_batch_decode_tokens(GdnB200Batch *batch, const int32_t *tokens, uin
 int gdn_b200_batch_fetch_logits(GdnB200Batch *batch, float *logits);
 /* Test hook: y[n][m] = sum_k w[m][k] x[n][k] through one tensor-core tile-GEMM
  * launch (w BF16-exact FP32 words, x FP32 entering as three BF16 terms;
- * k a multiple of 64, n <= 128). */
+ * k a multiple of 64, n <= 80). */
 int gdn_b200_test_tile_gemm(uint32_t m, uint32_t k, uint32_t n, const float *w, const float *x, float *y);
 
 #ifdef __cplusplus
