@@ -492,19 +492,31 @@ __device__ __forceinline__ void psum8(const Partials &v, uint32_t s, uint32_t ro
     }
 }
 
-/* RMSNorm of the residual of stream blockIdx.x (c_impl/gdn_model.cpp:1394-1476):
- * sums of squares per 8 elements, then per 16-element half, the halves summed
- * in order; scale = 1/sqrtf(sum/H + eps); out = (x * scale) * w, written as the
- * activation tiles of the next projection. Mode 0 (layer 0) loads the residual
- * with the token's embedding row (:3719-3731); mode 1 first adds the sums of
- * the previous projection (the residual add of :3351-3452, :3836-3842). */
+/* RMSNorm of the residual of stream blockIdx.x (c_impl/gdn_model.cpp:1394-1476
+ * in the FP32 contract): scale = 1/sqrtf(sum(x^2)/H + eps), out = (x * scale)
+ * * w, written as the activation tiles of the next projection. Mode 0 (layer 0)
+ * loads the residual with the token's embedding row (:3719-3731); mode 1
+ * first adds the sums of the previous projection (the residual add of
+ * :3351-3452, :3836-3842). Each thread keeps its (at most two) 8-element
+ * chunks in registers; every load is issued before the first dependent use. */
 __global__ void __launch_bounds__(256) input_kernel(const StepParams p, const float *__restrict__ norm_w, int mode,
                                                     const Partials add, TileOut out) {
-    __shared__ float chunk_sum[512];
-    __shared__ float scale_s;
+    __shared__ float wsum[8];
     pdl_trigger();
+    const uint32_t s = blockIdx.x, H = p.hidden, t = threadIdx.x, nch = H / 8;
+    /* the norm weights do not depend on the previous kernel */
+    float w[2][8];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint32_t c8 = t + 256 * r;
+        if (c8 < nch) {
+            const float4 w0 = reinterpret_cast<const float4 *>(norm_w)[2 * c8];
+            const float4 w1 = reinterpret_cast<const float4 *>(norm_w)[2 * c8 + 1];
+            w[r][0] = w0.x; w[r][1] = w0.y; w[r][2] = w0.z; w[r][3] = w0.w;
+            w[r][4] = w1.x; w[r][5] = w1.y; w[r][6] = w1.z; w[r][7] = w1.w;
+        }
+    }
     pdl_wait();
-    const uint32_t s = blockIdx.x, H = p.hidden, t = threadIdx.x;
     float *x = p.resid + (size_t)s * H;
     int32_t tok = 0;
     if (mode == 0) {
@@ -516,49 +528,55 @@ __global__ void __launch_bounds__(256) input_kernel(const StepParams p, const fl
             tok = 0;
         }
     }
-    float v[8];
-    for (uint32_t c8 = t; c8 < H / 8; c8 += 256) {
+    float v[2][8];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint32_t c8 = t + 256 * r;
+        if (c8 >= nch) continue;
         if (mode == 0) {
             const uint4 e = *reinterpret_cast<const uint4 *>(p.emb + (size_t)tok * H + c8 * 8);
-            const uint32_t w[4] = {e.x, e.y, e.z, e.w};
+            const uint32_t ew[4] = {e.x, e.y, e.z, e.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                v[2 * i] = __uint_as_float(w[i] << 16);
-                v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+                v[r][2 * i] = __uint_as_float(ew[i] << 16);
+                v[r][2 * i + 1] = __uint_as_float(ew[i] & 0xFFFF0000u);
             }
         } else {
-            float y[8];
-            psum8(add, s, c8 * 8, y);
             const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(x) + 2 * c8);
             const float4 a1 = __ldcg(reinterpret_cast<const float4 *>(x) + 2 * c8 + 1);
+            float y[8];
+            psum8(add, s, c8 * 8, y);
             const float xa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(xa[i], y[i]);
+            for (int i = 0; i < 8; ++i) v[r][i] = __fadd_rn(xa[i], y[i]);
         }
-        reinterpret_cast<float4 *>(x)[2 * c8] = make_float4(v[0], v[1], v[2], v[3]);
-        reinterpret_cast<float4 *>(x)[2 * c8 + 1] = make_float4(v[4], v[5], v[6], v[7]);
-        float acc = 0.0f;
+        reinterpret_cast<float4 *>(x)[2 * c8] = make_float4(v[r][0], v[r][1], v[r][2], v[r][3]);
+        reinterpret_cast<float4 *>(x)[2 * c8 + 1] = make_float4(v[r][4], v[r][5], v[r][6], v[r][7]);
+    }
+    float acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(v[i], v[i]));
-        chunk_sum[c8] = acc;
-    }
+    for (int r = 0; r < 2; ++r)
+        if (t + 256 * r < nch) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(v[r][i], v[r][i]));
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    if ((t & 31) == 0) wsum[t >> 5] = acc;
     __syncthreads();
-    if (t == 0) {
-        float sum = 0.0f;
-        for (uint32_t hf = 0; hf < H / 16; ++hf) sum = __fadd_rn(sum, __fadd_rn(chunk_sum[2 * hf], chunk_sum[2 * hf + 1]));
-        scale_s = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(sum, (float)H), p.eps)));
-    }
-    __syncthreads();
-    const float scale = scale_s;
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum = __fadd_rn(sum, wsum[i]);
+    const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(sum, (float)H), p.eps)));
     uint32_t n, npad;
     uint8_t *tiles = pass_tiles(out, s, n, npad);
-    for (uint32_t c8 = t; c8 < H / 8; c8 += 256) {
-        const float4 a0 = __ldcg(reinterpret_cast<const float4 *>(x) + 2 * c8);
-        const float4 a1 = __ldcg(reinterpret_cast<const float4 *>(x) + 2 * c8 + 1);
-        const float xa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const uint32_t c8 = t + 256 * r;
+        if (c8 >= nch) continue;
         float o[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(xa[i], scale), norm_w[c8 * 8 + i]);
+        for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(v[r][i], scale), w[r][i]);
         put_act8(tiles, npad, n, c8 * 8, o);
     }
 }
@@ -613,19 +631,20 @@ __global__ void __launch_bounds__(128) prep_kernel(const StepParams p, uint32_t 
         float *dst = kind == 0 ? qs + (t & 31) * 8 : (kind == 1 ? ks + (t & 31) * 8 : out + 4 + 512 + (t & 31) * 8);
 #pragma unroll
         for (int i = 0; i < 8; ++i) dst[i] = o[i];
-    } else if (t == 96) {
-        float ya[8], yb[8];
-        psum8(qkv, s, 4 * H + (h & ~7u), ya);
-        psum8(qkv, s, 4 * H + ((nh + h) & ~7u), yb);
-        float av = 0.0f, bv = 0.0f;
+    } else if (t == 96 || t == 97) {
+        /* a (t = 96) and b (t = 97) of the head */
+        const uint32_t row = t == 96 ? h : nh + h;
+        float y8[8];
+        psum8(qkv, s, 4 * H + (row & ~7u), y8);
+        float yv = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            av = ((uint32_t)i == (h & 7u)) ? ya[i] : av;
-            bv = ((uint32_t)i == ((nh + h) & 7u)) ? yb[i] : bv;
+        for (int i = 0; i < 8; ++i) yv = ((uint32_t)i == (row & 7u)) ? y8[i] : yv;
+        if (t == 97) {
+            scal[0] = sigmoid_ref(yv);
+        } else {
+            const float *a_log = aux + 14 * H + 256, *dt_bias = a_log + nh;
+            scal[1] = expf(__fmul_rn(-expf(a_log[h]), softplus_ref(__fadd_rn(yv, dt_bias[h]))));
         }
-        const float *a_log = aux + 14 * H + 256, *dt_bias = a_log + nh;
-        scal[0] = sigmoid_ref(bv);
-        scal[1] = expf(__fmul_rn(-expf(a_log[h]), softplus_ref(__fadd_rn(av, dt_bias[h]))));
     }
     __syncthreads();
     /* tree256: thread t holds elements 2t, 2t+1 (first level), the warp
@@ -727,6 +746,173 @@ __global__ void __launch_bounds__(256) recur_kernel(const StepParams p, uint32_t
         n1.w = __fadd_rn(__fmul_rn(decay, a1[i].w), __fmul_rn(k1.w, delta));
         __stcs(reinterpret_cast<float4 *>(S + (size_t)i * 256) + lane, n0);
         __stcs(reinterpret_cast<float4 *>(S + (size_t)i * 256) + 32 + lane, n1);
+    }
+}
+
+/* One head of one stream, layer l, in one CTA: the recurrence's inputs (as
+ * prep_kernel: conv + SiLU with the tail update, L2 norms, alpha, beta,
+ * decay), the gated delta rule over all 256 state columns (as recur_kernel),
+ * and the output RMSNorm x swish gate (as gate_norm_kernel) written as the O
+ * projection's activation tiles. Warp w owns columns 32w .. 32w+31 in eight
+ * double-buffered batches of four; the first batch is loaded before waiting
+ * for the QKVGAB projection, so its latency overlaps the prologue. */
+__global__ void __launch_bounds__(256, 2) head_kernel(const StepParams p, uint32_t layer, const Partials qkv,
+                                                      TileOut out) {
+    __shared__ __align__(16) float qs[256], ks[256], vs[256], os[256];
+    __shared__ float red[3][8];
+    __shared__ float scal[2];
+    pdl_trigger();
+    const uint32_t nh = p.heads, H = p.hidden;
+    const uint32_t h = blockIdx.x % nh, s = blockIdx.x / nh, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float *S = p.state + (size_t)s * p.state_stride + (((size_t)layer * nh + h) * 256 + warp * 32) * 256;
+    /* columns in batches of four, double-buffered: batch b + 1 is in flight
+     * while batch b is computed; batch 0 before waiting for the projection */
+    constexpr int kB = 4;
+    float4 a0[kB], a1[kB], c0[kB], c1[kB];
+#pragma unroll
+    for (int i = 0; i < kB; ++i) {
+        a0[i] = __ldcg(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + lane);
+        a1[i] = __ldcg(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + 32 + lane);
+    }
+    pdl_wait();
+    const float *aux = p.aux + (size_t)layer * p.aux_stride;
+    if (t < 96) {
+        const uint32_t kind = t >> 5, ch = h * 256 + (t & 31) * 8;
+        float y[8], o[8];
+        psum8(qkv, s, kind * H + ch, y);
+        const uint32_t par = __ldcg(p.tails_parity);
+        const size_t toff = (size_t)s * p.tails_stride + ((size_t)layer * 3 + kind) * 3 * H + ch;
+        conv8(p.tails + par * p.tails_buf + toff, p.tails + (par ^ 1u) * p.tails_buf + toff, H,
+              aux + 2 * H + 256 + ((size_t)kind * H + ch) * 4, y, true, o);
+        float *dst = (kind == 0 ? qs : (kind == 1 ? ks : vs)) + (t & 31) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = o[i];
+    } else if (t == 96 || t == 97) {
+        const uint32_t row = t == 96 ? h : nh + h;
+        float y8[8];
+        psum8(qkv, s, 4 * H + (row & ~7u), y8);
+        float yv = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) yv = ((uint32_t)i == (row & 7u)) ? y8[i] : yv;
+        if (t == 97) {
+            scal[0] = sigmoid_ref(yv);
+        } else {
+            const float *a_log = aux + 14 * H + 256, *dt_bias = a_log + nh;
+            scal[1] = expf(__fmul_rn(-expf(a_log[h]), softplus_ref(__fadd_rn(yv, dt_bias[h]))));
+        }
+    }
+    __syncthreads();
+    /* tree256 of q^2, k^2 (threads 0-127 hold pairs), then of qn . kn */
+    if (t < 128) {
+        const float2 q2 = reinterpret_cast<const float2 *>(qs)[t], k2 = reinterpret_cast<const float2 *>(ks)[t];
+        float sq = __fadd_rn(__fmul_rn(q2.x, q2.x), __fmul_rn(q2.y, q2.y));
+        float sk = __fadd_rn(__fmul_rn(k2.x, k2.x), __fmul_rn(k2.y, k2.y));
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+            sk = __fadd_rn(sk, __shfl_xor_sync(0xffffffffu, sk, o));
+        }
+        if (lane == 0) {
+            red[0][warp] = sq;
+            red[1][warp] = sk;
+        }
+    }
+    __syncthreads();
+    const float q_inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fadd_rn(__fadd_rn(red[0][0], red[0][1]),
+                                                                  __fadd_rn(red[0][2], red[0][3])), 1e-6f)));
+    const float k_inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fadd_rn(__fadd_rn(red[1][0], red[1][1]),
+                                                                  __fadd_rn(red[1][2], red[1][3])), 1e-6f)));
+    if (t < 128) {
+        const float2 q2 = reinterpret_cast<const float2 *>(qs)[t], k2 = reinterpret_cast<const float2 *>(ks)[t];
+        const float2 qn = make_float2(__fmul_rn(q2.x, q_inv), __fmul_rn(q2.y, q_inv));
+        const float2 kn = make_float2(__fmul_rn(k2.x, k_inv), __fmul_rn(k2.y, k_inv));
+        float a = __fadd_rn(__fmul_rn(qn.x, kn.x), __fmul_rn(qn.y, kn.y));
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane == 0) red[2][warp] = a;
+    }
+    __syncthreads();  /* every q_inv / k_inv read is done before qs / ks are overwritten */
+    if (t < 128) {
+        const float2 q2 = reinterpret_cast<const float2 *>(qs)[t], k2 = reinterpret_cast<const float2 *>(ks)[t];
+        reinterpret_cast<float2 *>(qs)[t] = make_float2(__fmul_rn(q2.x, q_inv), __fmul_rn(q2.y, q_inv));
+        reinterpret_cast<float2 *>(ks)[t] = make_float2(__fmul_rn(k2.x, k_inv), __fmul_rn(k2.y, k_inv));
+    }
+    __syncthreads();
+    const float alpha = __fadd_rn(__fadd_rn(red[2][0], red[2][1]), __fadd_rn(red[2][2], red[2][3]));
+    const float beta = scal[0], decay = scal[1];
+    const float4 k0 = reinterpret_cast<const float4 *>(ks)[lane], k1 = reinterpret_cast<const float4 *>(ks)[32 + lane];
+    const float4 q0 = reinterpret_cast<const float4 *>(qs)[lane], q1 = reinterpret_cast<const float4 *>(qs)[32 + lane];
+#pragma unroll 1
+    for (int b = 0; b < 32 / kB; ++b) {
+        float *Sb = S + (size_t)b * kB * 256;
+        if (b + 1 < 32 / kB) {
+#pragma unroll
+            for (int i = 0; i < kB; ++i) {
+                c0[i] = __ldcg(reinterpret_cast<const float4 *>(Sb + (size_t)(kB + i) * 256) + lane);
+                c1[i] = __ldcg(reinterpret_cast<const float4 *>(Sb + (size_t)(kB + i) * 256) + 32 + lane);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kB; ++i) {
+            float r = __fmul_rn(a0[i].x, k0.x), pp = __fmul_rn(a0[i].x, q0.x);
+            r = __fadd_rn(r, __fmul_rn(a0[i].y, k0.y)); pp = __fadd_rn(pp, __fmul_rn(a0[i].y, q0.y));
+            r = __fadd_rn(r, __fmul_rn(a0[i].z, k0.z)); pp = __fadd_rn(pp, __fmul_rn(a0[i].z, q0.z));
+            r = __fadd_rn(r, __fmul_rn(a0[i].w, k0.w)); pp = __fadd_rn(pp, __fmul_rn(a0[i].w, q0.w));
+            r = __fadd_rn(r, __fmul_rn(a1[i].x, k1.x)); pp = __fadd_rn(pp, __fmul_rn(a1[i].x, q1.x));
+            r = __fadd_rn(r, __fmul_rn(a1[i].y, k1.y)); pp = __fadd_rn(pp, __fmul_rn(a1[i].y, q1.y));
+            r = __fadd_rn(r, __fmul_rn(a1[i].z, k1.z)); pp = __fadd_rn(pp, __fmul_rn(a1[i].z, q1.z));
+            r = __fadd_rn(r, __fmul_rn(a1[i].w, k1.w)); pp = __fadd_rn(pp, __fmul_rn(a1[i].w, q1.w));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, o));
+                pp = __fadd_rn(pp, __shfl_xor_sync(0xffffffffu, pp, o));
+            }
+            const uint32_t col = warp * 32 + b * kB + i;
+            const float delta = __fmul_rn(beta, __fsub_rn(vs[col], __fmul_rn(decay, r)));
+            if (lane == 0) os[col] = __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pp), __fmul_rn(alpha, delta)));
+            float4 n0, n1;
+            n0.x = __fadd_rn(__fmul_rn(decay, a0[i].x), __fmul_rn(k0.x, delta));
+            n0.y = __fadd_rn(__fmul_rn(decay, a0[i].y), __fmul_rn(k0.y, delta));
+            n0.z = __fadd_rn(__fmul_rn(decay, a0[i].z), __fmul_rn(k0.z, delta));
+            n0.w = __fadd_rn(__fmul_rn(decay, a0[i].w), __fmul_rn(k0.w, delta));
+            n1.x = __fadd_rn(__fmul_rn(decay, a1[i].x), __fmul_rn(k1.x, delta));
+            n1.y = __fadd_rn(__fmul_rn(decay, a1[i].y), __fmul_rn(k1.y, delta));
+            n1.z = __fadd_rn(__fmul_rn(decay, a1[i].z), __fmul_rn(k1.z, delta));
+            n1.w = __fadd_rn(__fmul_rn(decay, a1[i].w), __fmul_rn(k1.w, delta));
+            __stcs(reinterpret_cast<float4 *>(Sb + (size_t)i * 256) + lane, n0);
+            __stcs(reinterpret_cast<float4 *>(Sb + (size_t)i * 256) + 32 + lane, n1);
+        }
+#pragma unroll
+        for (int i = 0; i < kB; ++i) {
+            a0[i] = c0[i];
+            a1[i] = c1[i];
+        }
+    }
+    __syncthreads();
+    /* output RMSNorm x swish gate (:3226-3349), warp 0: 8 elements per lane */
+    if (warp == 0) {
+        const float4 o0 = reinterpret_cast<const float4 *>(os)[2 * lane], o1 = reinterpret_cast<const float4 *>(os)[2 * lane + 1];
+        const float av[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+        float g[8];
+        psum8(qkv, s, 3 * H + h * 256 + lane * 8, g);
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = __fadd_rn(acc, __fmul_rn(av[i], av[i]));
+        const float half = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+        float sum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, half, 2 * j));
+        const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(sum, 256.0f), p.eps)));
+        const float *w = aux + H + lane * 8; /* o_norm */
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float nrm = __fmul_rn(__fmul_rn(av[i], scale), w[i]);
+            v[i] = __fmul_rn(__fmul_rn(nrm, g[i]), sigmoid_ref(g[i]));
+        }
+        uint32_t n, npad;
+        uint8_t *tiles = pass_tiles(out, s, n, npad);
+        put_act8(tiles, npad, n, h * 256 + lane * 8, v);
     }
 }
 
@@ -918,6 +1104,10 @@ cudaError_t launch_recur(const StepParams &p, uint32_t layer, const Partials &qk
 }
 
 size_t prep_floats(uint32_t streams, uint32_t heads) { return (size_t)streams * heads * kPrepFloats; }
+
+cudaError_t launch_head(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out, cudaStream_t stream) {
+    return launch_pdl(head_kernel, p.streams * p.heads, 256, 0, stream, p, layer, qkv, out);
+}
 
 cudaError_t launch_gate_norm(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out,
                              cudaStream_t stream) {

@@ -144,6 +144,9 @@ cudaError_t launch_input(const StepParams &p, const float *norm_w, int mode, con
  * the recurrence of layer l; prep holds prep_floats() floats */
 cudaError_t launch_recur(const StepParams &p, uint32_t layer, const Partials &qkv, float *prep, cudaStream_t stream);
 size_t prep_floats(uint32_t streams, uint32_t heads);
+/* prep, recurrence and output norm x swish gate of layer l in one kernel per
+ * (stream, head); writes the O projection's activation tiles (K = H) */
+cudaError_t launch_head(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out, cudaStream_t stream);
 /* output norm x swish gate as activation tiles (K = H) */
 cudaError_t launch_gate_norm(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out,
                              cudaStream_t stream);

@@ -337,9 +337,8 @@ int enqueue_step(GdnB200Batch *b, int greedy, uint32_t *launches) {
         const uint8_t *w = tm->img + (size_t)l * tm->layer_bytes;
         const float *aux = tm->aux + (size_t)l * tm->aux_stride;
         if (gemm_all(b, tm->qkv, w + tm->qkv.off, b->xb, b->xb_stride, &qkv, launches)) return -1;
-        BT_OK(launch_recur(sp, l, qkv, b->prep, b->stream));
-        BT_OK(launch_gate_norm(sp, l, qkv, xo, b->stream));
-        *launches += 3;
+        BT_OK(launch_head(sp, l, qkv, xo, b->stream));
+        ++*launches;
         if (gemm_all(b, tm->o, w + tm->o.off, b->xb, b->xb_stride, &o, launches)) return -1;
         BT_OK(launch_input(sp, aux + H + 256, 1, o, xo, b->stream));
         ++*launches;
