@@ -263,7 +263,8 @@ def run_streams(args):
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
 
-    model = gdn.Model(header=gdn.make_header(**SHAPE), seed=SEED)
+    shape = dict(SHAPE, layers=args.layers)
+    model = gdn.Model(header=gdn.make_header(**shape), seed=SEED)
     batch = gdn.Batch(model, per_rank)
     V = SHAPE["vocab"]
     ids = rank_streams(rank, world, per_rank)
@@ -292,7 +293,7 @@ def run_streams(args):
     ms_step = dev_ms / args.steps
     value = args.streams * args.steps / (dev_ms / 1000.0)
     e2e_value = args.streams * e2e_n / e2e_s
-    alg = step_bytes_streams(per_rank)
+    alg = step_bytes_streams(per_rank, shape)
     peak, peak_kind = peaks()
     achieved = alg / (ms_step / 1000.0) / 1e9
     line = {
@@ -302,7 +303,8 @@ def run_streams(args):
         "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"BASELINE config[3]: {args.streams} independent GDN-1.3B streams from zero fp32 "
                                "state, seeded uniform teacher-forced tokens per stream, sharded over the GPUs",
-                   "streams": args.streams, "streams_per_gpu": per_rank, "state": "fp32", "boundaries": "fp32",
+                   "streams": args.streams, "streams_per_gpu": per_rank, "layers": args.layers,
+                   "state": "fp32", "boundaries": "fp32",
                    "projections": "tcgen05 tile GEMM, activations as three BF16 terms, FP32 accumulation",
                    "l2": "no flush: 2.8 GB of weights plus the streams' state per step exceed the 126 MB L2",
                    "parallelism": f"stream-dp{world}"},
@@ -339,6 +341,8 @@ def main():
                     help="decode: the headline batch-1 decode (default); delta_rule: BASELINE config[1]; "
                          "streams: BASELINE config[3] multi-stream decode")
     ap.add_argument("--streams", type=int, default=64, help="total streams of --workload streams")
+    ap.add_argument("--layers", type=int, default=SHAPE["layers"],
+                    help="--workload streams only: fewer layers for a small profiling case (same per-layer shapes)")
     args = ap.parse_args()
     if args.workload == "delta_rule" and args.impl == "b200":
         return run_delta_rule(args)

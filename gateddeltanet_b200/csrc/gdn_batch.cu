@@ -753,27 +753,41 @@ __global__ void __launch_bounds__(256) recur_kernel(const StepParams p, uint32_t
  * prep_kernel: conv + SiLU with the tail update, L2 norms, alpha, beta,
  * decay), the gated delta rule over all 256 state columns (as recur_kernel),
  * and the output RMSNorm x swish gate (as gate_norm_kernel) written as the O
- * projection's activation tiles. Warp w owns columns 32w .. 32w+31 in eight
- * double-buffered batches of four; the first batch is loaded before waiting
- * for the QKVGAB projection, so its latency overlaps the prologue. */
+ * projection's activation tiles. Warp w owns columns 32w .. 32w+31 (32 KB,
+ * contiguous) and streams them through its own three-slot shared-memory ring
+ * of 4-column bulk copies (4 KB); the first three copies are issued before
+ * the kernel waits for the QKVGAB projection, so they overlap the prologue.
+ * Every ring wait is bounded (2 s) and reports through the status word. */
+constexpr int kHeadCols = 4;                      /* columns per copy */
+constexpr int kHeadSlots = 3;                     /* copies in flight per warp */
+constexpr uint32_t kHeadSlotBytes = kHeadCols * 1024u;
+constexpr size_t kHeadSmem = 8 * kHeadSlots * kHeadSlotBytes + 8 * kHeadSlots * 8 + 4 * 256 * 4 + 64;
 __global__ void __launch_bounds__(256, 2) head_kernel(const StepParams p, uint32_t layer, const Partials qkv,
                                                       TileOut out) {
-    __shared__ __align__(16) float qs[256], ks[256], vs[256], os[256];
-    __shared__ float red[3][8];
-    __shared__ float scal[2];
+    extern __shared__ __align__(128) uint8_t hsm[];
+    float *ring = reinterpret_cast<float *>(hsm);                                   /* [8 warps][slots][4][256] */
+    uint64_t *bars = reinterpret_cast<uint64_t *>(hsm + 8 * kHeadSlots * kHeadSlotBytes);  /* [8][slots] */
+    float *qs = reinterpret_cast<float *>(hsm + 8 * kHeadSlots * kHeadSlotBytes + 8 * kHeadSlots * 8);
+    float *ks = qs + 256, *vs = ks + 256, *os = vs + 256;
+    float *red = os + 256;  /* [3][4] + 2 */
+    float *scal = red + 12;
     pdl_trigger();
     const uint32_t nh = p.heads, H = p.hidden;
     const uint32_t h = blockIdx.x % nh, s = blockIdx.x / nh, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     float *S = p.state + (size_t)s * p.state_stride + (((size_t)layer * nh + h) * 256 + warp * 32) * 256;
-    /* columns in batches of four, double-buffered: batch b + 1 is in flight
-     * while batch b is computed; batch 0 before waiting for the projection */
-    constexpr int kB = 4;
-    float4 a0[kB], a1[kB], c0[kB], c1[kB];
-#pragma unroll
-    for (int i = 0; i < kB; ++i) {
-        a0[i] = __ldcg(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + lane);
-        a1[i] = __ldcg(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + 32 + lane);
+    float *wring = ring + (size_t)warp * kHeadSlots * kHeadCols * 256;
+    const uint32_t wbar = smem_u32(bars + warp * kHeadSlots);
+    if (lane == 0) {
+        for (int i = 0; i < kHeadSlots; ++i) mbar_init(wbar + 8 * i, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        /* S was last written by this layer's recurrence one step earlier */
+        for (int i = 0; i < kHeadSlots; ++i) {
+            mbar_expect_tx(wbar + 8 * i, kHeadSlotBytes);
+            bulk_g2s(smem_u32(wring + (size_t)i * kHeadCols * 256), S + (size_t)i * kHeadCols * 256, kHeadSlotBytes,
+                     wbar + 8 * i, policy_evict_first());
+        }
     }
+    __syncwarp();
     pdl_wait();
     const float *aux = p.aux + (size_t)layer * p.aux_stride;
     if (t < 96) {
@@ -813,15 +827,15 @@ __global__ void __launch_bounds__(256, 2) head_kernel(const StepParams p, uint32
             sk = __fadd_rn(sk, __shfl_xor_sync(0xffffffffu, sk, o));
         }
         if (lane == 0) {
-            red[0][warp] = sq;
-            red[1][warp] = sk;
+            red[warp] = sq;
+            red[4 + warp] = sk;
         }
     }
     __syncthreads();
-    const float q_inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fadd_rn(__fadd_rn(red[0][0], red[0][1]),
-                                                                  __fadd_rn(red[0][2], red[0][3])), 1e-6f)));
-    const float k_inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fadd_rn(__fadd_rn(red[1][0], red[1][1]),
-                                                                  __fadd_rn(red[1][2], red[1][3])), 1e-6f)));
+    const float q_inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3])),
+                                                        1e-6f)));
+    const float k_inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fadd_rn(__fadd_rn(red[4], red[5]), __fadd_rn(red[6], red[7])),
+                                                        1e-6f)));
     if (t < 128) {
         const float2 q2 = reinterpret_cast<const float2 *>(qs)[t], k2 = reinterpret_cast<const float2 *>(ks)[t];
         const float2 qn = make_float2(__fmul_rn(q2.x, q_inv), __fmul_rn(q2.y, q_inv));
@@ -829,7 +843,7 @@ __global__ void __launch_bounds__(256, 2) head_kernel(const StepParams p, uint32
         float a = __fadd_rn(__fmul_rn(qn.x, kn.x), __fmul_rn(qn.y, kn.y));
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-        if (lane == 0) red[2][warp] = a;
+        if (lane == 0) red[8 + warp] = a;
     }
     __syncthreads();  /* every q_inv / k_inv read is done before qs / ks are overwritten */
     if (t < 128) {
@@ -838,22 +852,36 @@ __global__ void __launch_bounds__(256, 2) head_kernel(const StepParams p, uint32
         reinterpret_cast<float2 *>(ks)[t] = make_float2(__fmul_rn(k2.x, k_inv), __fmul_rn(k2.y, k_inv));
     }
     __syncthreads();
-    const float alpha = __fadd_rn(__fadd_rn(red[2][0], red[2][1]), __fadd_rn(red[2][2], red[2][3]));
+    const float alpha = __fadd_rn(__fadd_rn(red[8], red[9]), __fadd_rn(red[10], red[11]));
     const float beta = scal[0], decay = scal[1];
     const float4 k0 = reinterpret_cast<const float4 *>(ks)[lane], k1 = reinterpret_cast<const float4 *>(ks)[32 + lane];
     const float4 q0 = reinterpret_cast<const float4 *>(qs)[lane], q1 = reinterpret_cast<const float4 *>(qs)[32 + lane];
+    bool ok = true;
 #pragma unroll 1
-    for (int b = 0; b < 32 / kB; ++b) {
-        float *Sb = S + (size_t)b * kB * 256;
-        if (b + 1 < 32 / kB) {
-#pragma unroll
-            for (int i = 0; i < kB; ++i) {
-                c0[i] = __ldcg(reinterpret_cast<const float4 *>(Sb + (size_t)(kB + i) * 256) + lane);
-                c1[i] = __ldcg(reinterpret_cast<const float4 *>(Sb + (size_t)(kB + i) * 256) + 32 + lane);
+    for (int b = 0; b < 32 / kHeadCols; ++b) {
+        const int sl = b % kHeadSlots;
+        /* bounded wait for the batch; the warp agrees on the outcome */
+        bool got = mbar_try(wbar + 8 * sl, (b / kHeadSlots) & 1);
+        if (!got) {
+            const uint64_t t0 = gtimer();
+            while (!(got = mbar_try(wbar + 8 * sl, (b / kHeadSlots) & 1)) && gtimer() - t0 < kWaitNs) {
             }
         }
+        if (!__all_sync(0xffffffffu, got)) {
+            if (lane == 0) report(p.status, kErrWaitA, blockIdx.x);
+            ok = false;
+            break;
+        }
+        const float *src = wring + (size_t)sl * kHeadCols * 256;
+        float4 a0[kHeadCols], a1[kHeadCols];
 #pragma unroll
-        for (int i = 0; i < kB; ++i) {
+        for (int i = 0; i < kHeadCols; ++i) {
+            a0[i] = reinterpret_cast<const float4 *>(src + (size_t)i * 256)[lane];
+            a1[i] = reinterpret_cast<const float4 *>(src + (size_t)i * 256)[32 + lane];
+        }
+        float *Sb = S + (size_t)b * kHeadCols * 256;
+#pragma unroll
+        for (int i = 0; i < kHeadCols; ++i) {
             float r = __fmul_rn(a0[i].x, k0.x), pp = __fmul_rn(a0[i].x, q0.x);
             r = __fadd_rn(r, __fmul_rn(a0[i].y, k0.y)); pp = __fadd_rn(pp, __fmul_rn(a0[i].y, q0.y));
             r = __fadd_rn(r, __fmul_rn(a0[i].z, k0.z)); pp = __fadd_rn(pp, __fmul_rn(a0[i].z, q0.z));
@@ -867,7 +895,7 @@ __global__ void __launch_bounds__(256, 2) head_kernel(const StepParams p, uint32
                 r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, o));
                 pp = __fadd_rn(pp, __shfl_xor_sync(0xffffffffu, pp, o));
             }
-            const uint32_t col = warp * 32 + b * kB + i;
+            const uint32_t col = warp * 32 + b * kHeadCols + i;
             const float delta = __fmul_rn(beta, __fsub_rn(vs[col], __fmul_rn(decay, r)));
             if (lane == 0) os[col] = __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pp), __fmul_rn(alpha, delta)));
             float4 n0, n1;
@@ -882,10 +910,21 @@ __global__ void __launch_bounds__(256, 2) head_kernel(const StepParams p, uint32
             __stcs(reinterpret_cast<float4 *>(Sb + (size_t)i * 256) + lane, n0);
             __stcs(reinterpret_cast<float4 *>(Sb + (size_t)i * 256) + 32 + lane, n1);
         }
-#pragma unroll
-        for (int i = 0; i < kB; ++i) {
-            a0[i] = c0[i];
-            a1[i] = c1[i];
+        /* the slot's data has been used by every lane: refill it with batch b + slots */
+        __syncwarp();
+        if (lane == 0 && b + kHeadSlots < 32 / kHeadCols) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_expect_tx(wbar + 8 * sl, kHeadSlotBytes);
+            bulk_g2s(smem_u32(wring + (size_t)sl * kHeadCols * 256), S + (size_t)(b + kHeadSlots) * kHeadCols * 256,
+                     kHeadSlotBytes, wbar + 8 * sl, policy_evict_first());
+        }
+    }
+    if (!ok && lane == 0) {
+        /* copies issued and not consumed land before the CTA exits */
+        for (int i = 0; i < kHeadSlots; ++i) {
+            const uint64_t t0 = gtimer();
+            while (!mbar_try(wbar + 8 * i, 0) && !mbar_try(wbar + 8 * i, 1) && gtimer() - t0 < kWaitNs) {
+            }
         }
     }
     __syncthreads();
@@ -1106,7 +1145,9 @@ cudaError_t launch_recur(const StepParams &p, uint32_t layer, const Partials &qk
 size_t prep_floats(uint32_t streams, uint32_t heads) { return (size_t)streams * heads * kPrepFloats; }
 
 cudaError_t launch_head(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out, cudaStream_t stream) {
-    return launch_pdl(head_kernel, p.streams * p.heads, 256, 0, stream, p, layer, qkv, out);
+    const cudaError_t e = cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(head_kernel, p.streams * p.heads, 256, kHeadSmem, stream, p, layer, qkv, out);
 }
 
 cudaError_t launch_gate_norm(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out,
