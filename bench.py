@@ -130,6 +130,26 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
+def energy_meter(device: int):
+    """NVML meter of this rank's GPU and its loaded-idle power (1 s), or (None, None)."""
+    try:
+        from gateddeltanet_b200.energy import EnergyMeter
+        m = EnergyMeter(device)
+        return m, m.idle_watts(1.0)
+    except Exception:
+        return None, None
+
+
+def energy_line(window, tokens: int, idle_w):
+    """Energy of the timed window of this rank's GPU (gateddeltanet_b200/energy.py)."""
+    if window is None:
+        return {"unavailable": "NVML energy queries not available"}
+    from gateddeltanet_b200.energy import summarize
+    out = summarize(window, tokens, idle_w)
+    out["scope"] = "rank 0's GPU over the timed decode window (host and server power not included)"
+    return out
+
+
 def cpu_baseline_port(n_tokens: int = 3):
     """Oracle port (reference arithmetic) on all host cores, bounded sample."""
     sys.path.insert(0, os.path.join(REPO, "tests"))
@@ -272,11 +292,15 @@ def run_streams(args):
     toks = np.array([token_stream(i, n_all, V) for i in ids], dtype=np.int32).T.copy()  # [n_all, per_rank]
     if args.warmup:
         batch.decode(toks[:args.warmup])
+    meter, idle_w = energy_meter(local)
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
     barrier()
+    if meter is not None:
+        meter.start()
     _, dev_ms = batch.decode(toks[args.warmup:args.warmup + args.steps])
+    window = meter.stop() if meter is not None else None
     barrier()
     dev_ms = max_over_ranks(dev_ms, device="cuda")
     # e2e: host tokens in, argmax out, every step through gdn_b200_batch_step_host
@@ -317,6 +341,7 @@ def run_streams(args):
                      "kernel": f"whole step ({launches} launches: tile GEMMs, recurrence, norms; one CUDA graph)"},
         "gpu_launches": launches * args.steps,
         "clocks": sampler.summary(),
+        "energy": energy_line(window, per_rank * args.steps, idle_w),
     }
     batch.free()
     model.free()
@@ -387,11 +412,15 @@ def main():
     rs.decode([teacher[i % 4096] for i in range(n_w)]) if n_w else None
     timed = [teacher[(n_w + i) % 4096] for i in range(args.steps)]
 
+    meter, idle_w = energy_meter(local)
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
     barrier()
+    if meter is not None:
+        meter.start()
     picks, kernel_ms = rs.decode(timed)
+    window = meter.stop() if meter is not None else None
     barrier()
     kernel_ms = max_over_ranks(kernel_ms, device="cuda")
 
@@ -435,6 +464,7 @@ def main():
                      "kernel": "gdn_decode_kernel<1> (BF16-boundary contract; one launch per token)"},
         "gpu_launches": args.steps,
         "clocks": sampler.summary(),
+        "energy": energy_line(window, args.steps, idle_w),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:

@@ -174,8 +174,15 @@ def test_batch_rejects_bad_tokens(small):
     b.free()
 
 
+def test_batch_small_long_trajectory(small):
+    """64 steps: the reordered FP32 sums must not drift toward the gate."""
+    model, oracle = small
+    worst = run_against_oracle(model, oracle, streams=2, steps=64, seeded_streams=(0,))
+    print(f"small model, 2 streams x 64 steps: worst logits rel-L2 {worst:.3e}")
+
+
 def test_batch_full_model_matches_oracle(lib):
     model = gdn.Model(header=header_for(ol.FULL_DIMS), seed=SEED)
     oracle = ol.Oracle(ol.FULL_DIMS, seed=SEED)
-    worst = run_against_oracle(model, oracle, streams=2, steps=3, seeded_streams=(1,))
-    print(f"GDN-1.3B, 2 streams x 3 steps: worst logits rel-L2 {worst:.3e}")
+    worst = run_against_oracle(model, oracle, streams=2, steps=8, seeded_streams=(1,))
+    print(f"GDN-1.3B, 2 streams x 8 steps: worst logits rel-L2 {worst:.3e}")
