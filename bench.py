@@ -266,7 +266,7 @@ def run_streams(args):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
-                                timeout=__import__("datetime").timedelta(seconds=600))
+                                timeout=__import__("datetime").timedelta(seconds=120))
     if args.streams % world:
         raise SystemExit("--streams must be a multiple of the GPU count")
     per_rank = args.streams // world
@@ -385,7 +385,7 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
-                                timeout=__import__("datetime").timedelta(seconds=600))
+                                timeout=__import__("datetime").timedelta(seconds=120))
 
     import gateddeltanet_b200 as gdn
     from gateddeltanet_b200 import build
