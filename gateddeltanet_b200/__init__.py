@@ -131,6 +131,8 @@ EXPORTS = [
      [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32, ctypes.c_int,
       ctypes.POINTER(ctypes.c_int32), _FP]),
     ("gdn_b200_batch_fetch_logits", ctypes.c_int, [ctypes.c_void_p, _FP]),
+    ("gdn_b200_prefill", ctypes.c_int,
+     [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32, _FP]),
     ("gdn_b200_test_tile_gemm", ctypes.c_int,
      [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, _FP, _FP, _FP]),
 ]
@@ -265,6 +267,15 @@ class RunState:
                                                       ctypes.byref(ms)),
               "gdn_b200_decode_tokens_noalloc")
         return out, float(ms.value)
+
+    def prefill(self, tokens: Sequence[int]) -> float:
+        """gdn_b200_prefill: advance by the tokens at once (no logits); returns device ms."""
+        tok = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        ms = ctypes.c_float(0.0)
+        check(self.lib.gdn_b200_prefill(ctypes.byref(self.model.m), ctypes.byref(self.s),
+                                        tok.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(tok),
+                                        ctypes.byref(ms)), "gdn_b200_prefill")
+        return float(ms.value)
 
     def trace(self, token: int) -> np.ndarray:
         """One traced step: array [cta, phase, 8] of %globaltimer ns stamps

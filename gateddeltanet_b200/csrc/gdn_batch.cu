@@ -955,6 +955,187 @@ __global__ void __launch_bounds__(256, 2) head_kernel(const StepParams p, uint32
     }
 }
 
+/* Prefill of one head, 64 state columns (block cb), over the ntok tokens of a
+ * chunk, in token order (c_impl/gdn_model.cpp:1543-1660 and :1932-2340 per
+ * token, FP32 contract). The tokens are the "streams" of the chunk's
+ * projections. In sub-chunks of kSub tokens: the raw q, k (all 256 channels of
+ * the head) and v (the block's 64) of every token from the QKVGAB partial
+ * sums, the causal conv over time (window from the run state's tails, then
+ * from the previous tokens), SiLU, L2 norms, alpha, beta, decay -- all in
+ * parallel over tokens; then the recurrence, token by token, on the block's
+ * state held in registers (warp w: columns w*8 .. w*8+7, lane l: k = 4l..4l+3
+ * and 128+4l..128+4l+3). S is read once and written once per chunk. The
+ * window's last three raw rows become the new tails, written to tails_out
+ * (this block's q/k quarter and its v channels) so the four blocks of a head
+ * never race on the tails they read. Layouts of the single-stream run state:
+ * S [L][nh][v][k], tails [L][q,k,v][H][4] (rows 0..2 oldest to newest). */
+constexpr int kSub = 16;
+constexpr int kPrefCh = 576;  /* q 256 | k 256 | v 64 */
+constexpr size_t kPrefillSmem = (size_t)(kSub + 3) * kPrefCh * 4 + (size_t)kSub * kPrefCh * 4 + (size_t)kSub * 4 * 4 + 64;
+__global__ void __launch_bounds__(256, 1) prefill_head_kernel(const StepParams p, uint32_t layer, const Partials qkv,
+                                                              float *state, const float *tails_in, float *tails_out,
+                                                              uint32_t ntok) {
+    extern __shared__ __align__(16) float psm[];
+    float *raw = psm;                                  /* [kSub + 3][576]: rows 0..2 = the three tokens before */
+    float *act = raw + (kSub + 3) * kPrefCh;           /* [kSub][576] */
+    float *sc = act + kSub * kPrefCh;                  /* [kSub][4]: alpha, beta, decay, - */
+    pdl_trigger();
+    pdl_wait();
+    const uint32_t nh = p.heads, H = p.hidden;
+    const uint32_t cb = blockIdx.x & 3u, h = blockIdx.x >> 2;
+    const uint32_t t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const float *aux = p.aux + (size_t)layer * p.aux_stride;
+    auto gch = [&](uint32_t c) -> uint32_t {  /* channel c of the block -> (kind, global channel) */
+        return c < 512 ? h * 256 + (c & 255u) : h * 256 + cb * 64 + (c - 512);
+    };
+    auto kind_of = [](uint32_t c) -> uint32_t { return c < 256 ? 0u : (c < 512 ? 1u : 2u); };
+    float *S = state + ((((size_t)layer * nh + h) * 256) + cb * 64 + warp * 8) * 256;
+    float4 a0[8], a1[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        a0[i] = __ldcg(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + lane);
+        a1[i] = __ldcg(reinterpret_cast<const float4 *>(S + (size_t)i * 256) + 32 + lane);
+    }
+    for (uint32_t c = t; c < (uint32_t)kPrefCh; c += 256) {
+        const uint32_t kind = kind_of(c);
+        const float4 tv = __ldcg(reinterpret_cast<const float4 *>(tails_in) + ((size_t)layer * 3 + kind) * H + gch(c));
+        raw[c] = tv.x;
+        raw[kPrefCh + c] = tv.y;
+        raw[2 * kPrefCh + c] = tv.z;
+    }
+    for (uint32_t j0 = 0; j0 < ntok; j0 += kSub) {
+        const uint32_t nj = min((uint32_t)kSub, ntok - j0);
+        __syncthreads();
+        /* raw projections of the sub-chunk's tokens, and a, b */
+        for (uint32_t idx = t; idx < nj * (kPrefCh / 8); idx += 256) {
+            const uint32_t j = idx / (kPrefCh / 8), c8 = idx % (kPrefCh / 8);
+            const uint32_t c = c8 * 8;
+            float y[8];
+            psum8(qkv, j0 + j, kind_of(c) * H + gch(c), y);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) raw[(3 + j) * kPrefCh + c + i] = y[i];
+        }
+        for (uint32_t idx = t; idx < 2 * nj; idx += 256) {
+            const uint32_t j = idx >> 1, which = idx & 1u;
+            const uint32_t row = which == 0 ? h : nh + h;
+            float y8[8];
+            psum8(qkv, j0 + j, 4 * H + (row & ~7u), y8);
+            float yv = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) yv = ((uint32_t)i == (row & 7u)) ? y8[i] : yv;
+            if (which == 1) {
+                sc[j * 4 + 1] = sigmoid_ref(yv);
+            } else {
+                const float *a_log = aux + 14 * H + 256, *dt_bias = a_log + nh;
+                sc[j * 4 + 2] = expf(__fmul_rn(-expf(a_log[h]), softplus_ref(__fadd_rn(yv, dt_bias[h]))));
+            }
+        }
+        __syncthreads();
+        /* conv over time + SiLU: token j's window is raw rows j .. j+3 */
+        for (uint32_t idx = t; idx < nj * kPrefCh; idx += 256) {
+            const uint32_t j = idx / kPrefCh, c = idx % kPrefCh;
+            const float4 w = reinterpret_cast<const float4 *>(aux + 2 * H + 256)[(size_t)kind_of(c) * H + gch(c)];
+            float sum = __fadd_rn(__fmul_rn(raw[j * kPrefCh + c], w.x), __fmul_rn(raw[(j + 1) * kPrefCh + c], w.y));
+            sum = __fadd_rn(sum, __fmul_rn(raw[(j + 2) * kPrefCh + c], w.z));
+            sum = __fadd_rn(sum, __fmul_rn(raw[(j + 3) * kPrefCh + c], w.w));
+            act[j * kPrefCh + c] = silu_ref(sum);
+        }
+        __syncthreads();
+        /* L2 norms and alpha per token (tree256: 8 per lane, then the butterfly); warp w: tokens w, w + 8 */
+        for (uint32_t j = warp; j < nj; j += 8) {
+            float *q = act + j * kPrefCh, *k = q + 256;
+            float qv[8], kv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                qv[i] = q[lane * 8 + i];
+                kv[i] = k[lane * 8 + i];
+            }
+            auto tree8 = [](const float (&v)[8], bool sq) -> float {
+                float l1[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    l1[i] = sq ? __fadd_rn(__fmul_rn(v[2 * i], v[2 * i]), __fmul_rn(v[2 * i + 1], v[2 * i + 1]))
+                               : __fadd_rn(v[2 * i], v[2 * i + 1]);
+                return __fadd_rn(__fadd_rn(l1[0], l1[1]), __fadd_rn(l1[2], l1[3]));
+            };
+            float sq = tree8(qv, true), sk = tree8(kv, true);
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+                sk = __fadd_rn(sk, __shfl_xor_sync(0xffffffffu, sk, o));
+            }
+            const float qi = __fdiv_rn(1.0f, sqrtf(__fadd_rn(sq, 1e-6f)));
+            const float ki = __fdiv_rn(1.0f, sqrtf(__fadd_rn(sk, 1e-6f)));
+            float pr[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                qv[i] = __fmul_rn(qv[i], qi);
+                kv[i] = __fmul_rn(kv[i], ki);
+                pr[i] = __fmul_rn(qv[i], kv[i]);
+                q[lane * 8 + i] = qv[i];
+                k[lane * 8 + i] = kv[i];
+            }
+            float al = tree8(pr, false);
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) al = __fadd_rn(al, __shfl_xor_sync(0xffffffffu, al, o));
+            if (lane == 0) sc[j * 4] = al;
+        }
+        __syncthreads();
+        /* the recurrence, token by token */
+        for (uint32_t j = 0; j < nj; ++j) {
+            const float *q = act + j * kPrefCh, *k = q + 256, *v = q + 512;
+            const float4 k0 = reinterpret_cast<const float4 *>(k)[lane], k1 = reinterpret_cast<const float4 *>(k)[32 + lane];
+            const float4 q0 = reinterpret_cast<const float4 *>(q)[lane], q1 = reinterpret_cast<const float4 *>(q)[32 + lane];
+            const float alpha = sc[j * 4], beta = sc[j * 4 + 1], decay = sc[j * 4 + 2];
+            float *attn = p.attn + (size_t)(j0 + j) * H + h * 256 + cb * 64 + warp * 8;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float r = __fmul_rn(a0[i].x, k0.x), pp = __fmul_rn(a0[i].x, q0.x);
+                r = __fadd_rn(r, __fmul_rn(a0[i].y, k0.y)); pp = __fadd_rn(pp, __fmul_rn(a0[i].y, q0.y));
+                r = __fadd_rn(r, __fmul_rn(a0[i].z, k0.z)); pp = __fadd_rn(pp, __fmul_rn(a0[i].z, q0.z));
+                r = __fadd_rn(r, __fmul_rn(a0[i].w, k0.w)); pp = __fadd_rn(pp, __fmul_rn(a0[i].w, q0.w));
+                r = __fadd_rn(r, __fmul_rn(a1[i].x, k1.x)); pp = __fadd_rn(pp, __fmul_rn(a1[i].x, q1.x));
+                r = __fadd_rn(r, __fmul_rn(a1[i].y, k1.y)); pp = __fadd_rn(pp, __fmul_rn(a1[i].y, q1.y));
+                r = __fadd_rn(r, __fmul_rn(a1[i].z, k1.z)); pp = __fadd_rn(pp, __fmul_rn(a1[i].z, q1.z));
+                r = __fadd_rn(r, __fmul_rn(a1[i].w, k1.w)); pp = __fadd_rn(pp, __fmul_rn(a1[i].w, q1.w));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, o));
+                    pp = __fadd_rn(pp, __shfl_xor_sync(0xffffffffu, pp, o));
+                }
+                const float delta = __fmul_rn(beta, __fsub_rn(v[warp * 8 + i], __fmul_rn(decay, r)));
+                if (lane == 0) attn[i] = __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pp), __fmul_rn(alpha, delta)));
+                a0[i].x = __fadd_rn(__fmul_rn(decay, a0[i].x), __fmul_rn(k0.x, delta));
+                a0[i].y = __fadd_rn(__fmul_rn(decay, a0[i].y), __fmul_rn(k0.y, delta));
+                a0[i].z = __fadd_rn(__fmul_rn(decay, a0[i].z), __fmul_rn(k0.z, delta));
+                a0[i].w = __fadd_rn(__fmul_rn(decay, a0[i].w), __fmul_rn(k0.w, delta));
+                a1[i].x = __fadd_rn(__fmul_rn(decay, a1[i].x), __fmul_rn(k1.x, delta));
+                a1[i].y = __fadd_rn(__fmul_rn(decay, a1[i].y), __fmul_rn(k1.y, delta));
+                a1[i].z = __fadd_rn(__fmul_rn(decay, a1[i].z), __fmul_rn(k1.z, delta));
+                a1[i].w = __fadd_rn(__fmul_rn(decay, a1[i].w), __fmul_rn(k1.w, delta));
+            }
+        }
+        __syncthreads();
+        /* the last three raw rows start the next window */
+        for (uint32_t idx = t; idx < 3 * kPrefCh; idx += 256) {
+            const uint32_t r = idx / kPrefCh, c = idx % kPrefCh;
+            raw[r * kPrefCh + c] = raw[(nj + r) * kPrefCh + c];
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        reinterpret_cast<float4 *>(S + (size_t)i * 256)[lane] = a0[i];
+        reinterpret_cast<float4 *>(S + (size_t)i * 256)[32 + lane] = a1[i];
+    }
+    for (uint32_t c = t; c < (uint32_t)kPrefCh; c += 256) {
+        const uint32_t kind = kind_of(c);
+        if (kind < 2 && ((c & 255u) >> 6) != cb) continue;  /* q/k tails: this block's quarter */
+        reinterpret_cast<float4 *>(tails_out)[((size_t)layer * 3 + kind) * H + gch(c)] =
+            make_float4(raw[c], raw[kPrefCh + c], raw[2 * kPrefCh + c], 0.0f);
+    }
+}
+
 /* Output RMSNorm x swish gate of one head of one stream (c_impl/gdn_model.cpp:
  * 3226-3349): sums of squares per 8 elements, then per 16-element half, the
  * halves summed in order; scale = 1/sqrtf(sum/256 + eps); out = ((a * scale)
@@ -1148,6 +1329,15 @@ cudaError_t launch_head(const StepParams &p, uint32_t layer, const Partials &qkv
     const cudaError_t e = cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHeadSmem);
     if (e != cudaSuccess) return e;
     return launch_pdl(head_kernel, p.streams * p.heads, 256, kHeadSmem, stream, p, layer, qkv, out);
+}
+
+cudaError_t launch_prefill_head(const StepParams &p, uint32_t layer, const Partials &qkv, float *state,
+                                const float *tails_in, float *tails_out, uint32_t ntok, cudaStream_t stream) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(prefill_head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrefillSmem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(prefill_head_kernel, p.heads * 4, 256, kPrefillSmem, stream, p, layer, qkv, state, tails_in,
+                      tails_out, ntok);
 }
 
 cudaError_t launch_gate_norm(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out,

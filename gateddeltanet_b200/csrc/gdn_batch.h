@@ -150,6 +150,12 @@ cudaError_t launch_head(const StepParams &p, uint32_t layer, const Partials &qkv
 /* output norm x swish gate as activation tiles (K = H) */
 cudaError_t launch_gate_norm(const StepParams &p, uint32_t layer, const Partials &qkv, TileOut out,
                              cudaStream_t stream);
+/* prefill: conv, norms and the recurrence of layer l for the ntok tokens of a
+ * chunk (the "streams" of its projections), on a single-stream run state's
+ * S [L][nh][v][k] and tails [L][3][H][4]; new tails go to tails_out; the
+ * outputs to p.attn [ntok][H] */
+cudaError_t launch_prefill_head(const StepParams &p, uint32_t layer, const Partials &qkv, float *state,
+                                const float *tails_in, float *tails_out, uint32_t ntok, cudaStream_t stream);
 /* m = silu(gate) * up as activation tiles (K = I) */
 cudaError_t launch_swiglu(const StepParams &p, const Partials &gu, TileOut out, cudaStream_t stream);
 /* FP32 logits and the per-stream argmax keys */

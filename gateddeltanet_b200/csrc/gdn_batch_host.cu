@@ -30,6 +30,7 @@
 namespace gdn {
 int host_fail(const char *msg);
 int host_device();
+int host_state_buffers(GDNRunState *state, float **S, float **tails, int *device, cudaStream_t *stream);
 }  // namespace gdn
 
 using namespace gdn::bt;
@@ -418,6 +419,20 @@ void free_batch(GdnB200Batch *b) {
     delete b;
 }
 
+/* The tile image of a model on a device, built on first use; one reference taken. */
+TileModel *acquire_tile_model(const GDNModel *model, int device) {
+    std::lock_guard<std::mutex> lk(g_bmu);
+    auto key = std::make_pair((const float *)model->weight_data, device);
+    auto it = g_tile_models.find(key);
+    if (it == g_tile_models.end()) {
+        TileModel *tm = build_tile_model(model);
+        if (tm == nullptr) return nullptr;
+        it = g_tile_models.emplace(key, tm).first;
+    }
+    ++it->second->refs;
+    return it->second;
+}
+
 int batch_supports(const GDNWeightHeader &c, uint32_t streams) {
     if (streams == 0 || streams > 1024) return bfail("gdn_b200 batch: streams must be 1..1024 (got %u)", streams);
     if (c.head_dim != 256 || c.conv_size != 4 || c.hidden_size != c.num_heads * 256)
@@ -445,20 +460,10 @@ GdnB200Batch *gdn_b200_batch_create(const GDNModel *model, uint32_t streams) {
         delete b;
         return nullptr;
     }
-    {
-        std::lock_guard<std::mutex> lk(g_bmu);
-        auto key = std::make_pair((const float *)model->weight_data, b->device);
-        auto it = g_tile_models.find(key);
-        if (it == g_tile_models.end()) {
-            TileModel *tm = build_tile_model(model);
-            if (tm == nullptr) {
-                delete b;
-                return nullptr;
-            }
-            it = g_tile_models.emplace(key, tm).first;
-        }
-        b->tm = it->second;
-        ++b->tm->refs;
+    b->tm = acquire_tile_model(model, b->device);
+    if (b->tm == nullptr) {
+        delete b;
+        return nullptr;
     }
     const uint32_t H = c.hidden_size, nh = c.num_heads, I = c.intermediate_size, V = c.vocab_size, L = c.num_layers;
     int sms = 0;
@@ -652,6 +657,154 @@ int gdn_b200_batch_fetch_logits(GdnB200Batch *b, float *logits) {
     return 0;
 }
 
+
+/* Prefill (no reference counterpart in the C ABI; the reference builds prompt
+ * state with FLA's chunked kernel, scripts/export_gdn_state.py:157-201): the
+ * prompt's tokens, up to 240 at a time, are the "streams" of the tile-GEMM
+ * projections, norms and SwiGLU; prefill_head_kernel runs the conv and the
+ * recurrence in token order on the run state's own S and tails. FP32
+ * contract; the run state ends as if the tokens had been decoded one by one
+ * (within FP32 summation-order differences), with no logits computed. */
+int gdn_b200_prefill(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n, float *device_ms) {
+    if (model == nullptr || state == nullptr || (tokens == nullptr && n > 0))
+        return bfail("gdn_b200 prefill: null argument");
+    if (n == 0) {
+        if (device_ms) *device_ms = 0.0f;
+        return 0;
+    }
+    const GDNWeightHeader &c = model->config;
+    if (batch_supports(c, 1) != 0) return -1;
+    for (uint32_t i = 0; i < n; ++i)
+        if (tokens[i] < 0 || (uint32_t)tokens[i] >= c.vocab_size)
+            return bfail("gdn_b200 prefill: token %d at %u out of range", tokens[i], i);
+    float *S = nullptr, *tails = nullptr;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    if (gdn::host_state_buffers(state, &S, &tails, &device, &stream) != 0) return -1;
+    BT_OK(cudaSetDevice(device));
+    /* the tile image stays cached with the model once built */
+    TileModel *tm = acquire_tile_model(model, device);
+    if (tm == nullptr) return -1;
+    const uint32_t H = c.hidden_size, I = c.intermediate_size, L = c.num_layers;
+    constexpr uint32_t kChunk = 3 * kMaxPassStreams;
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    size_t slots = 0;
+    for (const Matrix *mx : {&tm->qkv, &tm->o, &tm->gu, &tm->down}) {
+        const uint32_t g = gemm_grid(mx->mtiles(), mx->kblocks(), (uint32_t)sms);
+        slots = std::max<size_t>(slots, (size_t)g * gemm_max_local(mx->mtiles(), mx->kblocks(), g));
+    }
+    const size_t part_pass = slots * kMaxPassStreams * kTileM;
+    const size_t xb_stride = tile_pass_bytes(kMaxPassStreams, H), mb_stride = tile_pass_bytes(kMaxPassStreams, I);
+    const size_t tails_floats = (size_t)L * 3 * H * 4;
+    float *resid = nullptr, *attn = nullptr, *partial = nullptr, *tails_new = nullptr;
+    uint8_t *xb = nullptr, *mb = nullptr;
+    int32_t *dtok = nullptr;
+    uint32_t *step = nullptr, *status = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = 0;
+    auto cleanup = [&]() {
+        cudaStreamSynchronize(stream);
+        void *ptrs[] = {resid, attn, partial, tails_new, xb, mb, dtok, step, status};
+        for (void *q : ptrs) cudaFree(q);
+        if (e0) cudaEventDestroy(e0);
+        if (e1) cudaEventDestroy(e1);
+    };
+    if (cudaMalloc(&resid, (size_t)kChunk * H * 4) != cudaSuccess || cudaMalloc(&attn, (size_t)kChunk * H * 4) != cudaSuccess ||
+        cudaMalloc(&partial, 3 * part_pass * 4) != cudaSuccess || cudaMalloc(&tails_new, tails_floats * 4) != cudaSuccess ||
+        cudaMalloc(&xb, 3 * xb_stride) != cudaSuccess || cudaMalloc(&mb, 3 * mb_stride) != cudaSuccess ||
+        cudaMalloc(&dtok, (size_t)kChunk * 4) != cudaSuccess || cudaMalloc(&step, 4) != cudaSuccess ||
+        cudaMalloc(&status, 8) != cudaSuccess || cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) {
+        cleanup();
+        return bfail("gdn_b200 prefill: allocation failed");
+    }
+    cudaMemsetAsync(xb, 0, 3 * xb_stride, stream);
+    cudaMemsetAsync(mb, 0, 3 * mb_stride, stream);
+    cudaMemsetAsync(step, 0, 4, stream);
+    cudaMemsetAsync(status, 0, 8, stream);
+    cudaEventRecord(e0, stream);
+    for (uint32_t j0 = 0; j0 < n && rc == 0; j0 += kChunk) {
+        const uint32_t ntok = std::min(kChunk, n - j0);
+        const uint32_t passes = (ntok + kMaxPassStreams - 1) / kMaxPassStreams;
+        const uint32_t last = ntok - (passes - 1) * kMaxPassStreams, npad_last = (last + 15) / 16 * 16;
+        auto npad_of = [&](uint32_t ps) { return ps + 1 == passes ? npad_last : (uint32_t)kMaxPassStreams; };
+        StepParams sp;
+        memset(&sp, 0, sizeof(sp));
+        sp.streams = ntok;
+        sp.hidden = H;
+        sp.heads = c.num_heads;
+        sp.inter = I;
+        sp.vocab = c.vocab_size;
+        sp.layers = L;
+        sp.eps = c.norm_eps;
+        sp.emb = tm->emb;
+        sp.aux = tm->aux;
+        sp.aux_stride = tm->aux_stride;
+        sp.tokens = dtok;
+        sp.step = step;
+        sp.resid = resid;
+        sp.attn = attn;
+        sp.status = status;
+        const TileOut xo = {xb, xb_stride, npad_last, passes}, mo = {mb, mb_stride, npad_last, passes};
+        auto gemm = [&](const Matrix &mx, const uint8_t *a, const uint8_t *bt, size_t bt_stride, Partials *view) -> int {
+            const uint32_t grid = gemm_grid(mx.mtiles(), mx.kblocks(), (uint32_t)sms);
+            const uint32_t max_local = gemm_max_local(mx.mtiles(), mx.kblocks(), grid);
+            for (uint32_t ps = 0; ps < passes; ++ps) {
+                GemmParams p;
+                memset(&p, 0, sizeof(p));
+                p.a = a;
+                p.b = bt + ps * bt_stride;
+                p.kblocks = mx.kblocks();
+                p.mtiles = mx.mtiles();
+                p.npad = npad_of(ps);
+                gemm_slots(p.npad, &p.a_slots, &p.b_slots);
+                p.partial = partial + ps * part_pass;
+                p.max_local = max_local;
+                p.status = status;
+                BT_OK(launch_gemm(p, grid, stream));
+            }
+            *view = Partials{partial, part_pass, mx.mtiles() * mx.kblocks(), grid, mx.kblocks(), max_local, npad_last,
+                             passes};
+            return 0;
+        };
+        if (cudaMemcpyAsync(dtok, tokens + j0, (size_t)ntok * 4, cudaMemcpyHostToDevice, stream) != cudaSuccess) {
+            rc = bfail("gdn_b200 prefill: token upload failed");
+            break;
+        }
+        Partials none, qkv, o, gu, down;
+        memset(&none, 0, sizeof(none));
+        if (launch_input(sp, tm->aux, 0, none, xo, stream) != cudaSuccess) rc = -1;
+        for (uint32_t l = 0; l < L && rc == 0; ++l) {
+            const uint8_t *w = tm->img + (size_t)l * tm->layer_bytes;
+            const float *aux = tm->aux + (size_t)l * tm->aux_stride;
+            if (gemm(tm->qkv, w + tm->qkv.off, xb, xb_stride, &qkv) ||
+                launch_prefill_head(sp, l, qkv, S, tails, tails_new, ntok, stream) != cudaSuccess ||
+                launch_gate_norm(sp, l, qkv, xo, stream) != cudaSuccess ||
+                gemm(tm->o, w + tm->o.off, xb, xb_stride, &o) ||
+                launch_input(sp, aux + H + 256, 1, o, xo, stream) != cudaSuccess ||
+                gemm(tm->gu, w + tm->gu.off, xb, xb_stride, &gu) || launch_swiglu(sp, gu, mo, stream) != cudaSuccess ||
+                gemm(tm->down, w + tm->down.off, mb, mb_stride, &down)) {
+                rc = -1;
+                break;
+            }
+            if (l + 1 < L && launch_input(sp, tm->aux + (size_t)(l + 1) * tm->aux_stride, 1, down, xo, stream) != cudaSuccess)
+                rc = -1;
+        }
+        if (rc == 0 && cudaMemcpyAsync(tails, tails_new, tails_floats * 4, cudaMemcpyDeviceToDevice, stream) != cudaSuccess)
+            rc = bfail("gdn_b200 prefill: tail copy failed");
+    }
+    if (rc != 0 && gdn_b200_last_error()[0] == 0) bfail("gdn_b200 prefill: launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    cudaEventRecord(e1, stream);
+    uint32_t st[2] = {0, 0};
+    const cudaError_t se = cudaMemcpyAsync(st, status, 8, cudaMemcpyDeviceToHost, stream);
+    const cudaError_t ss = cudaStreamSynchronize(stream);
+    if (rc == 0 && (se != cudaSuccess || ss != cudaSuccess))
+        rc = bfail("gdn_b200 prefill: %s", cudaGetErrorString(se != cudaSuccess ? se : ss));
+    if (rc == 0 && st[0] != 0) rc = bfail("gdn_b200 prefill: device error %u at %u", st[0], st[1]);
+    if (rc == 0 && device_ms) cudaEventElapsedTime(device_ms, e0, e1);
+    cleanup();
+    return rc;
+}
 
 /* Test hook: Y[n][m] = sum_k W[m][k] X[n][k] through one tile-GEMM launch
  * (W BF16-exact FP32 words [m][k], X FP32 [n][k] split into three BF16 terms

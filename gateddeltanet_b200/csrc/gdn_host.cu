@@ -450,6 +450,16 @@ uint16_t bf16_rne_bits(float v) {
 namespace gdn {
 int host_fail(const char *msg) { return fail("%s", msg); }
 int host_device() { return g_device; }
+/* Device buffers of a run state: S [L][nh][v][k] FP32, tails [L][3][H][4] FP32. */
+int host_state_buffers(GDNRunState *state, float **S, float **tails, int *device, cudaStream_t *stream) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    *S = s->S;
+    *tails = s->tails;
+    *device = s->device;
+    *stream = s->stream;
+    return 0;
+}
 }  // namespace gdn
 
 /* ================================================================ C ABI */

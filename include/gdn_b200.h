@@ -172,6 +172,16 @@ int gdn_b200_batch_decode_tokens(GdnB200Batch *batch, const int32_t *tokens, uin
                                  int32_t *argmax_out, float *device_ms);
 /* Logits [streams][vocab] of the last step. */
 int gdn_b200_batch_fetch_logits(GdnB200Batch *batch, float *logits);
+/* Prefill: advance a run state by n prompt tokens at once (no logits), e.g.
+ * the prompt before decoding starts. The projections run as tensor-core GEMMs
+ * over up to 240 tokens at a time; the short convolution and the recurrence
+ * run in token order on the run state's own state. FP32 arithmetic: the state
+ * matches token-by-token decoding in the FP32-boundary contract within
+ * summation-order differences. device_ms, if not NULL, receives the device
+ * time. The counterpart of the reference's GPU prompt prefill
+ * (scripts/export_gdn_state.py:157-201), which feeds its .gdnstate export. */
+int gdn_b200_prefill(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n, float *device_ms);
+
 /* Test hook: y[n][m] = sum_k w[m][k] x[n][k] through one tensor-core tile-GEMM
  * launch (w BF16-exact FP32 words, x FP32 entering as three BF16 terms;
  * k a multiple of 64, n <= 80). */
