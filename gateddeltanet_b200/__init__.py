@@ -131,6 +131,10 @@ EXPORTS = [
      [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32, ctypes.c_int,
       ctypes.POINTER(ctypes.c_int32), _FP]),
     ("gdn_b200_batch_fetch_logits", ctypes.c_int, [ctypes.c_void_p, _FP]),
+    ("gdn_b200_score_window", ctypes.c_int,
+     [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32,
+      ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
+      ctypes.POINTER(ctypes.c_uint64)]),
     ("gdn_b200_prefill", ctypes.c_int,
      [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32, _FP]),
     ("gdn_b200_test_tile_gemm", ctypes.c_int,
@@ -276,6 +280,18 @@ class RunState:
                                         tok.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(tok),
                                         ctypes.byref(ms)), "gdn_b200_prefill")
         return float(ms.value)
+
+    def score_window(self, ctx: Sequence[int], cont: Sequence[int], use_prefill: bool = False):
+        """gdn_b200_score_window: (log-probability of cont given ctx, scored tokens); resets the state."""
+        a = np.ascontiguousarray(np.asarray(ctx, dtype=np.int32))
+        b = np.ascontiguousarray(np.asarray(cont, dtype=np.int32))
+        lp = ctypes.c_double(0.0)
+        n = ctypes.c_uint64(0)
+        P = ctypes.POINTER(ctypes.c_int32)
+        check(self.lib.gdn_b200_score_window(ctypes.byref(self.model.m), ctypes.byref(self.s), a.ctypes.data_as(P),
+                                             len(a), b.ctypes.data_as(P), len(b), int(bool(use_prefill)),
+                                             ctypes.byref(lp), ctypes.byref(n)), "gdn_b200_score_window")
+        return float(lp.value), int(n.value)
 
     def trace(self, token: int) -> np.ndarray:
         """One traced step: array [cta, phase, 8] of %globaltimer ns stamps

@@ -135,6 +135,8 @@ inline uint32_t epoch_stride(int L) { return (uint32_t)(L * kPhasesPerLayer + 1)
 
 size_t decode_smem_bytes(int H, int I);
 cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t stream);
+/* acc[0] += log_softmax(logits)[*target] (double), acc[1] += 1 (gdn_score.cu) */
+cudaError_t launch_score(const float *logits, uint32_t V, const int32_t *target, double *acc, cudaStream_t stream);
 
 }  // namespace gdn
 

@@ -963,6 +963,70 @@ int gdn_b200_delta_rule_step(uint32_t slices, float *S, const float *q, const fl
     return rc;
 }
 
+/* Teacher-forced scoring of one window, c_impl/host.cpp:1954-1994
+ * (score_window_hw): the state is reset, tokens = ctx ++ cont are fed in
+ * order except the last, and after each fed token i >= ctx_len - 1 the
+ * log-probability of tokens[i + 1] under the step's FP32 logits is added
+ * (gdn_score.cu). With use_prefill the first ctx_len - 1 tokens go through
+ * gdn_b200_prefill instead of one decode step each. */
+int gdn_b200_score_window(const GDNModel *model, GDNRunState *state, const int32_t *ctx, uint32_t ctx_len,
+                          const int32_t *cont, uint32_t cont_len, int use_prefill, double *logprob, uint64_t *scored) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    if (ctx == nullptr || cont == nullptr || ctx_len == 0 || cont_len == 0 || logprob == nullptr)
+        return fail("gdn_b200: invalid scoring window");
+    const GDNWeightHeader &c = model->config;
+    const uint32_t V = c.vocab_size, n = ctx_len + cont_len;
+    std::vector<int32_t> tokens(ctx, ctx + ctx_len);
+    tokens.insert(tokens.end(), cont, cont + cont_len);
+    for (uint32_t i = 0; i < n; ++i)
+        if (tokens[i] < 0 || (uint32_t)tokens[i] >= V) return fail("gdn_b200: scoring token %d out of range", tokens[i]);
+    CUDA_OK(cudaSetDevice(s->device));
+    const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
+    CUDA_OK(cudaMemsetAsync(s->S, 0, L * nh * 256 * 256 * sizeof(float), s->stream));
+    CUDA_OK(cudaMemsetAsync(s->tails, 0, L * 3 * H * 4 * sizeof(float), s->stream));
+    if (s->tokens_cap < n) {
+        cudaFree(s->tokens);
+        cudaFree(s->argmax);
+        s->tokens = nullptr;
+        s->argmax = nullptr;
+        s->tokens_cap = 0;
+        CUDA_OK(cudaMalloc(&s->tokens, n * sizeof(int32_t)));
+        CUDA_OK(cudaMalloc(&s->argmax, n * sizeof(int32_t)));
+        s->tokens_cap = n;
+    }
+    double *acc = nullptr;
+    CUDA_OK(cudaMalloc(&acc, 2 * sizeof(double)));
+    int rc = 0;
+    uint32_t first = 0;
+    if (use_prefill && ctx_len >= 2) {
+        CUDA_OK(cudaStreamSynchronize(s->stream));
+        rc = gdn_b200_prefill(model, state, tokens.data(), ctx_len - 1, nullptr);
+        first = ctx_len - 1;
+    }
+    if (rc == 0 && (cudaMemsetAsync(acc, 0, 2 * sizeof(double), s->stream) != cudaSuccess ||
+                    cudaMemcpyAsync(s->tokens, tokens.data(), n * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                    s->stream) != cudaSuccess))
+        rc = fail("gdn_b200: scoring setup failed");
+    gdn::DecodeParams p = make_params(*s);
+    for (uint32_t i = first; rc == 0 && i + 1 < n; ++i) {
+        p.token_src = s->tokens + i;
+        p.token_out = s->argmax + i;
+        if (launch(*s, p) != 0) rc = -1;
+        else if (i + 1 >= ctx_len && gdn::launch_score(s->logits, V, s->tokens + i + 1, acc, s->stream) != cudaSuccess)
+            rc = fail("gdn_b200: scoring launch failed");
+    }
+    double h[2] = {0.0, 0.0};
+    if (rc == 0 && cudaMemcpyAsync(h, acc, sizeof(h), cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
+        rc = fail("gdn_b200: scoring read-back failed");
+    if (rc == 0) rc = sync_and_check(*s);
+    cudaFree(acc);
+    if (rc != 0) return rc;
+    *logprob = h[0];
+    if (scored) *scored = (uint64_t)h[1];
+    return 0;
+}
+
 int gdn_b200_trace_step(const GDNModel *model, GDNRunState *state, int32_t token, uint64_t *trace_out,
                         size_t capacity) {
     Stream *s = find_stream(state);

@@ -182,6 +182,17 @@ int gdn_b200_batch_fetch_logits(GdnB200Batch *batch, float *logits);
  * (scripts/export_gdn_state.py:157-201), which feeds its .gdnstate export. */
 int gdn_b200_prefill(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n, float *device_ms);
 
+/* Teacher-forced scoring of one window, c_impl/host.cpp:1954-1994
+ * (score_window_hw): resets the run state to zero, feeds tokens = ctx ++ cont
+ * in order except the last, and sums over every fed token i >= ctx_len - 1
+ * the log-probability of tokens[i + 1] under that step's FP32 logits
+ * (max-shifted log-softmax in double). logprob receives the sum, scored (if
+ * not NULL) the number of scored tokens (cont_len). -1 if ctx_len or cont_len
+ * is 0 or a token is out of range. use_prefill != 0 feeds the first
+ * ctx_len - 1 tokens through gdn_b200_prefill (FP32) instead of decode steps. */
+int gdn_b200_score_window(const GDNModel *model, GDNRunState *state, const int32_t *ctx, uint32_t ctx_len,
+                          const int32_t *cont, uint32_t cont_len, int use_prefill, double *logprob, uint64_t *scored);
+
 /* Test hook: y[n][m] = sum_k w[m][k] x[n][k] through one tensor-core tile-GEMM
  * launch (w BF16-exact FP32 words, x FP32 entering as three BF16 terms;
  * k a multiple of 64, n <= 80). */
