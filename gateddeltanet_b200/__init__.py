@@ -94,6 +94,26 @@ EXPORTS = [
     ("gdn_set_native_debug_buffers", None, [_FP, _FP]),
     ("gdn_reset_mixed_mul_stats", None, []),
     ("gdn_get_mixed_mul_stats", None, None),  # returns a struct; argtypes set below
+    ("gdn_decode_step_host_partitioned", ctypes.c_int,
+     [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32)]),
+    ("gdn_forward", ctypes.c_int, [ctypes.c_void_p] * 34),
+    ("gdn_weight_shard_beats", ctypes.c_size_t, [ctypes.POINTER(GDNWeightHeader)]),
+    ("gdn_weight_shard_bytes", ctypes.c_size_t, [ctypes.POINTER(GDNWeightHeader)]),
+    ("gdn_validate_bf16_exact_weights", ctypes.c_int, [_FP, ctypes.POINTER(GDNWeightHeader)]),
+    ("gdn_build_weight_shards", None, [_FP, ctypes.POINTER(GDNWeightHeader), ctypes.c_void_p]),
+    ("gdn_validate_weight_shards", ctypes.c_int, [_FP, ctypes.POINTER(GDNWeightHeader), ctypes.c_void_p]),
+    ("gdn_aux_image_beats", ctypes.c_size_t, [ctypes.POINTER(GDNWeightHeader)]),
+    ("gdn_build_aux_image", None, [_FP, ctypes.POINTER(GDNWeightHeader), ctypes.c_void_p]),
+    ("gdn_validate_aux_image", ctypes.c_int, [ctypes.c_void_p, _FP, ctypes.POINTER(GDNWeightHeader)]),
+    ("gdn_scatter_recurrent_state", ctypes.c_int, [ctypes.c_void_p, _FP, ctypes.c_size_t]),
+    ("gdn_pack_conv_tails_bf16", ctypes.c_int, [ctypes.c_void_p, _FP, ctypes.c_size_t]),
+    ("gdn_test_fp32_to_bf16_rne_bits", ctypes.c_uint16, [ctypes.c_uint32]),
+    ("gdn_test_bf16_to_fp32_bits", ctypes.c_uint32, [ctypes.c_uint16]),
+    ("gdn_test_set_fp32_lane_bits", None, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32]),
+    ("gdn_test_get_fp32_lane_bits", ctypes.c_uint32, [ctypes.c_void_p, ctypes.c_uint32]),
+    ("gdn_test_set_bf16_lane_bits", None, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint16]),
+    ("gdn_test_get_bf16_lane_bits", ctypes.c_uint16, [ctypes.c_void_p, ctypes.c_uint32]),
+    ("gdn_b200_set_abi_compat", ctypes.c_int, [ctypes.c_int]),
     ("gdn_b200_set_device", ctypes.c_int, [ctypes.c_int]),
     ("gdn_b200_last_error", ctypes.c_char_p, []),
     ("gdn_b200_model_synth", ctypes.c_int, [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNWeightHeader), ctypes.c_uint64]),

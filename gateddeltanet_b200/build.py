@@ -17,7 +17,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libgdn_b200.so")
-SOURCES = ["gdn_decode.cu", "gdn_recurrence.cu", "gdn_batch.cu", "gdn_score.cu", "gdn_host.cu", "gdn_batch_host.cu"]
+SOURCES = ["gdn_decode.cu", "gdn_recurrence.cu", "gdn_batch.cu", "gdn_score.cu", "gdn_host.cu", "gdn_batch_host.cu",
+           "gdn_abi_host.cpp"]
 HEADERS = ["gdn_engine.h", "gdn_batch.h", "gdn_synth.h", "gdn_math.h", "exports.map"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -32,6 +32,16 @@
 #include <thread>
 #include <vector>
 
+namespace gdn {
+namespace abi {
+void gather_recurrent_state(Beat512 *const stripes[], float *rec, size_t floats);
+void unpack_conv_tails(const Beat512 *head, float *conv, size_t floats);
+void store_recurrent_state(Beat512 *const stripes[], const float *rec, size_t floats);
+void store_conv_tails(Beat512 *head, const float *conv, size_t floats);
+}  // namespace abi
+}  // namespace gdn
+
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -325,9 +335,19 @@ struct Stream {
     uint32_t epoch = 0;   /* exchange tag base of the next launch */
     int test_drop_cta = -1, test_drop_phase = -1;
     float *ws = nullptr;  /* pinned ABI workspace (host) */
+    /* reference-ABI compatibility (gdn_b200_set_abi_compat): the host shard and
+     * aux images of c_impl/gdn_model.cpp:1247-1294, whose state stripes
+     * (shards 28..31 past the weights) and workspace head buffer mirror the
+     * device state */
+    bool compat = false;
+    bool host_dirty = false;
+    Beat512 *shards[GEMV_CHANNELS] = {};
+    Beat512 *aux = nullptr;
+    size_t shard_beats = 0;
 };
 
 std::map<const void *, Stream *> g_streams;  /* keyed by GDNRunState.workspace */
+bool g_abi_compat = false;                   /* gdn_b200_set_abi_compat / GDN_B200_ABI_COMPAT=1 */
 
 float *g_debug_hidden = nullptr;
 float *g_debug_logits = nullptr;
@@ -336,6 +356,80 @@ Stream *find_stream(GDNRunState *state) {
     std::lock_guard<std::mutex> lock(g_mu);
     auto it = g_streams.find(state ? (const void *)state->workspace : nullptr);
     return it == g_streams.end() ? nullptr : it->second;
+}
+
+/* Host [L][h][k][v] / [L][kind][row][H] state <-> the device's [L][h][v][k] /
+ * [L][kind][H][4] layout. */
+int upload_state(Stream &st, const float *rec, const float *conv) {
+    Stream *s = &st;
+    const GDNWeightHeader &c = s->dm->cfg;
+    const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
+    const size_t rec_floats = L * nh * 256 * 256;
+    std::vector<float> S(rec_floats), T(L * 3 * H * 4, 0.0f);
+    parallel_for(L * nh, [&](size_t b, size_t e) {
+        for (size_t lh = b; lh < e; ++lh)
+            for (size_t k = 0; k < 256; ++k)
+                for (size_t v = 0; v < 256; ++v) S[(lh * 256 + v) * 256 + k] = rec[(lh * 256 + k) * 256 + v];
+    });
+    for (size_t lk = 0; lk < L * 3; ++lk)
+        for (size_t d = 0; d < H; ++d)
+            for (size_t r = 0; r < 3; ++r) T[(lk * H + d) * 4 + r] = conv[(lk * 3 + r) * H + d];
+    CUDA_OK(cudaSetDevice(s->device));
+    CUDA_OK(cudaMemcpyAsync(s->S, S.data(), S.size() * 4, cudaMemcpyHostToDevice, s->stream));
+    CUDA_OK(cudaMemcpyAsync(s->tails, T.data(), T.size() * 4, cudaMemcpyHostToDevice, s->stream));
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    return 0;
+}
+
+int download_state(Stream &st, float *rec, float *conv) {
+    Stream *s = &st;
+    const GDNWeightHeader &c = s->dm->cfg;
+    const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
+    std::vector<float> S(L * nh * 256 * 256), T(L * 3 * H * 4);
+    CUDA_OK(cudaSetDevice(s->device));
+    CUDA_OK(cudaMemcpyAsync(S.data(), s->S, S.size() * 4, cudaMemcpyDeviceToHost, s->stream));
+    CUDA_OK(cudaMemcpyAsync(T.data(), s->tails, T.size() * 4, cudaMemcpyDeviceToHost, s->stream));
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    parallel_for(L * nh, [&](size_t b, size_t e) {
+        for (size_t lh = b; lh < e; ++lh)
+            for (size_t k = 0; k < 256; ++k)
+                for (size_t v = 0; v < 256; ++v) rec[(lh * 256 + k) * 256 + v] = S[(lh * 256 + v) * 256 + k];
+    });
+    for (size_t lk = 0; lk < L * 3; ++lk)
+        for (size_t d = 0; d < H; ++d)
+            for (size_t r = 0; r < 3; ++r) conv[(lk * 3 + r) * H + d] = T[(lk * H + d) * 4 + r];
+    return 0;
+}
+
+/* Reference-ABI compatibility: state written by the caller into the host
+ * stripes / head buffer (gdn_scatter_recurrent_state, gdn_pack_conv_tails_bf16)
+ * goes to the device before the next step, and after every step the device
+ * state is written back there (BF16, the c_impl state format), so callers that
+ * read the stripes (c_impl/gdn_eval.cpp's state dump) see the current state. */
+Beat512 *stripe(Stream &s, int p) { return s.shards[GDN_RECURRENT_STATE_FIRST_PORT + p] + s.shard_beats; }
+
+int compat_pull(Stream &s) {
+    const GDNWeightHeader &c = s.dm->cfg;
+    const size_t rec_floats = (size_t)c.num_layers * c.num_heads * 256 * 256;
+    const size_t conv_floats = (size_t)c.num_layers * 9 * c.hidden_size;
+    std::vector<float> rec(rec_floats), conv(conv_floats);
+    Beat512 *st[4] = {stripe(s, 0), stripe(s, 1), stripe(s, 2), stripe(s, 3)};
+    gdn::abi::gather_recurrent_state(st, rec.data(), rec_floats);
+    gdn::abi::unpack_conv_tails(reinterpret_cast<const Beat512 *>(s.ws + GDN_WS_OFF_HEAD_BUF), conv.data(), conv_floats);
+    s.host_dirty = false;
+    return upload_state(s, rec.data(), conv.data());
+}
+
+int compat_push(Stream &s) {
+    const GDNWeightHeader &c = s.dm->cfg;
+    const size_t rec_floats = (size_t)c.num_layers * c.num_heads * 256 * 256;
+    const size_t conv_floats = (size_t)c.num_layers * 9 * c.hidden_size;
+    std::vector<float> rec(rec_floats), conv(conv_floats);
+    if (download_state(s, rec.data(), conv.data()) != 0) return -1;
+    Beat512 *st[4] = {stripe(s, 0), stripe(s, 1), stripe(s, 2), stripe(s, 3)};
+    gdn::abi::store_recurrent_state(st, rec.data(), rec_floats);
+    gdn::abi::store_conv_tails(reinterpret_cast<Beat512 *>(s.ws + GDN_WS_OFF_HEAD_BUF), conv.data(), conv_floats);
+    return 0;
 }
 
 gdn::DecodeParams make_params(const Stream &s) {
@@ -448,6 +542,18 @@ uint16_t bf16_rne_bits(float v) {
 /* Shared with the multi-stream layer (gdn_batch_host.cu): one error string and
  * one device selection per thread for the whole library. */
 namespace gdn {
+/* A caller wrote state through the reference's packing functions into buffers
+ * of a run state: mark it for upload before its next step. */
+void host_note_state_write(const void *buffer) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    for (auto &kv : g_streams) {
+        Stream *s = kv.second;
+        if (!s->compat) continue;
+        if (buffer == (const void *)(s->ws + GDN_WS_OFF_HEAD_BUF) ||
+            buffer == (const void *)(s->shards[GDN_RECURRENT_STATE_FIRST_PORT] + s->shard_beats))
+            s->host_dirty = true;
+    }
+}
 int host_fail(const char *msg) { return fail("%s", msg); }
 int host_device() { return g_device; }
 /* Device buffers of a run state: S [L][nh][v][k] FP32, tails [L][3][H][4] FP32. */
@@ -699,6 +805,36 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
     state->x = s->ws + GDN_WS_OFF_X;
     state->recurrent_state = s->ws + GDN_WS_OFF_REC_STATE;
     state->head_buffer = s->ws + GDN_WS_OFF_HEAD_BUF;
+    const char *env = getenv("GDN_B200_ABI_COMPAT");
+    if (g_abi_compat || (env != nullptr && env[0] == '1')) {
+        /* the reference's run state: 32 packed shards (28..31 followed by the
+         * BF16 state stripes) and the aux image (c_impl/gdn_model.cpp:1266-1293),
+         * and the reference's own arithmetic */
+        s->compat = true;
+        s->shard_beats = gdn_weight_shard_beats(&c);
+        for (int ch = 0; ch < GEMV_CHANNELS; ++ch) {
+            const bool st = ch >= GDN_RECURRENT_STATE_FIRST_PORT && ch < GDN_RECURRENT_STATE_FIRST_PORT + 4;
+            const size_t beats = s->shard_beats + (st ? GDN_RECURRENT_STATE_STRIPE_BF16_BEATS : 0);
+            s->shards[ch] = static_cast<Beat512 *>(aligned_alloc(64, beats * sizeof(Beat512)));
+            if (s->shards[ch] == nullptr) {
+                for (int j = 0; j < ch; ++j) free(s->shards[j]);
+                return cleanup(fail("gdn_b200: host shard allocation failed"));
+            }
+            if (st) memset(s->shards[ch] + s->shard_beats, 0, GDN_RECURRENT_STATE_STRIPE_BF16_BEATS * sizeof(Beat512));
+        }
+        gdn_build_weight_shards(model->weight_data, &c, s->shards);
+        s->aux = static_cast<Beat512 *>(aligned_alloc(64, gdn_aux_image_beats(&c) * sizeof(Beat512)));
+        if (s->aux == nullptr) {
+            for (auto &p : s->shards) free(p);
+            return cleanup(fail("gdn_b200: aux image allocation failed"));
+        }
+        gdn_build_aux_image(model->weight_data, &c, s->aux);
+        for (int ch = 0; ch < GEMV_CHANNELS; ++ch) state->weight_shards[ch] = s->shards[ch];
+        state->aux_weights = s->aux;
+        s->bf16_boundary = 1;
+        s->native_product = 1;
+        s->bf16_state = 1;
+    }
     {
         std::lock_guard<std::mutex> lock(g_mu);
         dm->refs++;
@@ -735,6 +871,8 @@ void gdn_run_state_free(GDNRunState *state) {
         cudaFree(s->argmax);
         cudaFreeHost(s->status_host);
         cudaFreeHost(s->ws);
+        for (auto &p : s->shards) free(p);
+        free(s->aux);
         cudaSetDevice(prev);
         std::lock_guard<std::mutex> lock(g_mu);
         DeviceModel *dm = s->dm;
@@ -774,6 +912,29 @@ int gdn_b200_test_drop_outputs(GDNRunState *state, int cta, int phase) {
     return 0;
 }
 
+/* One step from the FP32 embedding row in workspace[X]: the body of the
+ * reference's gdn_forward (c_impl/gdn_model.cpp:3719-3897). */
+static int forward_from_workspace(Stream &st) {
+    Stream *s = &st;
+    const GDNWeightHeader &c = s->dm->cfg;
+    const size_t H = c.hidden_size;
+    CUDA_OK(cudaSetDevice(s->device));
+    if (s->compat && s->host_dirty && compat_pull(*s) != 0) return -1;
+    CUDA_OK(cudaMemcpyAsync(s->x_embed, s->ws + GDN_WS_OFF_X, H * sizeof(float), cudaMemcpyHostToDevice, s->stream));
+    gdn::DecodeParams p = make_params(*s);
+    if (launch(*s, p) != 0) return -1;
+    /* token line -> workspace[X_NORM] (64 bytes, c_impl/host.cpp:1011-1017) */
+    CUDA_OK(cudaMemcpyAsync(s->ws + GDN_WS_OFF_X_NORM, s->status->token_line, 64, cudaMemcpyDeviceToHost, s->stream));
+    if (g_debug_hidden != nullptr)
+        CUDA_OK(cudaMemcpyAsync(g_debug_hidden, s->hidden, H * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+    if (g_debug_logits != nullptr)
+        CUDA_OK(cudaMemcpyAsync(g_debug_logits, s->logits, c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost,
+                                s->stream));
+    const int rc = sync_and_check(*s);
+    if (rc != 0) return rc;
+    return s->compat ? compat_push(*s) : 0;
+}
+
 int gdn_decode_step_host(const GDNModel *model, GDNRunState *state, const int32_t *token) {
     if (*token < 0 || (uint32_t)*token >= model->config.vocab_size) return fail("token id out of range");
     Stream *s = find_stream(state);
@@ -782,18 +943,51 @@ int gdn_decode_step_host(const GDNModel *model, GDNRunState *state, const int32_
     /* the host writes the FP32 embedding row into workspace[X]
      * (c_impl/gdn_model.cpp:3906-3908; c_impl/host.cpp:955-960) */
     memcpy(state->x, model->embeddings + (size_t)*token * H, H * sizeof(float));
-    CUDA_OK(cudaSetDevice(s->device));
-    CUDA_OK(cudaMemcpyAsync(s->x_embed, state->x, H * sizeof(float), cudaMemcpyHostToDevice, s->stream));
-    gdn::DecodeParams p = make_params(*s);
-    if (launch(*s, p) != 0) return -1;
-    /* token line -> workspace[X_NORM] (64 bytes, c_impl/host.cpp:1011-1017) */
-    CUDA_OK(cudaMemcpyAsync(s->ws + GDN_WS_OFF_X_NORM, s->status->token_line, 64, cudaMemcpyDeviceToHost, s->stream));
-    if (g_debug_hidden != nullptr)
-        CUDA_OK(cudaMemcpyAsync(g_debug_hidden, s->hidden, H * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
-    if (g_debug_logits != nullptr)
-        CUDA_OK(cudaMemcpyAsync(g_debug_logits, s->logits, model->config.vocab_size * sizeof(float),
-                                cudaMemcpyDeviceToHost, s->stream));
-    return sync_and_check(*s);
+    return forward_from_workspace(*s);
+}
+
+/* The SLR-partitioned C model of the reference computes the same step
+ * (c_impl/gdn_model.cpp:7216-7258); here it is the same engine call. */
+int gdn_decode_step_host_partitioned(const GDNModel *model, GDNRunState *state, const int32_t *token) {
+    return gdn_decode_step_host(model, state, token);
+}
+
+/* The kernel top of the reference (c_impl/gdn_model.h:224-259): one token from
+ * the embedding row the host wrote into workspace[X], against the run state
+ * whose workspace this is; the shard and aux pointers name the same weights the
+ * engine holds on the device. The state it decodes from is that run state's
+ * (after any caller write through gdn_scatter_recurrent_state /
+ * gdn_pack_conv_tails_bf16). Returns 0, or -1 for an unknown workspace. */
+int gdn_forward(const Beat512 *aux_weights, Beat512 *workspace, const Beat512 *mm0, const Beat512 *mm1,
+                const Beat512 *mm2, const Beat512 *mm3, const Beat512 *mm4, const Beat512 *mm5, const Beat512 *mm6,
+                const Beat512 *mm7, const Beat512 *mm8, const Beat512 *mm9, const Beat512 *mm10, const Beat512 *mm11,
+                const Beat512 *mm12, const Beat512 *mm13, const Beat512 *mm14, const Beat512 *mm15,
+                const Beat512 *mm16, const Beat512 *mm17, const Beat512 *mm18, const Beat512 *mm19,
+                const Beat512 *mm20, const Beat512 *mm21, const Beat512 *mm22, const Beat512 *mm23,
+                const Beat512 *mm24, const Beat512 *mm25, const Beat512 *mm26, const Beat512 *mm27, Beat512 *mm28,
+                Beat512 *mm29, Beat512 *mm30, Beat512 *mm31) {
+    (void)aux_weights;
+    const void *unused[] = {mm0, mm1, mm2, mm3, mm4, mm5, mm6, mm7, mm8, mm9, mm10, mm11, mm12, mm13, mm14, mm15,
+                            mm16, mm17, mm18, mm19, mm20, mm21, mm22, mm23, mm24, mm25, mm26, mm27, mm28, mm29, mm30,
+                            mm31};
+    for (const void *q : unused) (void)q;
+    Stream *s = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        auto it = g_streams.find((const void *)workspace);
+        if (it != g_streams.end()) s = it->second;
+    }
+    if (s == nullptr) return fail("gdn_forward: workspace does not belong to a run state of this library");
+    return forward_from_workspace(*s);
+}
+
+/* Reference-ABI compatibility for run states created after the call (also
+ * GDN_B200_ABI_COMPAT=1 in the environment): host shard and aux images,
+ * c_impl arithmetic, and the state stripes / head buffer kept in step with the
+ * device state. */
+int gdn_b200_set_abi_compat(int on) {
+    g_abi_compat = on != 0;
+    return 0;
 }
 
 int gdn_b200_decode_tokens(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n, int greedy,
@@ -1078,21 +1272,7 @@ int gdn_b200_state_upload(GDNRunState *state, const float *rec, size_t rec_float
     const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
     if (rec_floats != L * nh * 256 * 256 || conv_floats != L * 3 * 3 * H)
         return fail("gdn_b200: state sizes do not match the model (rec %zu, conv %zu)", rec_floats, conv_floats);
-    /* [L][h][k][v] -> [L][h][v][k];  [L][kind][row][H] -> [L][kind][H][4] */
-    std::vector<float> S(rec_floats), T(L * 3 * H * 4, 0.0f);
-    parallel_for(L * nh, [&](size_t b, size_t e) {
-        for (size_t lh = b; lh < e; ++lh)
-            for (size_t k = 0; k < 256; ++k)
-                for (size_t v = 0; v < 256; ++v) S[(lh * 256 + v) * 256 + k] = rec[(lh * 256 + k) * 256 + v];
-    });
-    for (size_t lk = 0; lk < L * 3; ++lk)
-        for (size_t d = 0; d < H; ++d)
-            for (size_t r = 0; r < 3; ++r) T[(lk * H + d) * 4 + r] = conv[(lk * 3 + r) * H + d];
-    CUDA_OK(cudaSetDevice(s->device));
-    CUDA_OK(cudaMemcpyAsync(s->S, S.data(), S.size() * 4, cudaMemcpyHostToDevice, s->stream));
-    CUDA_OK(cudaMemcpyAsync(s->tails, T.data(), T.size() * 4, cudaMemcpyHostToDevice, s->stream));
-    CUDA_OK(cudaStreamSynchronize(s->stream));
-    return 0;
+    return upload_state(*s, rec, conv);
 }
 
 int gdn_b200_state_download(GDNRunState *state, float *rec, size_t rec_floats, float *conv, size_t conv_floats) {
@@ -1102,20 +1282,7 @@ int gdn_b200_state_download(GDNRunState *state, float *rec, size_t rec_floats, f
     const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
     if (rec_floats != L * nh * 256 * 256 || conv_floats != L * 3 * 3 * H)
         return fail("gdn_b200: state sizes do not match the model");
-    std::vector<float> S(rec_floats), T(L * 3 * H * 4);
-    CUDA_OK(cudaSetDevice(s->device));
-    CUDA_OK(cudaMemcpyAsync(S.data(), s->S, S.size() * 4, cudaMemcpyDeviceToHost, s->stream));
-    CUDA_OK(cudaMemcpyAsync(T.data(), s->tails, T.size() * 4, cudaMemcpyDeviceToHost, s->stream));
-    CUDA_OK(cudaStreamSynchronize(s->stream));
-    parallel_for(L * nh, [&](size_t b, size_t e) {
-        for (size_t lh = b; lh < e; ++lh)
-            for (size_t k = 0; k < 256; ++k)
-                for (size_t v = 0; v < 256; ++v) rec[(lh * 256 + k) * 256 + v] = S[(lh * 256 + v) * 256 + k];
-    });
-    for (size_t lk = 0; lk < L * 3; ++lk)
-        for (size_t d = 0; d < H; ++d)
-            for (size_t r = 0; r < 3; ++r) conv[(lk * 3 + r) * H + d] = T[(lk * H + d) * 4 + r];
-    return 0;
+    return download_state(*s, rec, conv);
 }
 
 int gdn_b200_state_load_file(GDNRunState *state, const char *path, int32_t *seed_token) {

@@ -131,6 +131,17 @@ int gdn_b200_delta_rule_step(uint32_t slices, float *S, const float *q, const fl
  * reload it). Nothing faults or hangs on the GPU. */
 int gdn_b200_test_drop_outputs(GDNRunState *state, int cta, int phase);
 
+/* Reference-ABI compatibility for the run states created afterwards (also
+ * GDN_B200_ABI_COMPAT=1 in the environment): gdn_run_state_init then builds
+ * the reference's host images (32 packed shards with the BF16 state stripes,
+ * the aux image; about 2.8 GB of host memory per run state) and selects the
+ * c_impl arithmetic; state written through gdn_scatter_recurrent_state /
+ * gdn_pack_conv_tails_bf16 is uploaded before the next step, and after every
+ * step the device state is written back to the stripes and the head buffer,
+ * so an unmodified reference driver (c_impl/gdn_eval.cpp) runs on this
+ * library. Off by default. */
+int gdn_b200_set_abi_compat(int on);
+
 /* Number of SMs (CTAs) the decode kernel uses on the current device. */
 int gdn_b200_grid_size(void);
 

@@ -136,6 +136,46 @@ typedef struct {
     uint64_t overflows;
 } GDNMixedMulStats;
 
+/* The FPGA image layouts of the reference's run state (c_impl/gdn_model.h:
+ * 84-119): the recurrent state lives as BF16 stripes past the weights of
+ * shards 28..31, the conv tails as BF16 in the first half of each per
+ * layer/kind stripe of the workspace head buffer. */
+#define GDN_RECURRENT_STATE_PORTS       4
+#define GDN_RECURRENT_STATE_FIRST_PORT 28
+#define GDN_RECURRENT_STATE_STRIPE_FLOATS (GDN_WSF_STATE / GDN_RECURRENT_STATE_PORTS)
+#define GDN_RECURRENT_STATE_STRIPE_BF16_BEATS (GDN_RECURRENT_STATE_STRIPE_FLOATS / 32u)
+#define GDN_CONV_TAIL_STRIPES (24u * 3u)
+#define GDN_CONV_TAIL_FLOATS_PER_STRIPE (GDN_WSF_HEADBUF / GDN_CONV_TAIL_STRIPES)
+#define GDN_CONV_TAIL_RESERVED_BEATS_PER_STRIPE (GDN_CONV_TAIL_FLOATS_PER_STRIPE / 16u)
+#define GDN_CONV_TAIL_BF16_BEATS_PER_STRIPE (GDN_CONV_TAIL_FLOATS_PER_STRIPE / 32u)
+
+/* Host image helpers, c_impl/gdn_model.h:170-195 (behaviour
+ * c_impl/gdn_model.cpp:595-1080), implemented in gdn_abi_host.cpp with the
+ * reference's exact layouts. The engine does not read these images; a run
+ * state has them only in reference-ABI compatibility mode
+ * (gdn_b200_set_abi_compat). */
+size_t gdn_weight_shard_beats(const GDNWeightHeader *config);
+size_t gdn_weight_shard_bytes(const GDNWeightHeader *config);
+int gdn_validate_bf16_exact_weights(const float *weight_data, const GDNWeightHeader *config);
+void gdn_build_weight_shards(const float *weight_data, const GDNWeightHeader *config, Beat512 *const shards[]);
+int gdn_validate_weight_shards(const float *weight_data, const GDNWeightHeader *config, Beat512 *const shards[]);
+size_t gdn_aux_image_beats(const GDNWeightHeader *config);
+void gdn_build_aux_image(const float *weight_data, const GDNWeightHeader *config, Beat512 *aux_image);
+int gdn_validate_aux_image(const Beat512 *aux_image, const float *weight_data, const GDNWeightHeader *config);
+/* Writing state through these two also marks the owning run state (if any)
+ * for upload before its next decode step. */
+int gdn_scatter_recurrent_state(Beat512 *const state_stripes[], const float *recurrent_state,
+                                size_t recurrent_state_floats);
+int gdn_pack_conv_tails_bf16(Beat512 *workspace_head_buffer, const float *conv_tails, size_t conv_tail_floats);
+
+/* Lane helpers of the reference's tests, c_impl/gdn_model.cpp:338-366. */
+uint16_t gdn_test_fp32_to_bf16_rne_bits(uint32_t bits);
+uint32_t gdn_test_bf16_to_fp32_bits(uint16_t bits);
+void gdn_test_set_fp32_lane_bits(Beat512 *beat, uint32_t lane, uint32_t bits);
+uint32_t gdn_test_get_fp32_lane_bits(const Beat512 *beat, uint32_t lane);
+void gdn_test_set_bf16_lane_bits(Beat512 *beat, uint32_t lane, uint16_t bits);
+uint16_t gdn_test_get_bf16_lane_bits(const Beat512 *beat, uint32_t lane);
+
 /* Load a .gdnw file: header validation (magic "GDNWv1", version 1,
  * num_heads == num_v_heads, hidden == heads * head_dim) and the BF16-exactness
  * check of every word while reading. Returns 0, or -1 with a message.
@@ -162,6 +202,28 @@ void gdn_run_state_free(GDNRunState *state);
  * lowest index on ties) written as a float into workspace[X_NORM] lane 0.
  * Synchronous. Replaces c_impl/gdn_model.h:263 (c_impl/gdn_model.cpp:3900-3928). */
 int gdn_decode_step_host(const GDNModel *model, GDNRunState *state, const int32_t *token);
+
+/* The reference's SLR-partitioned step (c_impl/gdn_model.h:264,
+ * c_impl/gdn_model.cpp:7240-7258) computes the same step; here it is
+ * gdn_decode_step_host. */
+int gdn_decode_step_host_partitioned(const GDNModel *model, GDNRunState *state, const int32_t *token);
+
+/* The reference's kernel top (c_impl/gdn_model.h:224-259): one token from the
+ * FP32 embedding row in workspace[X] against the run state that owns
+ * `workspace`; the 32 shard pointers and the aux image name the weights the
+ * engine already holds on the device. -1 if the workspace is not a run state's. */
+int gdn_forward(const Beat512 *aux_weights, Beat512 *workspace, const Beat512 *weight_data_mm0,
+                const Beat512 *weight_data_mm1, const Beat512 *weight_data_mm2, const Beat512 *weight_data_mm3,
+                const Beat512 *weight_data_mm4, const Beat512 *weight_data_mm5, const Beat512 *weight_data_mm6,
+                const Beat512 *weight_data_mm7, const Beat512 *weight_data_mm8, const Beat512 *weight_data_mm9,
+                const Beat512 *weight_data_mm10, const Beat512 *weight_data_mm11, const Beat512 *weight_data_mm12,
+                const Beat512 *weight_data_mm13, const Beat512 *weight_data_mm14, const Beat512 *weight_data_mm15,
+                const Beat512 *weight_data_mm16, const Beat512 *weight_data_mm17, const Beat512 *weight_data_mm18,
+                const Beat512 *weight_data_mm19, const Beat512 *weight_data_mm20, const Beat512 *weight_data_mm21,
+                const Beat512 *weight_data_mm22, const Beat512 *weight_data_mm23, const Beat512 *weight_data_mm24,
+                const Beat512 *weight_data_mm25, const Beat512 *weight_data_mm26, const Beat512 *weight_data_mm27,
+                Beat512 *weight_data_mm28, Beat512 *weight_data_mm29, Beat512 *weight_data_mm30,
+                Beat512 *weight_data_mm31);
 
 /* Independent scalar LM head on the host: logits_out[v] = sum_i
  * lm_head[v][i] * bf16(hidden[i]) with the reference's BF16 product rounding.

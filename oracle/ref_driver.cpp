@@ -99,8 +99,67 @@ static int dump_primitives(const char *path) {
     return 0;
 }
 
+/* The reference's host image helpers on seeded inputs (layout goldens):
+ *   the 32 weight shards and the aux image of a small seeded model (the
+ *   builders are shape-driven: vocab 4096, hidden 512, 2 layers, 2 heads,
+ *   intermediate 1536), the four state stripes of a seeded BF16 state of that
+ *   model, and the conv-tail packing of a seeded GDN_WSF_HEADBUF-float array,
+ * written raw in that order (c_impl/gdn_model.cpp:674-935, 937-1027).
+ * tests/test_abi_layouts_cpu.py rebuilds the same images with
+ * libgdn_b200.so's restatement and compares digests. */
+static int dump_layouts(const char *path) {
+    GdnOracleDims d = {4096, 512, 2, 2, 256, 1536, 4, 1e-6f};
+    GDNWeightHeader hdr;
+    std::memset(&hdr, 0, sizeof(hdr));
+    std::memcpy(hdr.magic, "GDNWv1\0\0", 8);
+    hdr.version = 1;
+    hdr.vocab_size = d.vocab;
+    hdr.hidden_size = d.hidden;
+    hdr.num_layers = d.layers;
+    hdr.num_heads = d.heads;
+    hdr.num_v_heads = d.heads;
+    hdr.head_dim = d.head_dim;
+    hdr.intermediate_size = d.inter;
+    hdr.conv_size = d.conv;
+    hdr.max_seq_len = 2048;
+    hdr.norm_eps = d.eps;
+    std::vector<float> blob(gdn_oracle_weight_floats(&d));
+    gdn_oracle_synth_weights(&d, 4321, blob.data(), 8);
+    const size_t sb = gdn_weight_shard_beats(&hdr);
+    std::vector<Beat512> shard_mem((size_t)GEMV_CHANNELS * sb);
+    Beat512 *shards[GEMV_CHANNELS];
+    for (int c = 0; c < GEMV_CHANNELS; ++c) shards[c] = shard_mem.data() + (size_t)c * sb;
+    gdn_build_weight_shards(blob.data(), &hdr, shards);
+    std::vector<Beat512> aux(gdn_aux_image_beats(&hdr));
+    gdn_build_aux_image(blob.data(), &hdr, aux.data());
+    const size_t rec_floats = (size_t)d.layers * d.heads * 256 * 256;
+    std::vector<float> rec(rec_floats);
+    for (size_t i = 0; i < rec_floats; ++i) rec[i] = gdn_synth_round_bf16(gdn_synth_normal(77, GDN_SYNTH_STREAM_STATE, i, 0.05));
+    const size_t stripe_beats = rec_floats / 256 * 2;
+    std::vector<Beat512> stripe_mem(4 * stripe_beats);
+    Beat512 *stripes[4];
+    for (int p = 0; p < 4; ++p) stripes[p] = stripe_mem.data() + (size_t)p * stripe_beats;
+    if (gdn_scatter_recurrent_state(stripes, rec.data(), rec_floats) != 0) die("scatter failed");
+    std::vector<float> conv(GDN_WSF_HEADBUF);
+    for (size_t i = 0; i < conv.size(); ++i) conv[i] = gdn_synth_round_bf16(gdn_synth_normal(78, GDN_SYNTH_STREAM_STATE + 1, i, 0.5));
+    std::vector<Beat512> head(GDN_WSF_HEADBUF / 16);
+    if (gdn_pack_conv_tails_bf16(head.data(), conv.data(), conv.size()) != 0) die("conv pack failed");
+    FILE *f = std::fopen(path, "wb");
+    if (f == nullptr) die("cannot open layouts output");
+    std::fwrite("GDNLAYT1", 1, 8, f);
+    const uint64_t n[4] = {sb, aux.size(), stripe_beats, head.size()};
+    std::fwrite(n, 8, 4, f);
+    std::fwrite(shard_mem.data(), sizeof(Beat512), shard_mem.size(), f);
+    std::fwrite(aux.data(), sizeof(Beat512), aux.size(), f);
+    std::fwrite(stripe_mem.data(), sizeof(Beat512), stripe_mem.size(), f);
+    std::fwrite(head.data(), sizeof(Beat512), head.size(), f);
+    std::fclose(f);
+    return 0;
+}
+
 int main(int argc, char **argv) {
     if (argc == 3 && std::string(argv[1]) == "--primitives") return dump_primitives(argv[2]);
+    if (argc == 3 && std::string(argv[1]) == "--layouts") return dump_layouts(argv[2]);
     uint64_t seed = 1234;
     uint64_t stream_seed = 99;
     uint32_t stream_id = 0;

@@ -8,6 +8,10 @@ its outputs:
               BF16 product (gdn_native_bf16_mul_to_fp32) over fixed input
               grids (oracle/ref_driver.cpp dump_primitives): SHA-256 of the
               outputs plus an explicit sample.
+  layouts     the reference's host image helpers (oracle/ref_driver.cpp
+              dump_layouts): SHA-256 of the 32 packed weight shards and the aux
+              image of a small seeded model, of the four recurrent-state
+              stripes of a seeded state and of the conv-tail packing.
   decode      gdn_decode_step_host on seeded GDN-1.3B weights
               (gateddeltanet_b200/csrc/gdn_synth.h) and seeded token streams:
               per step the input token, the kernel's argmax, SHA-256 of the
@@ -65,6 +69,29 @@ def primitives(tmp: str) -> dict:
     }
 
 
+def layouts(tmp: str) -> dict:
+    path = os.path.join(tmp, "layouts.bin")
+    subprocess.run([DRIVER, "--layouts", path], check=True)
+    data = open(path, "rb").read()
+    assert data[:8] == b"GDNLAYT1"
+    sb, na, stb, nh = (int(x) for x in np.frombuffer(data[8:40], dtype=np.uint64))
+    off = 40
+    parts = {}
+    for name, n in (("shards", 32 * sb), ("aux", na), ("stripes", 4 * stb), ("conv_head", nh)):
+        parts[name] = np.frombuffer(data, dtype=np.uint8, count=64 * n, offset=off)
+        off += 64 * n
+    shard = parts["shards"].reshape(32, -1)
+    return {
+        "model": dict(vocab=4096, hidden=512, layers=2, heads=2, head_dim=256, inter=1536, conv=4, seed=4321),
+        "state_seed": 77, "conv_seed_full_dims": 78,
+        "shard_beats": sb, "aux_beats": na, "stripe_beats": stb, "conv_head_beats": nh,
+        "shard_sha256": [sha(shard[c]) for c in range(32)],
+        "aux_sha256": sha(parts["aux"]),
+        "stripes_sha256": sha(parts["stripes"]),
+        "conv_head_sha256": sha(parts["conv_head"]),
+    }
+
+
 def decode_case(tmp: str, c: dict) -> dict:
     path = os.path.join(tmp, f"{c['name']}.bin")
     cmd = [DRIVER, "--seed", str(c["seed"]), "--stream-seed", str(c["stream_seed"]), "--stream", str(c["stream"]),
@@ -100,6 +127,7 @@ def main() -> None:
             "generator": "tests/golden/make_golden.py via oracle/_ref/gdn_ref_driver "
                          "(reference c_impl/gdn_model.cpp compiled natively through oracle/hls_shim)",
             "primitives": primitives(tmp),
+            "layouts": layouts(tmp),
             "decode": [decode_case(tmp, c) for c in DECODE_CASES],
         }
     with open(os.path.join(HERE, "reference_goldens.json"), "w") as f:
