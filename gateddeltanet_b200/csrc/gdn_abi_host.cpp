@@ -16,6 +16,7 @@
  */
 #include "../../include/gdn_model.h"
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <thread>
@@ -304,18 +305,24 @@ int gdn_validate_weight_shards(const float *wd, const GDNWeightHeader *c, Beat51
             fprintf(stderr, "gdn: run state has no host shard image (enable gdn_b200_set_abi_compat)\n");
             return -1;
         }
-    int bad = 0;
-    walk_shards(wd, c, [&](size_t ch, size_t off, const RowBlock &b) {
-        if (bad) return;
-        for (size_t j = 0; j < b.beats() && !bad; ++j) {
-            const Beat512 e = b.beat(j);
-            if (memcmp(&e, shards[ch] + off + j, sizeof(Beat512)) != 0) {
-                fprintf(stderr, "gdn: packed shard mismatch channel=%zu beat=%zu\n", ch, off + j);
-                bad = 1;
+    std::vector<std::pair<size_t, std::pair<size_t, RowBlock>>> blocks;
+    walk_shards(wd, c, [&](size_t ch, size_t off, const RowBlock &b) { blocks.push_back({ch, {off, b}}); });
+    std::atomic<int> bad{0};
+    parallel_for(blocks.size(), [&](size_t lo, size_t hi) {
+        for (size_t i = lo; i < hi && !bad.load(std::memory_order_relaxed); ++i) {
+            const size_t ch = blocks[i].first, off = blocks[i].second.first;
+            const RowBlock &b = blocks[i].second.second;
+            for (size_t j = 0; j < b.beats(); ++j) {
+                const Beat512 e = b.beat(j);
+                if (memcmp(&e, shards[ch] + off + j, sizeof(Beat512)) != 0) {
+                    if (bad.exchange(1) == 0)
+                        fprintf(stderr, "gdn: packed shard mismatch channel=%zu beat=%zu\n", ch, off + j);
+                    break;
+                }
             }
         }
     });
-    return bad ? -1 : 0;
+    return bad.load() ? -1 : 0;
 }
 
 /* c_impl/gdn_model.cpp:937-940 */
