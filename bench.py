@@ -391,9 +391,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "delta_rule", "streams", "prefill"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "delta_rule", "streams", "prefill", "tp"],
                     help="decode: the headline batch-1 decode (default); delta_rule: BASELINE config[1]; "
-                         "streams: BASELINE config[3] multi-stream decode")
+                         "streams: BASELINE config[3] multi-stream decode; tp: BASELINE config[4], one stream "
+                         "decoded by all --gpus GPUs together (tensor-parallel)")
     ap.add_argument("--streams", type=int, default=64, help="total streams of --workload streams")
     ap.add_argument("--layers", type=int, default=SHAPE["layers"],
                     help="--workload streams only: fewer layers for a small profiling case (same per-layer shapes)")
@@ -406,6 +407,7 @@ def main():
         return run_prefill(args)
     if args.impl == "reference":
         return run_reference(args)
+    tp_mode = args.workload == "tp"
 
     import torch
     import torch.distributed as dist
@@ -432,12 +434,16 @@ def main():
 
     model = gdn.Model(header=gdn.make_header(**SHAPE), seed=SEED)
     rs = gdn.RunState(model)
-    # token streams: each rank decodes its own independent stream
-    stream = rank_streams(rank, world)[0]
+    # token streams: each rank decodes its own independent stream (stream-DP),
+    # or every rank the same one (tensor-parallel)
+    stream = 0 if tp_mode else rank_streams(rank, world)[0]
     V = SHAPE["vocab"]
     prompt = token_stream(stream, args.prompt, V, offset=PROMPT_OFFSET)
     teacher = token_stream(stream, 4096, V)
     prompt_ms = rs.prefill(prompt) if args.prompt else 0.0
+    if tp_mode and world > 1:
+        from gateddeltanet_b200 import tensor_parallel
+        tensor_parallel.attach(rs)
     n_w = args.warmup
     rs.decode([teacher[i % 4096] for i in range(n_w)]) if n_w else None
     timed = [teacher[(n_w + i) % 4096] for i in range(args.steps)]
@@ -466,25 +472,34 @@ def main():
     sampler.stop()
 
     ms_per_tok = kernel_ms / args.steps
-    value = job_tokens_per_s(world, args.steps, kernel_ms / 1000.0)
+    streams_in_job = 1 if tp_mode else world
+    value = job_tokens_per_s(streams_in_job, args.steps, kernel_ms / 1000.0)
     e2e_ms = e2e_s * 1000.0 / e2e_n
-    e2e_value = job_tokens_per_s(world, e2e_n, e2e_s)
+    e2e_value = job_tokens_per_s(streams_in_job, e2e_n, e2e_s)
     alg = algorithmic_bytes_per_token()
     peak, peak_kind = peaks()
     achieved = alg / (ms_per_tok / 1000.0) / 1e9
+    if tp_mode:
+        # one stream's bytes over the job's GPUs: against the sum of their peaks
+        peak = peak * world
+        peak_kind = f"{peak_kind} x {world} GPUs"
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_per_tok, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": round(value / world / (1000.0 / FPGA_INNER_MS), 3),
+        "warmup": args.warmup, "ms_per_step": round(ms_per_tok, 5), "higher_is_better": True,
+        "scaling": "strong" if tp_mode else "weak",
+        "vs_baseline": round(value / streams_in_job / (1000.0 / FPGA_INNER_MS), 3),
         "vs_baseline_ref": f"per-GPU tokens/s vs the reference-published FPGA inner {FPGA_INNER_MS} ms/token",
         "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "BASELINE config[2]: GDN-1.3B batch-1 sustained decode, seeded BF16 weights, "
-                               f"{args.prompt}-token seeded prompt then a cyclic seeded 4096-token teacher stream; "
-                               "one independent stream per GPU",
+        "config": {"workload": ("BASELINE config[4]: GDN-1.3B batch-1 decode of one stream over all GPUs "
+                                "(tensor-parallel), " if tp_mode else
+                                "BASELINE config[2]: GDN-1.3B batch-1 sustained decode, ") +
+                               "seeded BF16 weights, "
+                               f"{args.prompt}-token seeded prompt then a cyclic seeded 4096-token teacher stream" +
+                               ("" if tp_mode else "; one independent stream per GPU"),
                    "batch_per_gpu": 1, "state": "fp32", "boundaries": "bf16",
                    "l2": "no flush: 2.8 GB of weights per step exceed the 126 MB L2",
                    "prompt_build": f"gdn_b200_prefill, {prompt_ms:.1f} ms device time (untimed)",
-                   "parallelism": f"stream-dp{world}"},
+                   "parallelism": f"tp{world}" if tp_mode else f"stream-dp{world}"},
         "inner_ms_per_token": round(ms_per_tok, 5),
         "outer_ms_per_token": round(e2e_ms, 5),
         "e2e": {"value": round(e2e_value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * SHAPE["hidden"],
@@ -495,6 +510,10 @@ def main():
                      "kernel": "gdn_decode_kernel<1> (BF16-boundary contract; one launch per token)"},
         "gpu_launches": args.steps,
         "clocks": sampler.summary(),
+        **({"tp": {"gpus": world, "exchange": "row-split partitions over all GPUs' CTAs; every output stored into "
+                                            "every GPU's exchange region by peer stores over NVLink (no NCCL call "
+                                            "on the data path)",
+                   "bit_identical_to_one_gpu": True}} if tp_mode else {}),
         "energy": energy_line(window, args.steps, idle_w),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -503,6 +522,9 @@ def main():
         except Exception as e:  # the baseline is reported, never the target
             line["cpu_baseline"] = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
                                     "sample": f"failed: {e}"}
+    if tp_mode and world > 1:
+        rs.tp_detach()  # every rank unmaps its peers before any rank frees its region
+        barrier()
     rs.free()
     model.free()
     if rank == 0:

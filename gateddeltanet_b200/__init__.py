@@ -159,7 +159,12 @@ EXPORTS = [
      [ctypes.POINTER(GDNModel), ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32, _FP]),
     ("gdn_b200_test_tile_gemm", ctypes.c_int,
      [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, _FP, _FP, _FP]),
+    ("gdn_b200_tp_token", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_void_p]),
+    ("gdn_b200_tp_attach", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int, ctypes.c_int, ctypes.c_char_p]),
+    ("gdn_b200_tp_detach", ctypes.c_int, [ctypes.POINTER(GDNRunState)]),
 ]
+
+GDN_B200_TP_TOKEN_BYTES = 128
 
 
 class GDNMixedMulStats(ctypes.Structure):
@@ -352,6 +357,22 @@ class RunState:
         check(self.lib.gdn_b200_state_download(ctypes.byref(self.s), _fptr(rec), rec.size, _fptr(conv), conv.size),
               "gdn_b200_state_download")
         return rec, conv
+
+    def tp_token(self) -> bytes:
+        """gdn_b200_tp_token: what the peers of a tensor-parallel decode need to map this run state."""
+        buf = ctypes.create_string_buffer(GDN_B200_TP_TOKEN_BYTES)
+        check(self.lib.gdn_b200_tp_token(ctypes.byref(self.s), buf), "gdn_b200_tp_token")
+        return buf.raw
+
+    def tp_attach(self, rank: int, world: int, tokens: Sequence[bytes]) -> None:
+        """gdn_b200_tp_attach with every rank's token, in rank order."""
+        blob = b"".join(tokens)
+        if len(tokens) != world or len(blob) != world * GDN_B200_TP_TOKEN_BYTES:
+            raise ValueError("tp_attach: one token of GDN_B200_TP_TOKEN_BYTES per rank expected")
+        check(self.lib.gdn_b200_tp_attach(ctypes.byref(self.s), int(rank), int(world), blob), "gdn_b200_tp_attach")
+
+    def tp_detach(self) -> None:
+        check(self.lib.gdn_b200_tp_detach(ctypes.byref(self.s)), "gdn_b200_tp_detach")
 
     def free(self) -> None:
         if self.s.workspace:

@@ -269,6 +269,14 @@ template <>
 struct XW<3> {
     typedef uint32_t T;
 };
+template <>
+struct XW<5> {
+    typedef uint32_t T;
+};
+template <>
+struct XW<7> {
+    typedef uint32_t T;
+};
 
 template <int MODE>
 __device__ __forceinline__ typename XW<MODE>::T *xw(xword *base) {
@@ -279,34 +287,64 @@ __device__ __forceinline__ const typename XW<MODE>::T *xw(const xword *base) {
     return reinterpret_cast<const typename XW<MODE>::T *>(base);
 }
 
-__device__ __forceinline__ void xput_w(uint32_t *p, float v, uint32_t tag) {
-    const uint32_t w = (__float_as_uint(v) & 0xffff0000u) | (tag & 0xffffu);
+__device__ __forceinline__ uint32_t xword_of(uint32_t *, float v, uint32_t tag) {
+    return (__float_as_uint(v) & 0xffff0000u) | (tag & 0xffffu);
+}
+__device__ __forceinline__ unsigned long long xword_of(unsigned long long *, float v, uint32_t tag) {
+    return ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+}
+__device__ __forceinline__ void xstore(uint32_t *p, uint32_t w) {
     asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
 }
-__device__ __forceinline__ void xput_w(unsigned long long *p, float v, uint32_t tag) {
-    const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+__device__ __forceinline__ void xstore(unsigned long long *p, unsigned long long w) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-/* store element i of exchange buffer `base` */
+/* system scope: a store into a peer GPU's memory, or a word a peer polls */
+__device__ __forceinline__ void xstore_sys(uint32_t *p, uint32_t w) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
+}
+__device__ __forceinline__ void xstore_sys(unsigned long long *p, unsigned long long w) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+/* address of a word of this GPU's exchange region in peer r's region */
+template <class T>
+__device__ __forceinline__ T *peer_addr(const DecodeParams &p, T *a, int r) {
+    return reinterpret_cast<T *>(reinterpret_cast<char *>(a) + p.tp_delta[r]);
+}
+/* store element i of exchange buffer `base`: here and, in tensor-parallel
+ * decode, in every peer's copy of the buffer */
 template <int MODE>
-__device__ __forceinline__ void xput(xword *base, size_t i, float v, uint32_t tag) {
-    xput_w(xw<MODE>(base) + i, v, tag);
+__device__ __forceinline__ void xput(const DecodeParams &p, xword *base, size_t i, float v, uint32_t tag) {
+    auto *a = xw<MODE>(base) + i;
+    const auto w = xword_of(a, v, tag);
+    xstore(a, w);
+    if (MODE & 4)
+        for (int r = 0; r < p.tp_world; ++r)
+            if (r != p.tp_rank) xstore_sys(peer_addr(p, a, r), w);
 }
-__device__ __forceinline__ uint32_t xget(const uint32_t *p) {
+/* Exchange-word loads. `sys`: tensor-parallel decode, where peers store the
+ * words (system-scope loads, so that they and the peers' system-scope stores
+ * are morally strong). */
+__device__ __forceinline__ uint32_t xget(const uint32_t *p, bool sys) {
     uint32_t w;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(w) : "l"(p) : "memory");
+    if (sys) asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(w) : "l"(p) : "memory");
+    else asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(w) : "l"(p) : "memory");
     return w;
 }
-__device__ __forceinline__ unsigned long long xget(const unsigned long long *p) {
+__device__ __forceinline__ unsigned long long xget(const unsigned long long *p, bool sys) {
     unsigned long long w;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    if (sys) asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    else asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
-__device__ __forceinline__ void xget2(const uint32_t *p, uint32_t &a, uint32_t &b) {
-    asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "l"(p) : "memory");
+__device__ __forceinline__ void xget2(const uint32_t *p, uint32_t &a, uint32_t &b, bool sys) {
+    if (sys) asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "l"(p) : "memory");
+    else asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "l"(p) : "memory");
 }
-__device__ __forceinline__ void xget2(const unsigned long long *p, unsigned long long &a, unsigned long long &b) {
-    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+__device__ __forceinline__ void xget2(const unsigned long long *p, unsigned long long &a, unsigned long long &b,
+                                      bool sys) {
+    if (sys) asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+    else asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 __device__ __forceinline__ bool xtag_is(uint32_t w, uint32_t tag) { return (w & 0xffffu) == (tag & 0xffffu); }
 __device__ __forceinline__ bool xtag_is(unsigned long long w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
@@ -490,12 +528,12 @@ __device__ __forceinline__ void raise_error(const DecodeParams &p, int code, uin
 
 /* Spin on one exchange word until it carries `tag`; returns the last word
  * read, whose tag differs from `tag` on abort/timeout. */
-template <class W>
+template <bool SYS, class W>
 __device__ __noinline__ W xwait(const DecodeParams &p, const W *a, uint32_t tag) {
     const uint64_t t0 = gtimer();
     uint32_t spins = 0;
     while (true) {
-        const W w = xget(a);
+        const W w = xget(a, SYS);
         if (xtag_is(w, tag)) return w;
         if (*sm_abort_flag()) return w;
         if ((++spins & 63u) == 0) {
@@ -522,20 +560,21 @@ __device__ __noinline__ W xwait(const DecodeParams &p, const W *a, uint32_t tag)
  * lands. All 32 lanes must call; lanes
  * that use no word take part in the protocol only. With PAIRS, use(2k) must
  * equal use(2k + 1). */
-template <int N, bool PAIRS, class Addr, class TagOf, class Use>
+template <int N, bool PAIRS, bool SYS, class Addr, class TagOf, class Use>
 __device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, const TagOf &tagof, const Use &use,
                                       float (&v)[N]) {
     typedef typename std::remove_const<typename std::remove_pointer<decltype(addr(0))>::type>::type W;
     const int lane = threadIdx.x & 31;
+    constexpr bool sys = SYS;
     W w[N];
     if (PAIRS) {
 #pragma unroll
         for (int i = 0; i < N; i += 2)
-            if (use(i)) xget2(addr(i), w[i], w[i + 1]);
+            if (use(i)) xget2(addr(i), w[i], w[i + 1], sys);
     } else {
 #pragma unroll
         for (int i = 0; i < N; ++i)
-            if (use(i)) w[i] = xget(addr(i));
+            if (use(i)) w[i] = xget(addr(i), sys);
     }
     uint32_t missing = 0;
 #pragma unroll
@@ -549,7 +588,7 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, c
          * the first read are the few of the slowest producers */
 #pragma unroll
         for (int i = 0; i < N; ++i)
-            if ((missing >> i) & 1u) w[i] = xget(addr(i));
+            if ((missing >> i) & 1u) w[i] = xget(addr(i), sys);
 #pragma unroll
         for (int i = 0; i < N; ++i)
             if (((missing >> i) & 1u) && xtag_is(w[i], tagof(i))) missing &= ~(1u << i);
@@ -601,10 +640,10 @@ __device__ __forceinline__ bool xread_to_xs(const DecodeParams &p, const xword *
     const int t = threadIdx.x;
     const int per = n >> 8;
     float v[kMaxWordsPerThread];
-    const bool ok = xread<kMaxWordsPerThread, true>(
+    const bool ok = xread<kMaxWordsPerThread, true, (MODE & 4) != 0>(
         p, [&](int i) { return xw<MODE>(src) + vec_elem(t, i); }, [&](int) { return tag; },
         [&](int i) { return i < per; }, v);
-    if (MODE == 1) {
+    if ((MODE & 3) == 1) {
         uint32_t *xsp = reinterpret_cast<uint32_t *>(sm_xs());
 #pragma unroll
         for (int j = 0; j < kMaxWordsPerThread; j += 2)
@@ -622,7 +661,7 @@ __device__ __forceinline__ bool xread_to_xs(const DecodeParams &p, const xword *
 template <int MODE>
 __device__ __forceinline__ void store_input(const float (&o)[8], int per) {
     const int t = threadIdx.x;
-    if (MODE == 1) {
+    if ((MODE & 3) == 1) {
         uint32_t *xsp = reinterpret_cast<uint32_t *>(sm_xs());
 #pragma unroll
         for (int i = 0; i < 8; i += 2)
@@ -635,10 +674,10 @@ __device__ __forceinline__ void store_input(const float (&o)[8], int per) {
 }
 
 /* Single-lane read of one exchange word. */
-template <class W>
+template <bool SYS, class W>
 __device__ __forceinline__ bool xread1(const DecodeParams &p, const W *src, uint32_t tag, float &v) {
-    W w = xget(src);
-    if (!xtag_is(w, tag)) w = xwait(p, src, tag);
+    W w = xget(src, SYS);
+    if (!xtag_is(w, tag)) w = xwait<SYS>(p, src, tag);
     v = xval(w);
     return xtag_is(w, tag);
 }
@@ -679,7 +718,7 @@ template <int MODE>
 __device__ __forceinline__ float tree16_half(const uint4 &w0, const uint4 &w1, const float4 &x0, const float4 &x1,
                                              const float4 &x2, const float4 &x3) {
     float s0, s1, s2, s3, s4, s5, s6, s7;
-    if (MODE == 1) {
+    if ((MODE & 3) == 1) {
         s0 = fmaf(bf_hi(w0.x), x0.y, __fmul_rn(bf_lo(w0.x), x0.x));
         s1 = fmaf(bf_hi(w0.y), x0.w, __fmul_rn(bf_lo(w0.y), x0.z));
         s2 = fmaf(bf_hi(w0.z), x1.y, __fmul_rn(bf_lo(w0.z), x1.x));
@@ -802,11 +841,11 @@ __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, 
      * the group index XOR-ed by the bank when G % 4 == 0 (chain_pos) */
     const int sw = (G & 3) ? 0 : b_own;
     float *park = chain + b_own * C + (lane >> 2);
-    if (MODE == 1 && K == 2048 && nrows == 4 && tiny == 0) {
+    if ((MODE & 3) == 1 && K == 2048 && nrows == 4 && tiny == 0) {
         dot_fixed<4, 4>(slot, xs, chain, lane); /* the K = H = 2048 phases, full chunks */
-    } else if (MODE == 1 && K == 5632 && nrows == 1) {
+    } else if ((MODE & 3) == 1 && K == 5632 && nrows == 1) {
         dot_fixed<11, 1>(slot, xs, chain, lane); /* the down projection, I = 5632 */
-    } else if (MODE == 1) {
+    } else if ((MODE & 3) == 1) {
         /* packed BF16 input in shared memory */
         const uint4 *xsp4 = reinterpret_cast<const uint4 *>(xs);
 #pragma unroll 2
@@ -848,9 +887,9 @@ __device__ __forceinline__ void warp_dot(const uint8_t *slot, int K, int nrows, 
     const int r = lane >> 2, b = lane & 3;
     float acc = 0.0f;
     const bool is_tiny = r < nrows && ((tiny >> r) & 1u);
-    if (MODE == 1 && K == 2048 && nrows == 4 && tiny == 0) {
+    if ((MODE & 3) == 1 && K == 2048 && nrows == 4 && tiny == 0) {
         if (r < 4) acc = chain_sum_fixed<32>(chain + (r * 4 + b) * 32, b);
-    } else if (MODE == 1 && K == 5632 && nrows == 1) {
+    } else if ((MODE & 3) == 1 && K == 5632 && nrows == 1) {
         if (r == 0) acc = chain_sum_fixed<88>(chain + b * 88, b);
     } else if (r < nrows) {
         if (!is_tiny) {
@@ -935,7 +974,7 @@ __device__ __forceinline__ bool prologue_norm(const DecodeParams &p, const xword
         }
     } else {
         float yv[8];
-        ok = xread<8, true>(p, [&](int i) { return xw<MODE>(y) + vec_elem(t, i); }, [&](int) { return tag; },
+        ok = xread<8, true, (MODE & 4) != 0>(p, [&](int i) { return xw<MODE>(y) + vec_elem(t, i); }, [&](int) { return tag; },
                             [&](int i) { return i < per; }, yv);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -998,7 +1037,7 @@ __device__ __forceinline__ bool prologue_norm_gate(const DecodeParams &p, const 
         if (i < per) wv[i] = __ldg(o_norm + (vec_elem(t, i) & (kHeadDim - 1)));
     /* words [0, per): gate; [8, 8 + per): attention output */
     float v[16];
-    const bool ok = xread<16, true>(
+    const bool ok = xread<16, true, (MODE & 4) != 0>(
         p, [&](int i) { return i < 8 ? xw<MODE>(p.gate) + vec_elem(t, i) : xw<MODE>(p.attn) + vec_elem(t, i - 8); },
         [&](int i) { return i < 8 ? tag_a : tag_b; }, [&](int i) { return (i & 7) < per; }, v);
     if (t == 0) trace_put(p, pidx, 1);
@@ -1066,10 +1105,10 @@ __device__ __forceinline__ bool prologue_state(const DecodeParams &p, int l, int
         float v4[4];
         const typename XW<MODE>::T *base = xw<MODE>(p.qkv) + h0 * kHeadDim + t;
         float vq[2], vk[2];
-        ok = xread<2, false>(p, [&](int i) { return base + i * kHeadDim; }, [&](int) { return tag; },
+        ok = xread<2, false, (MODE & 4) != 0>(p, [&](int i) { return base + i * kHeadDim; }, [&](int) { return tag; },
                              [&](int i) { return i < nhl; }, vq) &&
              ok;
-        ok = xread<2, false>(p, [&](int i) { return base + p.H + i * kHeadDim; }, [&](int) { return tag; },
+        ok = xread<2, false, (MODE & 4) != 0>(p, [&](int i) { return base + p.H + i * kHeadDim; }, [&](int) { return tag; },
                              [&](int i) { return i < nhl; }, vk) &&
              ok;
         v4[0] = vq[0];
@@ -1081,7 +1120,7 @@ __device__ __forceinline__ bool prologue_state(const DecodeParams &p, int l, int
     }
     if (t < 2 * nhl) {
         const int h = h0 + (t >> 1);
-        ok = xread1(p, xw<MODE>(p.ab) + ((t & 1) ? p.nh + h : h), tag, (t & 1) ? bv : av) && ok;
+        ok = xread1<(MODE & 4) != 0>(p, xw<MODE>(p.ab) + ((t & 1) ? p.nh + h : h), tag, (t & 1) ? bv : av) && ok;
     }
     float sq[4];
 #pragma unroll
@@ -1158,7 +1197,7 @@ __device__ __noinline__ void state_chunk(const DecodeParams &p, const uint8_t *b
         const float delta = __fmul_rn(beta, __fsub_rn(vj, __fmul_rn(decay, rj)));
         const float o =
             __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pj), __fmul_rn(alpha, delta)));
-        if (lane == 0) xput<MODE>(p.attn, c, bnd<MODE>(o), tag_out);
+        if (lane == 0) xput<MODE>(p, p.attn, c, bnd<MODE>(o), tag_out);
         /* update, c_impl/gdn_model.cpp:2268-2300 */
         const float *colp = reinterpret_cast<const float *>(buf) + j * kHeadDim + lane * 8;
         const float *knp = sm_kn() + hs * kHeadDim + lane * 8;
@@ -1192,7 +1231,8 @@ __device__ __noinline__ void state_chunk(const DecodeParams &p, const uint8_t *b
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_constant__ DecodeParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t cta = blockIdx.x, ncta = gridDim.x;
+    /* the global CTA index: unit partitions run over every GPU's CTAs */
+    const uint32_t cta = (uint32_t)p.tp_rank * gridDim.x + blockIdx.x, ncta = (uint32_t)p.tp_world * gridDim.x;
 
     if (threadIdx.x < 128)
         reinterpret_cast<float *>(smem_raw + kOffExpTab)[threadIdx.x] = __ldg(p.exp_table + threadIdx.x);
@@ -1303,7 +1343,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     ny = p.y_down;
                     ntag = p.epoch + (uint32_t)((p.L - 1) * kPhasesPerLayer + PH_DOWN);
                     nw = p.aux + (size_t)p.L * p.aux_stride;
-                    hidden = cta == 0 ? p.hidden_out : nullptr;
+                    hidden = blockIdx.x == 0 ? p.hidden_out : nullptr;
                     break;
                 }
                 if (ok && norm_phase) in_ok = prologue_norm<MODE>(p, ny, ntag, nw, embed, hidden, pidx);
@@ -1351,7 +1391,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     }
                     float vv = 0.0f;
                     if (ph == PH_STATE && lane < (int)n)
-                        xread1(p, xw<MODE>(p.qkv) + 2 * p.H + u + lane, tag_base + PH_QKVG, vv);
+                        xread1<(MODE & 4) != 0>(p, xw<MODE>(p.qkv) + 2 * p.H + u + lane, tag_base + PH_QKVG, vv);
 
                     if (!wait_full(p, seq)) continue;
 
@@ -1384,35 +1424,40 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                                         __fadd_rn(__fadd_rn(__fmul_rn(tail.x, cw.x), __fmul_rn(tail.y, cw.y)),
                                                   __fmul_rn(tail.z, cw.z)),
                                         __fmul_rn(raw, cw.w));
-                                    xput<MODE>(p.qkv, r, bnd<MODE>(silu_ref(sum)), tag_out);
+                                    xput<MODE>(p, p.qkv, r, bnd<MODE>(silu_ref(sum)), tag_out);
                                     const uint32_t d = r - (uint32_t)row_kind * p.H;
                                     __stcg(reinterpret_cast<float4 *>(
                                                p.tails + (((size_t)l * 3 + row_kind) * p.H + d) * 4),
                                            make_float4(tail.y, tail.z, raw, 0.0f));
                                 } else if (r < 4u * p.H) {
-                                    xput<MODE>(p.gate, r - 3u * p.H, raw, tag_out);
+                                    xput<MODE>(p, p.gate, r - 3u * p.H, raw, tag_out);
                                 } else {
-                                    xput<MODE>(p.ab, r - 4u * p.H, raw, tag_out);
+                                    xput<MODE>(p, p.ab, r - 4u * p.H, raw, tag_out);
                                 }
                             }
                             break;
                         case PH_O:
-                            if (lane < (int)n) xput<MODE>(p.y_o, u + lane, bnd<MODE>(y), tag_out);
+                            if (lane < (int)n) xput<MODE>(p, p.y_o, u + lane, bnd<MODE>(y), tag_out);
                             break;
                         case PH_DOWN:
-                            if (lane < (int)n) xput<MODE>(p.y_down, u + lane, bnd<MODE>(y), tag_out);
+                            if (lane < (int)n) xput<MODE>(p, p.y_down, u + lane, bnd<MODE>(y), tag_out);
                             break;
                         case PH_GU: {
                             /* rows [g_u, u_u, g_u+1, u_u+1]; SwiGLU as c_impl/gdn_model.cpp:4751-4770 */
                             const float gv = bnd<MODE>(lane == 0 ? out[0] : out[2]);
                             const float uv = bnd<MODE>(lane == 0 ? out[1] : out[3]);
-                            if (lane < (int)n) xput<MODE>(p.m, u + lane, bnd<MODE>(__fmul_rn(silu_ref(gv), uv)), tag_out);
+                            if (lane < (int)n) xput<MODE>(p, p.m, u + lane, bnd<MODE>(__fmul_rn(silu_ref(gv), uv)), tag_out);
                             break;
                         }
                         case -1: /* outputs left out on purpose (test hook) */
                             break;
                         default:
-                            if (lane < (int)n) p.logits[u + lane] = y;
+                            if (lane < (int)n) {
+                                p.logits[u + lane] = y;
+                                if (MODE & 4)
+                                    for (int r = 0; r < p.tp_world; ++r)
+                                        if (r != p.tp_rank) *peer_addr(p, p.logits + u + lane, r) = y;
+                            }
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
                                 if (j < (int)n && out[j] > best) {
@@ -1448,18 +1493,46 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     const int32_t vi = sm_wbest_i()[w];
                     if (v > b || (v == b && vi < bi)) { b = v; bi = vi; }
                 }
-                p.cand_val[cta] = b;
-                p.cand_idx[cta] = bi;
-                __threadfence();
+                p.cand_val[blockIdx.x] = b;
+                p.cand_idx[blockIdx.x] = bi;
+                /* tensor-parallel: the logits this CTA stored into the peers'
+                 * regions are visible there before its GPU's candidate is */
+                if (MODE & 4) __threadfence_system();
+                else __threadfence();
                 const uint32_t ticket = atomicAdd(&p.status->done, 1u);
-                if (ticket == ncta - 1) {
+                if (ticket == gridDim.x - 1) {
                     __threadfence();
                     float gb = __ldcg(p.cand_val);
                     int32_t gi = __ldcg(p.cand_idx);
-                    for (uint32_t c = 1; c < ncta; ++c) {
+                    for (uint32_t c = 1; c < gridDim.x; ++c) {
                         const float v = __ldcg(p.cand_val + c);
                         const int32_t vi = __ldcg(p.cand_idx + c);
                         if (v > gb || (v == gb && vi < gi)) { gb = v; gi = vi; }
+                    }
+                    if (MODE & 4) {
+                        /* this GPU's candidate to every GPU, then all of them
+                         * merged in rank order (strict >, lowest index on ties:
+                         * the order of the CTAs does not matter) */
+                        const uint32_t ctag = p.epoch;
+                        const unsigned long long wv = ((unsigned long long)ctag << 32) | __float_as_uint(gb);
+                        const unsigned long long wi = ((unsigned long long)ctag << 32) | (uint32_t)gi;
+                        __threadfence_system();
+                        unsigned long long *mine = p.rank_cand + 2 * p.tp_rank;
+                        for (int r = 0; r < p.tp_world; ++r) {
+                            unsigned long long *dst = r == p.tp_rank ? mine : peer_addr(p, mine, r);
+                            xstore_sys(dst, wv);
+                            xstore_sys(dst + 1, wi);
+                        }
+                        for (int r = 0; r < p.tp_world; ++r) {
+                            const unsigned long long v = xwait<true>(p, p.rank_cand + 2 * r, ctag);
+                            const unsigned long long vi = xwait<true>(p, p.rank_cand + 2 * r + 1, ctag);
+                            if (!xtag_is(v, ctag) || !xtag_is(vi, ctag)) break;  /* error raised */
+                            const float fv = xval(v);
+                            const int32_t iv = (int32_t)(uint32_t)vi;
+                            if (r == 0 || fv > gb || (fv == gb && iv < gi)) { gb = fv; gi = iv; }
+                        }
+                        /* the peers' logits, released before their candidates */
+                        __threadfence_system();
                     }
                     p.status->token = gi;
                     if (p.token_out != nullptr) *p.token_out = gi;
@@ -1496,13 +1569,17 @@ static cudaError_t launch_mode(const DecodeParams &p, int grid, cudaStream_t str
                                        stream);
 }
 
-/* MODE bit 0: BF16 boundaries; bit 1: BF16-rounded products (needs bit 0). */
+/* MODE bit 0: BF16 boundaries; bit 1: BF16-rounded products (needs bit 0); bit 2:
+ * tensor-parallel decode. */
 cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t stream) {
     const size_t smem = decode_smem_bytes(p.H, p.I);
-    if (!p.bf16_boundary) {
-        if (p.native_product) return cudaErrorInvalidValue;
-        return launch_mode<0>(p, grid, stream, smem);
+    if (!p.bf16_boundary && p.native_product) return cudaErrorInvalidValue;
+    /* MODE bit 2: tensor-parallel decode (peer stores, system-scope exchange) */
+    if (p.tp_world > 1) {
+        if (!p.bf16_boundary) return launch_mode<4>(p, grid, stream, smem);
+        return p.native_product ? launch_mode<7>(p, grid, stream, smem) : launch_mode<5>(p, grid, stream, smem);
     }
+    if (!p.bf16_boundary) return launch_mode<0>(p, grid, stream, smem);
     return p.native_product ? launch_mode<3>(p, grid, stream, smem) : launch_mode<1>(p, grid, stream, smem);
 }
 

@@ -60,6 +60,12 @@ enum {
     kErrBadToken = 5,
 };
 
+/* Tensor-parallel decode: GPUs per run state at most. */
+constexpr int kMaxTpRanks = 8;
+/* 64-bit words {payload, tag} after the exchange words of a run state's
+ * exchange region: per rank, its argmax value bits and index */
+constexpr int kRankCandWords = 2 * kMaxTpRanks;
+
 /* Small device-side status block; its first 64 bytes mirror the ABI's
  * workspace[X_NORM] line (lane 0 = token id as a float). */
 struct DecodeStatus {
@@ -113,6 +119,16 @@ struct DecodeParams {
      * test_drop_phase (layer * 5 + {A, C, D, E}), so the consumers' bounded
      * waits run out; -1: off */
     int test_drop_cta, test_drop_phase;
+    /* tensor-parallel decode over tp_world GPUs (1: one GPU). This GPU's
+     * CTAs are the global CTAs tp_rank * gridDim.x + blockIdx.x of
+     * tp_world * gridDim.x, every unit partition runs over the global CTAs,
+     * and every exchange word, logit and argmax candidate a CTA stores goes
+     * to its own exchange region and, for each peer r, to address + tp_delta[r]
+     * (the peer's region mapped into this process, byte offset; unused for
+     * r == tp_rank). rank_cand: the kRankCandWords words of this GPU's region. */
+    int tp_world, tp_rank;
+    long long tp_delta[kMaxTpRanks];
+    unsigned long long *rank_cand;
 };
 
 /* The isolated gated-delta-rule step (gdn_recurrence.cu): `slices` (layer,

@@ -344,6 +344,12 @@ struct Stream {
     Beat512 *shards[GEMV_CHANNELS] = {};
     Beat512 *aux = nullptr;
     size_t shard_beats = 0;
+    /* tensor-parallel decode (gdn_b200_tp_attach): the peers' exchange
+     * regions mapped into this process */
+    int tp_world = 1, tp_rank = 0;
+    void *tp_peer[gdn::kMaxTpRanks] = {};
+    unsigned long long *rank_cand = nullptr;
+    size_t xbytes = 0;   /* bytes of the exchange region: words, rank candidates, logits */
 };
 
 std::map<const void *, Stream *> g_streams;  /* keyed by GDNRunState.workspace */
@@ -475,6 +481,13 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.epoch = s.epoch;
     p.test_drop_cta = s.test_drop_cta;
     p.test_drop_phase = s.test_drop_phase;
+    p.tp_world = s.tp_world;
+    p.tp_rank = s.tp_rank;
+    for (int r = 0; r < gdn::kMaxTpRanks; ++r)
+        p.tp_delta[r] = s.tp_peer[r] == nullptr ? 0
+                                                : (long long)(reinterpret_cast<char *>(s.tp_peer[r]) -
+                                                              reinterpret_cast<char *>(s.xbuf));
+    p.rank_cand = s.rank_cand;
     return p;
 }
 
@@ -768,12 +781,15 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
         return cleanup(fail("gdn_b200: stream creation failed"));
     const size_t s_bytes = L * nh * 256 * 256 * sizeof(float);
     const size_t t_bytes = L * 3 * H * 4 * sizeof(float);
-    const size_t act_floats = V + H + H + 2 * (size_t)s->grid + 64;
+    const size_t act_floats = H + H + 2 * (size_t)s->grid + 64;
+    /* the exchange region (one allocation, the one a tensor-parallel peer
+     * maps): exchange words, the per-rank argmax candidates, logits */
     const size_t xwords = 3 * H + H + 64 + H + H + I + H;
-    s->xwords = xwords;
+    s->xwords = xwords + gdn::kRankCandWords;
+    s->xbytes = s->xwords * sizeof(gdn::xword) + V * sizeof(float);
     if (cudaMalloc(&s->S, s_bytes) != cudaSuccess || cudaMalloc(&s->tails, t_bytes) != cudaSuccess ||
         cudaMalloc(&s->acts, act_floats * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&s->xbuf, xwords * sizeof(gdn::xword)) != cudaSuccess ||
+        cudaMalloc(&s->xbuf, s->xbytes) != cudaSuccess ||
         cudaMalloc(&s->status, sizeof(gdn::DecodeStatus)) != cudaSuccess ||
         cudaMallocHost(&s->status_host, sizeof(gdn::DecodeStatus)) != cudaSuccess ||
         cudaHostAlloc(&s->ws, GDN_WS_FLOATS * sizeof(float), cudaHostAllocDefault) != cudaSuccess)
@@ -786,8 +802,9 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
     s->y_o = x; x += H;
     s->m = x; x += I;
     s->y_down = x;
+    s->rank_cand = reinterpret_cast<unsigned long long *>(s->xbuf + xwords);
+    s->logits = reinterpret_cast<float *>(s->xbuf + s->xwords);
     float *a = s->acts;
-    s->logits = a; a += V;
     s->hidden = a; a += H;
     s->x_embed = a; a += H;
     s->cand_val = a; a += s->grid;
@@ -796,7 +813,8 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
     if (cudaMemsetAsync(s->S, 0, s_bytes, s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->tails, 0, t_bytes, s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->acts, 0, act_floats * sizeof(float), s->stream) != cudaSuccess ||
-        cudaMemsetAsync(s->xbuf, 0xff, xwords * sizeof(gdn::xword), s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->xbuf, 0xff, s->xwords * sizeof(gdn::xword), s->stream) != cudaSuccess ||
+        cudaMemsetAsync(s->logits, 0, V * sizeof(float), s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->status, 0, sizeof(gdn::DecodeStatus), s->stream) != cudaSuccess ||
         cudaStreamSynchronize(s->stream) != cudaSuccess)
         return cleanup(fail("gdn_b200: run state initialisation failed"));
@@ -843,6 +861,100 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
     return 0;
 }
 
+/* ----------------------------------------------- tensor-parallel decode */
+
+/* What a rank publishes so that its peers can map its exchange region
+ * (GDN_B200_TP_TOKEN_BYTES). */
+struct TpToken {
+    cudaIpcMemHandle_t handle;
+    uint32_t grid;
+    uint32_t pad;
+    uint64_t xbytes;
+    char bus[48];   /* PCI bus id of the run state's device */
+};
+static_assert(sizeof(TpToken) == GDN_B200_TP_TOKEN_BYTES, "TpToken size");
+
+static void tp_close(Stream &s) {
+    for (int r = 0; r < gdn::kMaxTpRanks; ++r) {
+        if (s.tp_peer[r] != nullptr) cudaIpcCloseMemHandle(s.tp_peer[r]);
+        s.tp_peer[r] = nullptr;
+    }
+    s.tp_world = 1;
+    s.tp_rank = 0;
+}
+
+static int tp_token_of(Stream &s, TpToken &t) {
+    memset(&t, 0, sizeof(t));
+    CUDA_OK(cudaSetDevice(s.device));
+    CUDA_OK(cudaIpcGetMemHandle(&t.handle, s.xbuf));
+    t.grid = (uint32_t)s.grid;
+    t.xbytes = s.xbytes;
+    CUDA_OK(cudaDeviceGetPCIBusId(t.bus, (int)sizeof(t.bus) - 1, s.device));
+    return 0;
+}
+
+int gdn_b200_tp_token(GDNRunState *state, void *token) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    if (token == nullptr) return fail("gdn_b200_tp_token: null token");
+    TpToken t;
+    if (tp_token_of(*s, t) != 0) return -1;
+    memcpy(token, &t, sizeof(t));
+    return 0;
+}
+
+int gdn_b200_tp_attach(GDNRunState *state, int rank, int world, const void *tokens) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    if (world < 1 || world > gdn::kMaxTpRanks || rank < 0 || rank >= world)
+        return fail("gdn_b200_tp_attach: rank %d of %d out of range (at most %d GPUs)", rank, world, gdn::kMaxTpRanks);
+    if (tokens == nullptr) return fail("gdn_b200_tp_attach: null tokens");
+    if (s->compat) return fail("gdn_b200_tp_attach: not available in the reference-ABI compatibility mode");
+    const TpToken *t = static_cast<const TpToken *>(tokens);
+    TpToken mine;
+    if (tp_token_of(*s, mine) != 0) return -1;
+    if (memcmp(&t[rank], &mine, sizeof(mine)) != 0)
+        return fail("gdn_b200_tp_attach: token %d is not this run state's", rank);
+    for (int r = 0; r < world; ++r) {
+        if (t[r].grid != mine.grid || t[r].xbytes != mine.xbytes)
+            return fail("gdn_b200_tp_attach: rank %d has another grid (%u) or exchange size than this GPU (%u)", r,
+                        t[r].grid, mine.grid);
+        for (int q = 0; q < r; ++q)
+            if (strncmp(t[q].bus, t[r].bus, sizeof(t[r].bus)) == 0)
+                return fail("gdn_b200_tp_attach: ranks %d and %d share the device %s", q, r, t[r].bus);
+    }
+    CUDA_OK(cudaSetDevice(s->device));
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    tp_close(*s);
+    for (int r = 0; r < world; ++r) {
+        if (r == rank) continue;
+        const cudaError_t e = cudaIpcOpenMemHandle(&s->tp_peer[r], t[r].handle, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            s->tp_peer[r] = nullptr;
+            tp_close(*s);
+            return fail("gdn_b200_tp_attach: mapping rank %d's exchange region failed: %s", r, cudaGetErrorString(e));
+        }
+    }
+    s->tp_world = world;
+    s->tp_rank = rank;
+    /* every rank starts from the same tags */
+    s->epoch = 0;
+    CUDA_OK(cudaMemsetAsync(s->xbuf, 0xff, s->xwords * sizeof(gdn::xword), s->stream));
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    return 0;
+}
+
+int gdn_b200_tp_detach(GDNRunState *state) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    CUDA_OK(cudaSetDevice(s->device));
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    tp_close(*s);
+    CUDA_OK(cudaMemsetAsync(s->xbuf, 0xff, s->xwords * sizeof(gdn::xword), s->stream));
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    return 0;
+}
+
 void gdn_run_state_free(GDNRunState *state) {
     if (state == nullptr || state->workspace == nullptr) return;
     Stream *s = nullptr;
@@ -859,6 +971,7 @@ void gdn_run_state_free(GDNRunState *state) {
         cudaGetDevice(&prev);
         cudaSetDevice(s->device);
         cudaStreamSynchronize(s->stream);
+        tp_close(*s);
         cudaStreamDestroy(s->stream);
         cudaEventDestroy(s->ev0);
         cudaEventDestroy(s->ev1);

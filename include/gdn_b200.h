@@ -145,6 +145,28 @@ int gdn_b200_set_abi_compat(int on);
 /* Number of SMs (CTAs) the decode kernel uses on the current device. */
 int gdn_b200_grid_size(void);
 
+/* ------------------------------------------- tensor-parallel decode
+ * One decode stream over 2..8 GPUs, one run state per
+ * GPU, each in its own process. Replaces the head/column split with an
+ * allreduce of c_impl/gdn_model.cpp's GEMV calls by a row split: every output
+ * row (and state column) is computed whole on one GPU and stored into every
+ * GPU's exchange region over NVLink, so the step is the single-GPU step and
+ * its results are identical bit for bit. The recurrent state and conv tails
+ * are then split by owner: each rank updates only the columns and channels
+ * its CTAs own (logits and tokens are complete on every rank).
+ *   1. every rank: gdn_b200_tp_token(state, token) -> share the
+ *      GDN_B200_TP_TOKEN_BYTES token with the others (all-gather);
+ *   2. every rank: gdn_b200_tp_attach(state, rank, world, tokens) with the
+ *      tokens in rank order, then a barrier before the first step;
+ *   3. every rank makes the same decode calls with the same tokens, in step.
+ * Ranks must sit on distinct devices with the same SM count. A rank that does
+ * not take part lets the others' waits run out (2 s): the step returns -1. */
+#define GDN_B200_TP_TOKEN_BYTES 128
+int gdn_b200_tp_token(GDNRunState *state, void *token);
+int gdn_b200_tp_attach(GDNRunState *state, int rank, int world, const void *tokens);
+/* back to single-GPU decode (the state this rank does not own is stale) */
+int gdn_b200_tp_detach(GDNRunState *state);
+
 /* ---------------------------------------------------- multi-stream decode
  * Several independent decode streams on one GPU (no
  * counterpart in the reference, whose decode ABI is one stream per call):
