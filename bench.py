@@ -509,7 +509,9 @@ def main():
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(),
                      "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg,
-                     "kernel": "gdn_decode_kernel<1> (BF16-boundary contract; one launch per token)"},
+                     "kernel": ("gdn_decode_kernel<5> (tensor-parallel, BF16-boundary contract; one launch per "
+                                "token per GPU)" if tp_mode and world > 1 else
+                                "gdn_decode_kernel<1> (BF16-boundary contract; one launch per token)")},
         "gpu_launches": args.steps,
         "clocks": sampler.summary(),
         **({"tp": {"gpus": world, "exchange": "row-split partitions over all GPUs' CTAs; every output stored into "
