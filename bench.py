@@ -41,17 +41,42 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "GDN-1.3B batch-1 decode ms/token (inner+outer) & % HBM roofline; streams tok/s"
+WORKLOAD_TEXT = ("BASELINE config[2]: GDN-1.3B batch-1 sustained decode, seeded BF16 weights, seeded prompt then a "
+                 "cyclic seeded 4096-token teacher stream")
 FPGA_INNER_MS = 8.141  # reference-published inner ms/token (Alveo U55C)
 from gateddeltanet_b200.workload import (PROMPT_OFFSET, SEED, SHAPE, STREAM_SEED, job_tokens_per_s,  # noqa: E402
                                          max_over_ranks, rank_streams, token_stream)
 
 
-def algorithmic_bytes_per_token(s=SHAPE) -> int:
-    """Per-token HBM bytes at batch 1 (weights read once, state read+written once)."""
+NUMERICS = {  # gdn_b200_set_numerics contracts
+    "cimpl": (True, True, True),    # the reference's own arithmetic (default; BF16 state)
+    "engine": (True, False, False),  # exact products, FP32 state
+    "fp32": (False, False, False),   # the FP32 control
+}
+KERNEL_MODE = {"cimpl": 11, "engine": 1, "fp32": 0}
+
+
+def state_bytes_per_value(numerics: str) -> int:
+    return 2 if NUMERICS[numerics][2] else 4
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def algorithmic_bytes_per_token(s=SHAPE, numerics: str = "cimpl") -> int:
+    """Per-token HBM bytes at batch 1 (weights read once, state read+written
+    once, in the contract's storage: BF16 for c_impl, FP32 otherwise)."""
     H, I, V, L, nh = s["hidden"], s["inter"], s["vocab"], s["layers"], s["heads"]
     gemv = 2 * (L * (4 * H * H + 2 * nh * H + H * H + 2 * I * H + I * H) + V * H)
     aux = 4 * (L * (H + 256 + H + 12 * H + 2 * nh) + H)
-    state = 2 * L * nh * 256 * 256 * 4
+    state = 2 * L * nh * 256 * 256 * state_bytes_per_value(numerics)
     tails = L * 3 * H * 16 * 2
     io = 2 * H + 4 * V + 4
     return gemv + aux + state + tails + io
@@ -165,6 +190,7 @@ def cpu_baseline_port(n_tokens: int = 3):
         times.append(time.perf_counter() - t)
     ms = statistics.median(times) * 1000.0
     return {"value": round(1000.0 / ms, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "cpu_model": cpu_model(),
             "sample": f"{n_tokens} GDN-1.3B decode tokens (oracle/gdn_oracle.c, reference arithmetic: BF16 products, "
                       f"BF16 state), median {ms:.1f} ms/token, weight synthesis {setup:.1f} s untimed"}
 
@@ -180,22 +206,24 @@ def run_reference(args):
                           "(the reference sources are needed to build it)"}))
         return 0
     warm = min(args.warmup, 1)
-    budget_ms = 60000.0
     out = subprocess.run([driver, "--seed", str(SEED), "--stream-seed", str(STREAM_SEED), "--warmup", str(warm),
-                          "--steps", str(args.steps), "--budget-ms", str(budget_ms)],
+                          "--steps", str(args.steps)],
                          capture_output=True, text=True, check=True)
     res = json.loads(out.stdout.strip().splitlines()[-1])
     ms = float(res["mean_ms_per_token"])
     tps = 1000.0 / ms
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tps, 5), "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "steps": int(res["steps"]), "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "GDN-1.3B batch-1 teacher-forced decode (seeded weights and token stream)",
-                   "batch": 1},
+        "config": {"workload": WORKLOAD_TEXT,
+                   "batch_per_gpu": 1, "numerics": "cimpl (the reference's own arithmetic)",
+                   "note": "the reference's per-token CPU cost does not depend on the recurrent state, so its "
+                           "stream starts from zero state instead of the prefilled prompt state"},
         "cpu_baseline": {"value": round(tps, 5), "unit": "tokens/s", "cores": 1, "kind": "reference",
+                         "cpu_model": cpu_model(),
                          "sample": f"{res['steps']} timed tokens after {warm} warm-up (reference gdn_decode_step_host, "
-                                   f"native build, single-threaded monolith; bounded to {budget_ms / 1000:.0f} s)"},
+                                   f"native build, single-threaded monolith)"},
         "e2e": {"value": round(tps, 5), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -382,6 +410,62 @@ def run_streams(args):
     return 0
 
 
+def sustained_window(rs, teacher, start, seconds, device, idle_w, barrier):
+    """Decode the cyclic teacher stream for >= `seconds` of device time in
+    4096-token device-resident calls (inner ms/token, clocks and NVML energy
+    over that window), then for about as long through gdn_decode_step_host
+    with host buffers (outer ms/token)."""
+    meter, _ = energy_meter(device)
+    sampler = ClockSampler(device)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    if meter is not None:
+        meter.start()
+    dev_ms, tokens, pos = 0.0, 0, start
+    t0 = time.perf_counter()
+    while dev_ms < seconds * 1000.0:
+        chunk = [teacher[(pos + i) % 4096] for i in range(4096)]
+        _, ms = rs.decode(chunk)
+        dev_ms += ms
+        tokens += len(chunk)
+        pos += len(chunk)
+    wall = time.perf_counter() - t0
+    win = meter.stop() if meter is not None else None
+    barrier()
+    sampler.stop()
+    out_n, t1 = 0, time.perf_counter()
+    while time.perf_counter() - t1 < min(seconds, 20.0):
+        for _ in range(256):
+            rs.step(teacher[(pos + out_n) % 4096])
+            out_n += 1
+    outer_s = time.perf_counter() - t1
+    return {"tokens": tokens, "device_s": round(dev_ms / 1000.0, 3), "wall_s": round(wall, 3),
+            "inner_ms_per_token": round(dev_ms / tokens, 5),
+            "outer_tokens": out_n, "outer_ms_per_token": round(outer_s * 1000.0 / out_n, 5),
+            "clocks": sampler.summary(), "energy": energy_line(win, tokens, idle_w),
+            "note": "after the main timed tokens; inner = device-resident loop (CUDA events), outer = "
+                    "gdn_decode_step_host per token with host buffers (wall clock)"}
+
+
+def contract_timing(model, teacher, numerics, device):
+    """ms/token and roofline of another numeric contract on its own run state
+    (zero state, 64 warm-up and 1024 timed tokens)."""
+    import gateddeltanet_b200 as gdn
+    rs = gdn.RunState(model)
+    rs.set_numerics(*NUMERICS[numerics])
+    rs.decode([teacher[i] for i in range(64)])
+    _, ms = rs.decode([teacher[(64 + i) % 4096] for i in range(1024)])
+    rs.free()
+    ms_tok = ms / 1024
+    alg = algorithmic_bytes_per_token(numerics=numerics)
+    peak, peak_kind = peaks()
+    return {"numerics": numerics, "ms_per_token": round(ms_tok, 5), "tokens_per_s": round(1000.0 / ms_tok, 2),
+            "roofline": {"achieved": round(alg / (ms_tok / 1000.0) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(alg / (ms_tok / 1000.0) / 1e9 / peak, 4), "algorithmic_bytes_per_launch": alg,
+                         "kernel": f"gdn_decode_kernel<{KERNEL_MODE[numerics]}>"}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -390,6 +474,11 @@ def main():
     ap.add_argument("--prompt", type=int, default=4096)
     ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--numerics", default="cimpl", choices=sorted(NUMERICS),
+                    help="numeric contract of the timed decode: cimpl (default, the reference's own arithmetic, "
+                         "bit-exact), engine (exact products, FP32 state), fp32 (the FP32 control)")
+    ap.add_argument("--sustain-s", type=float, default=20.0,
+                    help="length of the sustained window (config[2], energy per token); 0 skips it")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="decode", choices=["decode", "delta_rule", "streams", "prefill", "tp"],
                     help="decode: the headline batch-1 decode (default); delta_rule: BASELINE config[1]; "
@@ -434,6 +523,7 @@ def main():
 
     model = gdn.Model(header=gdn.make_header(**SHAPE), seed=SEED)
     rs = gdn.RunState(model)
+    rs.set_numerics(*NUMERICS[args.numerics])
     # token streams: each rank decodes its own independent stream (stream-DP),
     # or every rank the same one (tensor-parallel)
     stream = 0 if tp_mode else rank_streams(rank, world)[0]
@@ -473,12 +563,23 @@ def main():
     barrier()
     sampler.stop()
 
+    # sustained window (config[2]): >= --sustain-s of device-resident decode of
+    # the cyclic teacher stream, then as long through gdn_decode_step_host,
+    # with NVML energy and clocks over the inner window
+    sustained = None
+    if args.sustain_s > 0 and not tp_mode:
+        sustained = sustained_window(rs, teacher, n_w + args.steps, args.sustain_s, local, idle_w, barrier)
+    # the other contract beside the headline one: a short timing of the
+    # engine contract (exact products, FP32 state) on its own run state
+    other = None
+    if not tp_mode and args.numerics == "cimpl":
+        other = contract_timing(model, teacher, "engine", local)
     ms_per_tok = kernel_ms / args.steps
     streams_in_job = 1 if tp_mode else world
     value = job_tokens_per_s(streams_in_job, args.steps, kernel_ms / 1000.0)
     e2e_ms = e2e_s * 1000.0 / e2e_n
     e2e_value = job_tokens_per_s(streams_in_job, e2e_n, e2e_s)
-    alg = algorithmic_bytes_per_token()
+    alg = algorithmic_bytes_per_token(numerics=args.numerics)
     peak, peak_kind = peaks()
     achieved = alg / (ms_per_tok / 1000.0) / 1e9
     if tp_mode:
@@ -498,7 +599,10 @@ def main():
                                "seeded BF16 weights, "
                                f"{args.prompt}-token seeded prompt then a cyclic seeded 4096-token teacher stream" +
                                ("" if tp_mode else "; one independent stream per GPU"),
-                   "batch_per_gpu": 1, "state": "fp32", "boundaries": "bf16",
+                   "batch_per_gpu": 1, "numerics": args.numerics,
+                   "state": "bf16" if NUMERICS[args.numerics][2] else "fp32",
+                   "boundaries": "bf16" if NUMERICS[args.numerics][0] else "fp32",
+                   "products": "bf16-rounded (reference)" if NUMERICS[args.numerics][1] else "exact",
                    "l2": "no flush: 2.8 GB of weights per step exceed the 126 MB L2",
                    "prompt_build": f"gdn_b200_prefill, {prompt_ms:.1f} ms device time (untimed)",
                    "parallelism": f"tp{world}" if tp_mode else f"stream-dp{world}"},
@@ -509,9 +613,10 @@ def main():
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(),
                      "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg,
-                     "kernel": ("gdn_decode_kernel<5> (tensor-parallel, BF16-boundary contract; one launch per "
-                                "token per GPU)" if tp_mode and world > 1 else
-                                "gdn_decode_kernel<1> (BF16-boundary contract; one launch per token)")},
+                     "kernel": (f"gdn_decode_kernel<{KERNEL_MODE[args.numerics] + 4}> (tensor-parallel, {args.numerics} "
+                                "contract; one launch per token per GPU)" if tp_mode and world > 1 else
+                                f"gdn_decode_kernel<{KERNEL_MODE[args.numerics]}> ({args.numerics} contract; one "
+                                "launch per token)")},
         "gpu_launches": args.steps,
         "clocks": sampler.summary(),
         **({"tp": {"gpus": world, "exchange": "row-split partitions over all GPUs' CTAs; every output stored into "
@@ -519,6 +624,8 @@ def main():
                                             "on the data path)",
                    "bit_identical_to_one_gpu": True}} if tp_mode else {}),
         "energy": energy_line(window, args.steps, idle_w),
+        **({"sustained": sustained} if sustained is not None else {}),
+        **({"other_contract": other} if other is not None else {}),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:

@@ -136,6 +136,7 @@ EXPORTS = [
     ("gdn_b200_delta_rule_step", ctypes.c_int,
      [ctypes.c_uint32, _FP, _FP, _FP, _FP, _FP, _FP, _FP, ctypes.c_uint32, _FP]),
     ("gdn_b200_test_drop_outputs", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int, ctypes.c_int]),
+    ("gdn_b200_test_force_exact_products", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int]),
     ("gdn_b200_grid_size", ctypes.c_int, []),
     ("gdn_b200_batch_create", ctypes.c_void_p, [ctypes.POINTER(GDNModel), ctypes.c_uint32]),
     ("gdn_b200_batch_free", None, [ctypes.c_void_p]),
@@ -339,11 +340,22 @@ class RunState:
               "gdn_b200_fetch_outputs")
         return logits, hidden
 
-    def set_numerics(self, bf16_boundary: bool = True, bf16_products: bool = False, bf16_state: bool = False) -> None:
-        """Engine default (True, False, False); the c_impl's own arithmetic is
-        (True, True, True); the FP32 control is (False, False, False)."""
+    # the supported numeric contracts (gdn_b200_set_numerics)
+    CIMPL = (True, True, True)
+    ENGINE = (True, False, False)
+    FP32 = (False, False, False)
+
+    def set_numerics(self, bf16_boundary: bool = True, bf16_products: bool = True, bf16_state: bool = True) -> None:
+        """The c_impl contract (True, True, True) is the default; (True, False,
+        False) exact products with FP32 state; (False, False, False) the FP32
+        control."""
         check(self.lib.gdn_b200_set_numerics(ctypes.byref(self.s), int(bool(bf16_boundary)), int(bool(bf16_products)),
                                              int(bool(bf16_state))), "gdn_b200_set_numerics")
+
+    def force_exact_products(self, on: bool = True) -> None:
+        """Test hook: the exact emulation of the BF16 product in every phase."""
+        check(self.lib.gdn_b200_test_force_exact_products(ctypes.byref(self.s), int(bool(on))),
+              "gdn_b200_test_force_exact_products")
 
     def load_state(self, rec: np.ndarray, conv: np.ndarray) -> None:
         rec = np.ascontiguousarray(rec, dtype=np.float32)

@@ -43,7 +43,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return LIB
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-O3",
+    cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-O3,-ffp-contract=off",
            "-I", os.path.join(REPO, "include"), "-I", CSRC, "-o", tmp,
            *[os.path.join(CSRC, s) for s in SOURCES], "-lpthread",
            "-Xlinker", "--version-script=" + os.path.join(CSRC, "exports.map")]

@@ -30,7 +30,8 @@
 namespace gdn {
 int host_fail(const char *msg);
 int host_device();
-int host_state_buffers(GDNRunState *state, float **S, float **tails, int *device, cudaStream_t *stream);
+int host_state_begin(GDNRunState *state, float **S, float **tails, int *device, cudaStream_t *stream);
+int host_state_end(GDNRunState *state, float *S, bool write_back);
 }  // namespace gdn
 
 using namespace gdn::bt;
@@ -665,22 +666,13 @@ int gdn_b200_batch_fetch_logits(GdnB200Batch *b, float *logits) {
  * recurrence in token order on the run state's own S and tails. FP32
  * contract; the run state ends as if the tokens had been decoded one by one
  * (within FP32 summation-order differences), with no logits computed. */
-int gdn_b200_prefill(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n, float *device_ms) {
-    if (model == nullptr || state == nullptr || (tokens == nullptr && n > 0))
-        return bfail("gdn_b200 prefill: null argument");
-    if (n == 0) {
-        if (device_ms) *device_ms = 0.0f;
-        return 0;
-    }
+static int prefill_on(const GDNModel *model, const int32_t *tokens, uint32_t n, float *device_ms, float *S,
+                      float *tails, int device, cudaStream_t stream) {
     const GDNWeightHeader &c = model->config;
     if (batch_supports(c, 1) != 0) return -1;
     for (uint32_t i = 0; i < n; ++i)
         if (tokens[i] < 0 || (uint32_t)tokens[i] >= c.vocab_size)
             return bfail("gdn_b200 prefill: token %d at %u out of range", tokens[i], i);
-    float *S = nullptr, *tails = nullptr;
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    if (gdn::host_state_buffers(state, &S, &tails, &device, &stream) != 0) return -1;
     BT_OK(cudaSetDevice(device));
     /* the tile image stays cached with the model once built */
     TileModel *tm = acquire_tile_model(model, device);
@@ -804,6 +796,25 @@ int gdn_b200_prefill(const GDNModel *model, GDNRunState *state, const int32_t *t
     if (rc == 0 && device_ms) cudaEventElapsedTime(device_ms, e0, e1);
     cleanup();
     return rc;
+}
+
+/* The run state's recurrent state is converted to natural FP32 for the
+ * prefill kernels and written back into its own storage afterwards (rounded
+ * to BF16 when the run state keeps the c_impl contract's BF16 state). */
+int gdn_b200_prefill(const GDNModel *model, GDNRunState *state, const int32_t *tokens, uint32_t n, float *device_ms) {
+    if (model == nullptr || state == nullptr || (tokens == nullptr && n > 0))
+        return bfail("gdn_b200 prefill: null argument");
+    if (n == 0) {
+        if (device_ms) *device_ms = 0.0f;
+        return 0;
+    }
+    float *S = nullptr, *tails = nullptr;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    if (gdn::host_state_begin(state, &S, &tails, &device, &stream) != 0) return -1;
+    const int rc = prefill_on(model, tokens, n, device_ms, S, tails, device, stream);
+    const int rc2 = gdn::host_state_end(state, S, rc == 0);
+    return rc != 0 ? rc : rc2;
 }
 
 /* Test hook: Y[n][m] = sum_k W[m][k] X[n][k] through one tile-GEMM launch

@@ -147,13 +147,28 @@ int engine_supports(const GDNWeightHeader &c) {
     if (c.head_dim != 256) return fail("gdn_b200: head_dim must be 256 (got %u)", c.head_dim);
     if (c.conv_size != 4) return fail("gdn_b200: conv_size must be 4 (got %u)", c.conv_size);
     if (H % 512 || I % 512 || H == 0 || I == 0) return fail("gdn_b200: hidden and intermediate must be multiples of 512");
-    if (2 * I > (uint32_t)gdn::kSlotBytes) return fail("gdn_b200: intermediate must be at most %d", gdn::kSlotBytes / 2);
+    if (c.vocab_size % 16) return fail("gdn_b200: vocab must be a multiple of 16 (the LM head's 16-row tiles)");
     if (c.num_heads > 8 || H > GDN_WSF_HID) return fail("gdn_b200: at most 8 heads (hidden <= 2048)");
     if (I > GDN_WSF_MLP || c.vocab_size > GDN_WSF_LOGITS || c.vocab_size == 0)
         return fail("gdn_b200: intermediate/vocab exceed the workspace ABI");
     if ((size_t)c.num_layers * c.num_heads * 256 * 256 > GDN_WSF_STATE ||
         (size_t)c.num_layers * 3 * 3 * H > GDN_WSF_HEADBUF || c.num_layers == 0)
         return fail("gdn_b200: layer count exceeds the workspace ABI");
+    return 0;
+}
+
+/* Per-CTA limits of the decode kernel for `ncta` CTAs: every CTA owns units
+ * of every phase (so that no CTA can run two phases ahead of one it reads
+ * from), at most one O / DOWN row and one state column per consumer warp. */
+int engine_grid_ok(const GDNWeightHeader &c, int ncta) {
+    const uint32_t H = c.hidden_size, cols = c.num_heads * 256;
+    const uint32_t units[] = {4 * H / gdn::kTileRowsQKVG, cols, H, 2 * c.intermediate_size / gdn::kTileRowsGU,
+                              c.vocab_size / gdn::kTileRowsLM};
+    for (uint32_t u : units)
+        if (u < (uint32_t)ncta) return fail("gdn_b200: %d CTAs exceed the %u units of a phase", ncta, u);
+    if ((H + ncta - 1) / ncta > (uint32_t)gdn::kMaxNarrowRows || (cols + ncta - 1) / ncta > (uint32_t)gdn::kMaxStateCols)
+        return fail("gdn_b200: %d CTAs are too few for this model (at most %d rows and state columns per CTA)", ncta,
+                    gdn::kMaxNarrowRows);
     return 0;
 }
 
@@ -164,12 +179,16 @@ struct DeviceModel {
     int refs = 0;
     GDNWeightHeader cfg;
     uint8_t *wimg = nullptr;
-    size_t layer_stride = 0, off_o = 0, off_gu = 0, off_down = 0;
+    size_t layer_stride = 0, off_ab = 0, off_o = 0, off_gu = 0, off_down = 0;
     uint8_t *w_lm = nullptr;
     uint16_t *emb = nullptr;
     float *aux = nullptr;
     size_t aux_stride = 0;
     float *exp_table = nullptr;
+    float *decay_tab = nullptr;     /* [L][nh][65536], see gdn_engine.h */
+    uint32_t *exp_exc = nullptr;    /* the host library's expf exceptions, device copy */
+    uint32_t exp_exc_n = 0;
+    float fast_x_min = INFINITY;    /* DecodeParams.fast_x_min */
     bool model_alive = true;
 };
 
@@ -178,13 +197,59 @@ std::map<const float *, DeviceModel *> g_models;  /* keyed by GDNModel.weight_da
 
 inline uint16_t hi16(float v) { return (uint16_t)(f2u(v) >> 16); }
 
-/* Device column position p of a GEMV row -> natural column. Inside each
- * 512-column group the device row holds columns 0..7 of halves 0..31, then
- * columns 8..15 of halves 0..31 (gdn_engine.h). */
-inline size_t natural_col(size_t p) {
-    const size_t g = p >> 9, w = p & 511;
-    const size_t hi = w >> 8, half = (w & 255) >> 3, e = w & 7;
-    return (g << 9) + half * 16 + hi * 8 + e;
+/* Device image positions -> natural (row, column) of a projection (layouts
+ * in gdn_engine.h). Tiled: element i of [K/(64 G) column chunks][T tiles][G
+ * groups][TR rows][64]; row-major: element i of [K/512 column chunks][R
+ * rows][8 groups][64]. In both, the 16-byte pieces of a 128-byte group are
+ * permuted (by the row in tiles, by the group otherwise). */
+inline void tiled_src(size_t i, size_t TR, size_t G, size_t rows, size_t *row, size_t *col) {
+    const size_t T = rows / TR, chunk = T * G * TR * 64;
+    const size_t j = i / chunk, rem = i % chunk;
+    const size_t t = rem / (G * TR * 64), rem2 = rem % (G * TR * 64);
+    const size_t gi = rem2 / (TR * 64), r = (rem2 % (TR * 64)) / 64, c = rem2 % 64;
+    *row = t * TR + r;
+    *col = (j * G + gi) * 64 + (((c >> 3) ^ (r & 7)) << 3) + (c & 7);
+}
+inline void rowmajor_src(size_t i, size_t rows, size_t *row, size_t *col) {
+    const size_t chunk = rows * 512;
+    const size_t j = i / chunk, rem = i % chunk;
+    const size_t g = j * 8 + (rem % 512) / 64, c = rem % 64;
+    *row = rem / 512;
+    *col = g * 64 + (((c >> 3) ^ (g & 7)) << 3) + (c & 7);
+}
+
+/* The reference's scalar functions with the host C library
+ * (c_impl/gdn_model.cpp:1307-1330). */
+float host_softplus(float x) {
+    if (x > 20.0f) return x;
+    if (x < -20.0f) return expf(x);
+    return log1pf(expf(x));
+}
+
+/* Negative floats x in [-104, 0] whose host expf(x) differs from the
+ * correctly rounded exp(x) (taken as the double-precision exp rounded to
+ * float), in increasing bit order; computed once per process. */
+const std::vector<uint32_t> &host_exp_exceptions() {
+    static std::once_flag once;
+    static std::vector<uint32_t> exc;
+    std::call_once(once, [] {
+        const uint64_t lo = 0x80000000ull, hi = 0xC2D00001ull; /* -0 .. -104 */
+        const int nt = hw_threads();
+        std::vector<std::vector<uint32_t>> part(nt);
+        std::vector<std::thread> th;
+        for (int k = 0; k < nt; ++k)
+            th.emplace_back([&, k] {
+                const uint64_t b = lo + (hi - lo) * k / nt, e = lo + (hi - lo) * (k + 1) / nt;
+                for (uint64_t u = b; u < e; ++u) {
+                    const float x = u2f((uint32_t)u);
+                    const float g = expf(x), c = (float)exp((double)x);
+                    if (f2u(g) != f2u(c)) part[k].push_back((uint32_t)u);
+                }
+            });
+        for (auto &x : th) x.join();
+        for (auto &v : part) exc.insert(exc.end(), v.begin(), v.end());
+    });
+    return exc;
 }
 
 void free_device_model(DeviceModel *dm) {
@@ -196,6 +261,8 @@ void free_device_model(DeviceModel *dm) {
     cudaFree(dm->emb);
     cudaFree(dm->aux);
     cudaFree(dm->exp_table);
+    cudaFree(dm->decay_tab);
+    cudaFree(dm->exp_exc);
     cudaSetDevice(prev);
     delete dm;
 }
@@ -220,63 +287,103 @@ int upload_bf16(uint16_t *dst, size_t n, F fill) {
     return 0;
 }
 
+/* Smallest nonzero weight magnitude of the rounded-product GEMVs, and whether
+ * any of their weights is subnormal or not finite. */
+void gemv_weight_range(const GDNModel *model, float *wmin, bool *bad) {
+    const GDNWeightHeader &c = model->config;
+    const size_t H = c.hidden_size, I = c.intermediate_size;
+    std::vector<std::pair<const float *, size_t>> spans;
+    for (uint32_t l = 0; l < c.num_layers; ++l) {
+        const GDNLayerWeights &w = model->layers[l];
+        for (const float *pp : {w.q_proj, w.k_proj, w.v_proj, w.g_proj, w.o_proj}) spans.push_back({pp, H * H});
+        for (const float *pp : {w.mlp_gate_proj, w.mlp_up_proj, w.mlp_down_proj}) spans.push_back({pp, I * H});
+    }
+    spans.push_back({model->lm_head, (size_t)c.vocab_size * H});
+    std::mutex mu;
+    float best = INFINITY;
+    bool any_bad = false;
+    for (auto &sp : spans) {
+        parallel_for(sp.second, [&](size_t b, size_t e) {
+            float m = INFINITY;
+            bool bd = false;
+            for (size_t i = b; i < e; ++i) {
+                const uint32_t u = f2u(sp.first[i]) & 0x7fffffffu;
+                if (u == 0) continue;
+                if (u < 0x00800000u || u >= 0x7f800000u) bd = true;
+                else m = std::min(m, u2f(u));
+            }
+            std::lock_guard<std::mutex> lock(mu);
+            best = std::min(best, m);
+            any_bad = any_bad || bd;
+        });
+    }
+    *wmin = best;
+    *bad = any_bad;
+}
+
 DeviceModel *build_device_model(const GDNModel *model) {
     const GDNWeightHeader &c = model->config;
     const size_t H = c.hidden_size, nh = c.num_heads, I = c.intermediate_size, V = c.vocab_size, L = c.num_layers;
     DeviceModel *dm = new DeviceModel();
     dm->cfg = c;
     dm->device = g_device;
-    const size_t rows_a = 4 * H + 2 * nh;
-    dm->off_o = rows_a * H * 2;
+    const size_t rows_a = 4 * H;
+    dm->off_ab = rows_a * H * 2;
+    dm->off_o = dm->off_ab + 2 * nh * H * 2;
     dm->off_gu = dm->off_o + H * H * 2;
     dm->off_down = dm->off_gu + 2 * I * H * 2;
     dm->layer_stride = ((dm->off_down + H * I * 2) + 255) & ~(size_t)255;
     dm->aux_stride = (14 * H + 256 + 2 * nh + 3) & ~(size_t)3;
+    const size_t decay_n = L * nh * 65536;
     if (cudaMalloc(&dm->wimg, dm->layer_stride * L) != cudaSuccess || cudaMalloc(&dm->w_lm, V * H * 2) != cudaSuccess ||
         cudaMalloc(&dm->emb, V * H * 2) != cudaSuccess ||
-        cudaMalloc(&dm->aux, (dm->aux_stride * L + H) * sizeof(float)) != cudaSuccess) {
+        cudaMalloc(&dm->aux, (dm->aux_stride * L + H) * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&dm->decay_tab, decay_n * sizeof(float)) != cudaSuccess) {
         fail("gdn_b200: device weight image allocation failed (%.2f GB)",
              (double)(dm->layer_stride * L + 2 * V * H * 2) / 1e9);
         free_device_model(dm);
         return nullptr;
     }
-    /* per layer: QKVGAB, O, GU (interleaved), DOWN, as one contiguous range */
+    /* per layer: QKVG (8-row tiles), AB, O (row-major), GU (16-row tiles),
+     * DOWN (row-major), as one contiguous range */
     for (size_t l = 0; l < L; ++l) {
         const GDNLayerWeights &w = model->layers[l];
         uint16_t *base = reinterpret_cast<uint16_t *>(dm->wimg + l * dm->layer_stride);
         const size_t n = dm->off_down / 2 + H * I;
         const int rc = upload_bf16(base, n, [&](uint16_t *st, size_t b, size_t e, size_t so) {
             for (size_t i = b; i < e; ++i) {
-                float v;
-                if (i < rows_a * H) {
-                    const size_t r = i / H, col = natural_col(i % H);
-                    const float *src;
-                    if (r < H) src = w.q_proj + r * H;
-                    else if (r < 2 * H) src = w.k_proj + (r - H) * H;
-                    else if (r < 3 * H) src = w.v_proj + (r - 2 * H) * H;
-                    else if (r < 4 * H) src = w.g_proj + (r - 3 * H) * H;
-                    else if (r < 4 * H + nh) src = w.a_proj + (r - 4 * H) * H;
-                    else src = w.b_proj + (r - 4 * H - nh) * H;
-                    v = src[col];
+                size_t r, col;
+                const float *src;
+                if (i < dm->off_ab / 2) {
+                    tiled_src(i, gdn::kTileRowsQKVG, gdn::kGroupsQKVG, 4 * H, &r, &col);
+                    const float *m = r < H ? w.q_proj : r < 2 * H ? w.k_proj : r < 3 * H ? w.v_proj : w.g_proj;
+                    src = m + (r % H) * H + col;
+                } else if (i < dm->off_o / 2) {
+                    const size_t j = i - dm->off_ab / 2;
+                    r = j / H;
+                    src = ((r & 1) ? w.b_proj : w.a_proj) + (r >> 1) * H + j % H;
                 } else if (i < dm->off_gu / 2) {
-                    const size_t j = i - dm->off_o / 2;
-                    v = w.o_proj[(j / H) * H + natural_col(j % H)];
+                    rowmajor_src(i - dm->off_o / 2, H, &r, &col);
+                    src = w.o_proj + r * H + col;
                 } else if (i < dm->off_down / 2) {
-                    const size_t j = i - dm->off_gu / 2, r = j / H, col = natural_col(j % H);
-                    v = ((r & 1) ? w.mlp_up_proj : w.mlp_gate_proj)[(r >> 1) * H + col];
+                    tiled_src(i - dm->off_gu / 2, gdn::kTileRowsGU, gdn::kGroupsGU, 2 * I, &r, &col);
+                    src = ((r & 1) ? w.mlp_up_proj : w.mlp_gate_proj) + (r >> 1) * H + col;
                 } else {
-                    const size_t j = i - dm->off_down / 2;
-                    v = w.mlp_down_proj[(j / I) * I + natural_col(j % I)];
+                    rowmajor_src(i - dm->off_down / 2, H, &r, &col);
+                    src = w.mlp_down_proj + r * I + col;
                 }
-                st[so + (i - b)] = hi16(v);
+                st[so + (i - b)] = hi16(*src);
             }
         });
         if (rc != 0) { free_device_model(dm); return nullptr; }
     }
     if (upload_bf16(reinterpret_cast<uint16_t *>(dm->w_lm), V * H,
                     [&](uint16_t *st, size_t b, size_t e, size_t so) {
-                        for (size_t i = b; i < e; ++i)
-                            st[so + (i - b)] = hi16(model->lm_head[(i / H) * H + natural_col(i % H)]);
+                        for (size_t i = b; i < e; ++i) {
+                            size_t r, col;
+                            tiled_src(i, gdn::kTileRowsLM, gdn::kGroupsLM, V, &r, &col);
+                            st[so + (i - b)] = hi16(model->lm_head[r * H + col]);
+                        }
                     }) != 0 ||
         upload_bf16(dm->emb, V * H, [&](uint16_t *st, size_t b, size_t e, size_t so) {
             for (size_t i = b; i < e; ++i) st[so + (i - b)] = hi16(model->embeddings[i]);
@@ -299,9 +406,35 @@ DeviceModel *build_device_model(const GDNModel *model) {
         memcpy(a + 14 * H + 256 + nh, w.dt_bias, nh * 4);
     }
     memcpy(aux.data() + dm->aux_stride * L, model->final_norm, H * 4);
+    /* decay = exp(-exp(a_log) * softplus(a + dt_bias)) for every BF16 a, with
+     * the host library, in the reference's operation order
+     * (c_impl/gdn_model.cpp:2101-2105) */
+    std::vector<float> decay(decay_n);
+    parallel_for(L * nh, [&](size_t b, size_t e) {
+        for (size_t lh = b; lh < e; ++lh) {
+            const GDNLayerWeights &w = model->layers[lh / nh];
+            const float alog = w.a_log[lh % nh], dtb = w.dt_bias[lh % nh];
+            const float ea = expf(alog);
+            for (uint32_t bits = 0; bits < 65536u; ++bits) {
+                const float a = u2f(bits << 16);
+                const float decay_in = a + dtb;
+                const float decay_val = -ea * host_softplus(decay_in);
+                decay[lh * 65536 + bits] = expf(decay_val);
+            }
+        }
+    });
+    const std::vector<uint32_t> &exc = host_exp_exceptions();
+    dm->exp_exc_n = (uint32_t)exc.size();
+    float wmin = INFINITY;
+    bool wbad = false;
+    gemv_weight_range(model, &wmin, &wbad);
+    dm->fast_x_min = (wbad || !(wmin > 0.0f)) ? INFINITY : (float)(ldexp(1.0, -126) / (double)wmin * (1.0 + 1e-6));
     float table[128];
     gdn_exp_table_fill(table);
     if (cudaMemcpy(dm->aux, aux.data(), aux.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dm->decay_tab, decay.data(), decay_n * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMalloc(&dm->exp_exc, std::max<size_t>(exc.size(), 1) * 4) != cudaSuccess ||
+        (exc.size() && cudaMemcpy(dm->exp_exc, exc.data(), exc.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) ||
         cudaMalloc(&dm->exp_table, sizeof(table)) != cudaSuccess ||
         cudaMemcpy(dm->exp_table, table, sizeof(table), cudaMemcpyHostToDevice) != cudaSuccess) {
         fail("gdn_b200: aux upload failed");
@@ -317,15 +450,17 @@ struct Stream {
     DeviceModel *dm = nullptr;
     int device = 0;
     int grid = 0;
+    /* numeric contract: the reference's own (c_impl) unless gdn_b200_set_numerics chooses another */
     int bf16_boundary = 1;
-    int native_product = 0;
-    int bf16_state = 0;
+    int native_product = 1;
+    int bf16_state = 1;
+    int force_exact = 0;   /* test hook: exact emulation of the BF16 product in every phase */
     cudaStream_t stream = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float *S = nullptr, *tails = nullptr, *acts = nullptr;
-    gdn::xword *xbuf = nullptr;  /* exchange words: qkv | gate | ab | attn | y_o | m | y_down */
+    gdn::xword *xbuf = nullptr;  /* exchange words: qkv | gate | attn | y_o | m | y_down */
     size_t xwords = 0;
-    gdn::xword *qkv, *gate, *ab, *attn, *y_o, *m, *y_down;
+    gdn::xword *qkv, *gate, *attn, *y_o, *m, *y_down;
     float *logits, *hidden, *x_embed, *cand_val;
     int32_t *cand_idx = nullptr;
     gdn::DecodeStatus *status = nullptr;
@@ -364,8 +499,10 @@ Stream *find_stream(GDNRunState *state) {
     return it == g_streams.end() ? nullptr : it->second;
 }
 
-/* Host [L][h][k][v] / [L][kind][row][H] state <-> the device's [L][h][v][k] /
- * [L][kind][H][4] layout. */
+/* Host [L][h][k][v] / [L][kind][row][H] state <-> the device's storage
+ * ([L][h][v][k] columns, FP32 or BF16, pieces permuted; gdn_engine.h) /
+ * [L][kind][H][4] tails. The recurrent state passes through a natural FP32
+ * [L][h][v][k] device buffer and the layout kernels of gdn_decode.cu. */
 int upload_state(Stream &st, const float *rec, const float *conv) {
     Stream *s = &st;
     const GDNWeightHeader &c = s->dm->cfg;
@@ -381,9 +518,14 @@ int upload_state(Stream &st, const float *rec, const float *conv) {
         for (size_t d = 0; d < H; ++d)
             for (size_t r = 0; r < 3; ++r) T[(lk * H + d) * 4 + r] = conv[(lk * 3 + r) * H + d];
     CUDA_OK(cudaSetDevice(s->device));
-    CUDA_OK(cudaMemcpyAsync(s->S, S.data(), S.size() * 4, cudaMemcpyHostToDevice, s->stream));
-    CUDA_OK(cudaMemcpyAsync(s->tails, T.data(), T.size() * 4, cudaMemcpyHostToDevice, s->stream));
-    CUDA_OK(cudaStreamSynchronize(s->stream));
+    float *tmp = nullptr;
+    CUDA_OK(cudaMalloc(&tmp, rec_floats * 4));
+    cudaError_t e = cudaMemcpyAsync(tmp, S.data(), rec_floats * 4, cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) e = gdn::launch_state_from_fp32(tmp, s->S, s->bf16_state, L * nh * 256, s->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->tails, T.data(), T.size() * 4, cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return fail("gdn_b200: state upload failed: %s", cudaGetErrorString(e));
     return 0;
 }
 
@@ -391,13 +533,19 @@ int download_state(Stream &st, float *rec, float *conv) {
     Stream *s = &st;
     const GDNWeightHeader &c = s->dm->cfg;
     const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
-    std::vector<float> S(L * nh * 256 * 256), T(L * 3 * H * 4);
+    const size_t rec_floats = L * nh * 256 * 256;
+    std::vector<float> S(rec_floats), T(L * 3 * H * 4);
     CUDA_OK(cudaSetDevice(s->device));
-    CUDA_OK(cudaMemcpyAsync(S.data(), s->S, S.size() * 4, cudaMemcpyDeviceToHost, s->stream));
-    CUDA_OK(cudaMemcpyAsync(T.data(), s->tails, T.size() * 4, cudaMemcpyDeviceToHost, s->stream));
-    CUDA_OK(cudaStreamSynchronize(s->stream));
-    parallel_for(L * nh, [&](size_t b, size_t e) {
-        for (size_t lh = b; lh < e; ++lh)
+    float *tmp = nullptr;
+    CUDA_OK(cudaMalloc(&tmp, rec_floats * 4));
+    cudaError_t e = gdn::launch_state_to_fp32(s->S, s->bf16_state, tmp, L * nh * 256, s->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(S.data(), tmp, rec_floats * 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(T.data(), s->tails, T.size() * 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return fail("gdn_b200: state download failed: %s", cudaGetErrorString(e));
+    parallel_for(L * nh, [&](size_t b, size_t e2) {
+        for (size_t lh = b; lh < e2; ++lh)
             for (size_t k = 0; k < 256; ++k)
                 for (size_t v = 0; v < 256; ++v) rec[(lh * 256 + k) * 256 + v] = S[(lh * 256 + v) * 256 + k];
     });
@@ -453,6 +601,7 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.bf16_state = s.bf16_state;
     p.wimg = dm.wimg;
     p.layer_stride = dm.layer_stride;
+    p.off_ab = dm.off_ab;
     p.off_o = dm.off_o;
     p.off_gu = dm.off_gu;
     p.off_down = dm.off_down;
@@ -461,13 +610,23 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.aux = dm.aux;
     p.aux_stride = dm.aux_stride;
     p.exp_table = dm.exp_table;
+    p.decay_tab = dm.decay_tab;
+    p.exp_exc = dm.exp_exc;
+    p.exp_exc_n = dm.exp_exc_n;
+    {
+        /* the BF16-valued entries of the exception list (a handful) */
+        const std::vector<uint32_t> &exc = host_exp_exceptions();
+        for (uint32_t u : exc)
+            if ((u & 0xffffu) == 0 && p.exp_exc_bf16_n < (uint32_t)gdn::kMaxExcBf16) p.exp_exc_bf16[p.exp_exc_bf16_n++] = u;
+    }
+    p.fast_x_min = dm.fast_x_min;
+    p.force_exact = s.force_exact;
     p.S = s.S;
     p.tails = s.tails;
     p.y_o = s.y_o;
     p.y_down = s.y_down;
     p.qkv = s.qkv;
     p.gate = s.gate;
-    p.ab = s.ab;
     p.attn = s.attn;
     p.m = s.m;
     p.logits = s.logits;
@@ -511,6 +670,18 @@ int check_status(Stream &s) {
                                   "aborted", "token id out of range"};
     return fail("gdn_b200: decode kernel reported %s (cta %u, at %u)", names[err >= 0 && err <= 5 ? err : 4], cta,
                 where);
+}
+
+/* A launch of a multi-token loop failed: the launches already queued still
+ * run; wait for them and report what the kernel recorded (or the launch
+ * error) before returning -1, so the caller sees a settled run state. */
+int abort_loop(Stream &s, int launched) {
+    const std::string launch_err = g_last_error;
+    cudaStreamSynchronize(s.stream);
+    if (cudaMemcpy(s.status_host, s.status, sizeof(gdn::DecodeStatus), cudaMemcpyDeviceToHost) == cudaSuccess &&
+        s.status_host->err != gdn::kErrNone && check_status(s) != 0)
+        return fail("%s (after %d launched steps; %s)", g_last_error.c_str(), launched, launch_err.c_str());
+    return fail("%s (after %d launched steps)", launch_err.c_str(), launched);
 }
 
 int sync_and_check(Stream &s) {
@@ -569,14 +740,43 @@ void host_note_state_write(const void *buffer) {
 }
 int host_fail(const char *msg) { return fail("%s", msg); }
 int host_device() { return g_device; }
-/* Device buffers of a run state: S [L][nh][v][k] FP32, tails [L][3][H][4] FP32. */
-int host_state_buffers(GDNRunState *state, float **S, float **tails, int *device, cudaStream_t *stream) {
+/* The recurrent state of a run state as FP32 [L][nh][v][k] in natural order
+ * (the layout of the prefill kernels), in a device buffer that
+ * host_state_end writes back into the run state's own storage (rounded to
+ * BF16 when the run state keeps BF16 state) and frees. Tails: FP32
+ * [L][3][H][4], the run state's own buffer. */
+int host_state_begin(GDNRunState *state, float **S, float **tails, int *device, cudaStream_t *stream) {
     Stream *s = find_stream(state);
     if (s == nullptr) return fail("gdn_b200: unknown run state");
-    *S = s->S;
+    const GDNWeightHeader &c = s->dm->cfg;
+    const size_t cols = (size_t)c.num_layers * c.num_heads * 256;
+    CUDA_OK(cudaSetDevice(s->device));
+    float *tmp = nullptr;
+    CUDA_OK(cudaMalloc(&tmp, cols * 256 * 4));
+    const cudaError_t e = gdn::launch_state_to_fp32(s->S, s->bf16_state, tmp, cols, s->stream);
+    if (e != cudaSuccess) {
+        cudaFree(tmp);
+        return fail("gdn_b200: state conversion failed: %s", cudaGetErrorString(e));
+    }
+    *S = tmp;
     *tails = s->tails;
     *device = s->device;
     *stream = s->stream;
+    return 0;
+}
+int host_state_end(GDNRunState *state, float *S, bool write_back) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) {
+        cudaFree(S);
+        return fail("gdn_b200: unknown run state");
+    }
+    const GDNWeightHeader &c = s->dm->cfg;
+    const size_t cols = (size_t)c.num_layers * c.num_heads * 256;
+    cudaError_t e = cudaSuccess;
+    if (write_back) e = gdn::launch_state_from_fp32(S, s->S, s->bf16_state, cols, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    cudaFree(S);
+    if (e != cudaSuccess) return fail("gdn_b200: state conversion failed: %s", cudaGetErrorString(e));
     return 0;
 }
 }  // namespace gdn
@@ -755,11 +955,13 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
      * every CTA owns work in every phase (the exchange ordering relies on it) */
     s->grid = gdn_b200_grid_size();
     {
-        const int units[] = {(int)(4 * model->config.hidden_size + 2 * model->config.num_heads),
-                             (int)(model->config.num_heads * 256), (int)model->config.hidden_size,
-                             (int)model->config.intermediate_size, (int)model->config.vocab_size};
+        const GDNWeightHeader &hc = model->config;
+        const int units[] = {(int)(4 * hc.hidden_size / gdn::kTileRowsQKVG), (int)(hc.num_heads * 256),
+                             (int)hc.hidden_size, (int)(2 * hc.intermediate_size / gdn::kTileRowsGU),
+                             (int)(hc.vocab_size / gdn::kTileRowsLM)};
         for (int u : units) s->grid = std::min(s->grid, u);
     }
+    if (engine_grid_ok(model->config, s->grid) != 0) return -1;
     const GDNWeightHeader &c = model->config;
     const size_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size, nh = c.num_heads, L = c.num_layers;
     auto cleanup = [&](int rc) {
@@ -784,7 +986,7 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
     const size_t act_floats = H + H + 2 * (size_t)s->grid + 64;
     /* the exchange region (one allocation, the one a tensor-parallel peer
      * maps): exchange words, the per-rank argmax candidates, logits */
-    const size_t xwords = 3 * H + H + 64 + H + H + I + H;
+    const size_t xwords = 3 * H + H + H + H + I + H;
     s->xwords = xwords + gdn::kRankCandWords;
     s->xbytes = s->xwords * sizeof(gdn::xword) + V * sizeof(float);
     if (cudaMalloc(&s->S, s_bytes) != cudaSuccess || cudaMalloc(&s->tails, t_bytes) != cudaSuccess ||
@@ -797,7 +999,6 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
     gdn::xword *x = s->xbuf;
     s->qkv = x; x += 3 * H;
     s->gate = x; x += H;
-    s->ab = x; x += 64;
     s->attn = x; x += H;
     s->y_o = x; x += H;
     s->m = x; x += I;
@@ -809,7 +1010,9 @@ int gdn_run_state_init(GDNRunState *state, const GDNModel *model, uint32_t max_t
     s->x_embed = a; a += H;
     s->cand_val = a; a += s->grid;
     s->cand_idx = reinterpret_cast<int32_t *>(a);
-    /* exchange words start with tag 0xffffffff, which no launch uses */
+    /* exchange words start as all ones: tag 0xffff (32-bit words) or
+     * 0xffffffff (64-bit words), which the first launches (epoch 0, tags
+     * 0 .. 5L) never use; every refill with ones also restarts the epoch */
     if (cudaMemsetAsync(s->S, 0, s_bytes, s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->tails, 0, t_bytes, s->stream) != cudaSuccess ||
         cudaMemsetAsync(s->acts, 0, act_floats * sizeof(float), s->stream) != cudaSuccess ||
@@ -952,6 +1155,7 @@ int gdn_b200_tp_detach(GDNRunState *state) {
     tp_close(*s);
     CUDA_OK(cudaMemsetAsync(s->xbuf, 0xff, s->xwords * sizeof(gdn::xword), s->stream));
     CUDA_OK(cudaStreamSynchronize(s->stream));
+    s->epoch = 0;
     return 0;
 }
 
@@ -998,19 +1202,44 @@ void gdn_run_state_free(GDNRunState *state) {
 int gdn_b200_set_numerics(GDNRunState *state, int bf16_boundary, int bf16_products, int bf16_state) {
     Stream *s = find_stream(state);
     if (s == nullptr) return fail("gdn_b200: unknown run state");
-    if (bf16_products && !bf16_boundary) return fail("gdn_b200: BF16-rounded products need BF16 boundaries");
-    const int boundary = bf16_boundary ? 1 : 0;
+    const int boundary = bf16_boundary ? 1 : 0, products = bf16_products ? 1 : 0, bstate = bf16_state ? 1 : 0;
+    const bool fp32 = !boundary && !products && !bstate, engine = boundary && !products && !bstate,
+               cimpl = boundary && products && bstate;
+    if (!(fp32 || engine || cimpl))
+        return fail("gdn_b200: numerics (%d, %d, %d) is not a contract of this engine: (1, 1, 1) the reference's "
+                    "own (c_impl), (1, 0, 0) exact products with FP32 state, (0, 0, 0) the FP32 control",
+                    boundary, products, bstate);
+    CUDA_OK(cudaSetDevice(s->device));
+    if (bstate != s->bf16_state) {
+        /* the state changes storage (BF16 <-> FP32): convert it in place */
+        const GDNWeightHeader &c = s->dm->cfg;
+        const size_t cols = (size_t)c.num_layers * c.num_heads * 256;
+        float *tmp = nullptr;
+        CUDA_OK(cudaMalloc(&tmp, cols * 256 * 4));
+        cudaError_t e = gdn::launch_state_to_fp32(s->S, s->bf16_state, tmp, cols, s->stream);
+        if (e == cudaSuccess) e = gdn::launch_state_from_fp32(tmp, s->S, bstate, cols, s->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+        cudaFree(tmp);
+        if (e != cudaSuccess) return fail("gdn_b200: state conversion failed: %s", cudaGetErrorString(e));
+    }
     if (boundary != s->bf16_boundary) {
         /* the exchange word width follows the boundary contract (32-bit words
-         * for BF16 boundaries, 64-bit for FP32): start the buffers over with
-         * the tag no launch uses rather than reinterpret the other width */
-        CUDA_OK(cudaSetDevice(s->device));
+         * for BF16 boundaries, 64-bit for FP32): start the buffers over, and
+         * the tags with them */
         CUDA_OK(cudaMemsetAsync(s->xbuf, 0xff, s->xwords * sizeof(gdn::xword), s->stream));
         CUDA_OK(cudaStreamSynchronize(s->stream));
+        s->epoch = 0;
     }
     s->bf16_boundary = boundary;
-    s->native_product = bf16_products ? 1 : 0;
-    s->bf16_state = bf16_state ? 1 : 0;
+    s->native_product = products;
+    s->bf16_state = bstate;
+    return 0;
+}
+
+int gdn_b200_test_force_exact_products(GDNRunState *state, int on) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    s->force_exact = on ? 1 : 0;
     return 0;
 }
 
@@ -1128,7 +1357,7 @@ int gdn_b200_decode_tokens(const GDNModel *model, GDNRunState *state, const int3
     for (uint32_t i = 0; i < n; ++i) {
         p.token_src = (greedy && i > 0) ? s->argmax + (i - 1) : s->tokens + i;
         p.token_out = s->argmax + i;
-        if (launch(*s, p) != 0) return -1;
+        if (launch(*s, p) != 0) return abort_loop(*s, (int)i);
     }
     CUDA_OK(cudaEventRecord(s->ev1, s->stream));
     if (argmax_out != nullptr)
@@ -1195,7 +1424,7 @@ int gdn_b200_decode_tokens_noalloc(const GDNModel *model, GDNRunState *state, co
     for (uint32_t i = 0; i < n; ++i) {
         p.token_src = (greedy && i > 0) ? dmax + (i - 1) : dtok + i;
         p.token_out = dmax + i;
-        if (launch(*s, p) != 0) return -1;
+        if (launch(*s, p) != 0) return abort_loop(*s, (int)i);
     }
     CUDA_OK(cudaEventRecord(s->ev1, s->stream));
     if (argmax_out != nullptr)

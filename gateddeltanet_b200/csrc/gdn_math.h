@@ -90,9 +90,9 @@ GDN_HD float gdn_expf(float x, const float *table) {
     const float bb = GDN_SUB(rh, r1);
     const float e2 = GDN_ADD(GDN_SUB(r1, GDN_SUB(rh, bb)), GDN_SUB(-p2, bb)); /* TwoSum error */
     const float rl = GDN_SUB(e2, GDN_MUL(n, GDN_EXP_L3));
-    /* exp(r) - 1 = rh + q,  q = rl + rh^2 (1/2 + rh (1/6 + rh/24)) */
+    /* exp(rh + rl) - 1 = rh + q,  q = rl (1 + rh) + rh^2 (1/2 + rh (1/6 + rh/24)) */
     const float poly = GDN_ADD(0.5f, GDN_MUL(rh, GDN_ADD(0x1.555556p-3f, GDN_MUL(rh, 0x1.555556p-5f))));
-    const float q = GDN_ADD(rl, GDN_MUL(GDN_MUL(rh, rh), poly));
+    const float q = GDN_ADD(GDN_ADD(rl, GDN_MUL(rl, rh)), GDN_MUL(GDN_MUL(rh, rh), poly));
     const int j = N & 63;
     const int k = N >> 6; /* arithmetic shift: N = 64 k + j */
     const float th = table[j], tl = table[64 + j];
@@ -109,6 +109,54 @@ GDN_HD float gdn_expf(float x, const float *table) {
     out = (x < -103.97208404541015625f) ? 0.0f : out;
     out = (x > 88.72283935546875f) ? INFINITY : out;
     out = (x != x) ? x : out;
+    return out;
+}
+
+/* exp(x) as gdn_expf, and whether its rounding is in doubt. The float-float
+ * value before the final rounding, s + tail, is within ~2^-39 of exp(x); its
+ * rounding error err = (s + tail) - m is computed, and `zone` is set when the
+ * value lies within GDN_EXP_ZONE ulp of a rounding boundary (the midpoint
+ * between m and the float on err's side, half an ulp away -- a quarter of m's
+ * ulp below a power of two), where a libm that is not correctly rounded may
+ * round the other way. Results below the normal range (x < -87.33) are
+ * always flagged: their final scaling rounds a second time. NaN and
+ * overflowing inputs are not flagged. A flagged caller decides with a
+ * more precise evaluation (the decode kernel's exact-exp path). */
+#define GDN_EXP_ZONE 0.004f
+GDN_HD float gdn_expf_zone(float x, const float *table, bool *zone) {
+    const float xc = fminf(fmaxf(x, -104.0f), 89.0f);
+    const float n = rintf(GDN_MUL(xc, GDN_EXP_INV_L));
+    const int N = (int)n;
+    const float r1 = fmaf(-n, GDN_EXP_L1, xc);
+    const float p2 = GDN_MUL(n, GDN_EXP_L2);
+    const float rh = GDN_SUB(r1, p2);
+    const float bb = GDN_SUB(rh, r1);
+    const float e2 = GDN_ADD(GDN_SUB(r1, GDN_SUB(rh, bb)), GDN_SUB(-p2, bb));
+    const float rl = GDN_SUB(e2, GDN_MUL(n, GDN_EXP_L3));
+    const float poly = GDN_ADD(0.5f, GDN_MUL(rh, GDN_ADD(0x1.555556p-3f, GDN_MUL(rh, 0x1.555556p-5f))));
+    const float q = GDN_ADD(GDN_ADD(rl, GDN_MUL(rl, rh)), GDN_MUL(GDN_MUL(rh, rh), poly));
+    const int j = N & 63;
+    const int k = N >> 6;
+    const float th = table[j], tl = table[64 + j];
+    const float a = GDN_MUL(th, rh);
+    const float a_err = fmaf(th, rh, -a);
+    const float s = GDN_ADD(th, a);
+    const float s_err = GDN_SUB(a, GDN_SUB(s, th));
+    const float tail = GDN_ADD(GDN_ADD(GDN_ADD(a_err, s_err), GDN_MUL(th, q)), GDN_MUL(tl, GDN_ADD(1.0f, rh)));
+    const float m = GDN_ADD(s, tail);
+    /* rounding error of m: s - m is exact (Sterbenz), the sum rounds once */
+    const float err = GDN_ADD(GDN_SUB(s, m), tail);
+    /* ulp of m (m in [0.99, 1.99]); the gap below a power of two is half of it */
+    const float u = (m >= 1.0f) ? 0x1p-23f : 0x1p-24f;
+    const float gap = (err < 0.0f && (m == 1.0f)) ? GDN_MUL(0.5f, u) : u;
+    const int k1 = k >> 1;
+    const float v = GDN_MUL(GDN_MUL(m, gdn_pow2f(k1)), gdn_pow2f(k - k1));
+    float out = v;
+    out = (x < -103.97208404541015625f) ? 0.0f : out;
+    out = (x > 88.72283935546875f) ? INFINITY : out;
+    out = (x != x) ? x : out;
+    const bool near = fabsf(err) >= GDN_MUL(GDN_SUB(0.5f, GDN_EXP_ZONE), gap);
+    *zone = (x == x) && !(x > 88.72283935546875f) && (near || x < -87.33f);
     return out;
 }
 

@@ -35,17 +35,21 @@ int gdn_b200_model_synth(GDNModel *model, const GDNWeightHeader *config, uint64_
  * gdn_model_load reads (scripts/export_gdn_c.py:177-210). */
 int gdn_b200_model_save(const GDNModel *model, const char *path);
 
-/* Numerics of a stream (defaults 1, 0, 0):
- *   bf16_boundary  1: round every activation to BF16 where the reference does
- *                  (its all-BF16 transient contract); 0: keep FP32 (the "FP32
- *                  control" of the parity gates).
- *   bf16_products  1: round each GEMV product to BF16 with DAZ/FTZ before the
- *                  sum, the c_impl/FPGA product contract
- *                  (c_impl/gdn_model.cpp:392-466); 0: exact products (the
- *                  PyTorch/GPU arithmetic). Needs bf16_boundary.
- *   bf16_state     1: store the recurrent state rounded to BF16 after each
- *                  update (c_impl/gdn_model.cpp:2268-2300); 0: FP32 state.
- * GEMV sums always follow the reference's reduction order. */
+/* Numeric contract of a stream. Three are supported:
+ *   (1, 1, 1)  the default: the reference's own arithmetic (c_impl): every
+ *              activation rounded to BF16 where the reference rounds it, each
+ *              GEMV product rounded to BF16 with DAZ/FTZ before the sum
+ *              (c_impl/gdn_model.cpp:392-466), the recurrent state stored in
+ *              BF16 after each update (2268-2300), transcendental functions
+ *              rounded as the host C library rounds them. Reproduces
+ *              gdn_decode_step_host of the reference bit for bit.
+ *   (1, 0, 0)  BF16 boundaries, exact products, FP32 state (the PyTorch/GPU
+ *              arithmetic of the reference's training stack).
+ *   (0, 0, 0)  the FP32 control of the parity gates: FP32 boundaries, exact
+ *              products, FP32 state.
+ * GEMV sums always follow the reference's reduction order. Other
+ * combinations return -1. Switching between BF16 and FP32 state converts the
+ * stream's state (FP32 -> BF16 rounds to nearest even). */
 int gdn_b200_set_numerics(GDNRunState *state, int bf16_boundary, int bf16_products, int bf16_state);
 
 /* Replace / read the decode state in the .gdnstate section layouts:
@@ -98,9 +102,9 @@ int gdn_b200_decode_tokens_noalloc(const GDNModel *model, GDNRunState *state, co
 
 /* One decode step of `token` with the kernel's phase trace enabled: for every
  * CTA and phase (layer * 5 + {QKVG, state, O, gate/up, down}, then the LM
- * head) eight %globaltimer stamps in ns -- consumers done with the previous
- * phase, past the grid barrier, phase input built, own chunks done, producer's
- * first and last copy issued, two unused. Layout [cta][phase][8]; returns the
+ * head) eight %globaltimer stamps in ns -- [0] consumers done with the
+ * previous phase, [1] phase inputs arrived, [2] phase input built, [3] the
+ * phase's chunks done, [6] input reductions done; [4], [5], [7] unused. Layout [cta][phase][8]; returns the
  * number of (cta, phase) records or -1. The B200 counterpart of the
  * reference's GDN_CALL_PROBE cycle stamps (c_impl/gdn_model.cpp:18-127). */
 int gdn_b200_trace_step(const GDNModel *model, GDNRunState *state, int32_t token, uint64_t *trace_out,
@@ -124,12 +128,19 @@ int gdn_b200_delta_rule_step(uint32_t slices, float *S, const float *q, const fl
 
 /* Test hook for the failure path (no counterpart in the reference): until
  * called again with cta = -1, every decode step of `state` has CTA `cta`
- * leave out its outputs of phase `phase` (layer * 5 + 0 for QKVGAB, + 2 for O,
+ * leave out its outputs of phase `phase` (layer * 5 + 0 for QKVG, + 2 for O,
  * + 3 for gate/up, + 4 for down). The CTAs waiting for them give up after
  * their wait limit (2 s), the step returns -1 with the kernel's error, and
  * the run state stays usable (its recurrent state is then partly updated:
  * reload it). Nothing faults or hangs on the GPU. */
 int gdn_b200_test_drop_outputs(GDNRunState *state, int cta, int phase);
+
+/* Test hook (no counterpart in the reference): with on != 0 every GEMV of
+ * `state` in the c_impl contract uses the exact emulation of the reference's
+ * BF16 product (special values, DAZ, FTZ) instead of the packed BF16
+ * multiply, which the kernel otherwise uses whenever no product of a phase
+ * can fall below the normal range. Results are identical either way. */
+int gdn_b200_test_force_exact_products(GDNRunState *state, int on);
 
 /* Reference-ABI compatibility for the run states created afterwards (also
  * GDN_B200_ABI_COMPAT=1 in the environment): gdn_run_state_init then builds

@@ -22,6 +22,17 @@ its outputs:
 tests/test_oracle_golden.py recomputes all of it with the CPU oracle and
 requires bit equality. Needs the reference sources (only in the build
 container): `make -C oracle ref && python tests/golden/make_golden.py`.
+
+  --config0 [DUMP]   BASELINE config[0] as specified: 256 teacher-forced
+              steps from zero state on the seeded GDN-1.3B weights (seed 1234,
+              token stream seed 99, stream 0) through the reference's
+              gdn_decode_step_host, digested into
+              tests/golden/reference_config0_256.json (per step: token, argmax,
+              SHA-256 of the FP32 logits and hidden vector, top-5; the final
+              recurrent state and conv tails). The reference takes 7-14 s per
+              token single-threaded (30-60 minutes); DUMP reuses a driver
+              output written earlier with
+              `gdn_ref_driver --seed 1234 --stream-seed 99 --stream 0 --steps 256 --out DUMP`.
 """
 from __future__ import annotations
 
@@ -119,7 +130,50 @@ def decode_case(tmp: str, c: dict) -> dict:
     return out
 
 
+CONFIG0 = dict(name="config0_256", seed=1234, stream_seed=99, stream=0, steps=256, state_seed=0)
+
+
+def digest_dump(c: dict, path: str) -> dict:
+    steps, rest = oracle_lib.read_ref_dump(path)
+    assert len(steps) == c["steps"], f"dump has {len(steps)} steps, expected {c['steps']}"
+    d = oracle_lib.FULL_DIMS
+    nrec = d["layers"] * d["heads"] * d["head_dim"] * d["head_dim"]
+    rec, conv = rest[:nrec], rest[nrec:]
+    out = dict(c)
+    out["steps_out"] = []
+    for s in steps:
+        top = np.argsort(-s["logits"], kind="stable")[:5]
+        out["steps_out"].append({
+            "token": s["token"], "argmax": s["argmax"],
+            "logits_sha256": sha(s["logits"]), "hidden_sha256": sha(s["hidden"]),
+            "top5_index": top.tolist(), "top5_value": [float(s["logits"][i]) for i in top],
+        })
+    out["mean_reference_ms"] = float(np.mean([s["ms"] for s in steps]))
+    out["rec_sha256"] = sha(rec)
+    out["conv_sha256"] = sha(conv)
+    return out
+
+
+def config0(dump: str | None) -> None:
+    with tempfile.TemporaryDirectory() as tmp:
+        if dump is None:
+            dump = os.path.join(tmp, "config0.bin")
+            subprocess.run([DRIVER, "--seed", str(CONFIG0["seed"]), "--stream-seed", str(CONFIG0["stream_seed"]),
+                            "--stream", str(CONFIG0["stream"]), "--steps", str(CONFIG0["steps"]), "--out", dump],
+                           check=True)
+        gold = digest_dump(CONFIG0, dump)
+    gold["generator"] = ("tests/golden/make_golden.py --config0 via oracle/_ref/gdn_ref_driver (reference "
+                         "c_impl/gdn_model.cpp compiled natively through oracle/hls_shim)")
+    path = os.path.join(HERE, "reference_config0_256.json")
+    with open(path, "w") as f:
+        json.dump(gold, f, indent=0)
+    print("wrote", path)
+
+
 def main() -> None:
+    if len(sys.argv) > 1 and sys.argv[1] == "--config0":
+        config0(sys.argv[2] if len(sys.argv) > 2 else None)
+        return
     if not os.path.exists(DRIVER):
         raise SystemExit("build the reference first: make -C oracle ref")
     with tempfile.TemporaryDirectory() as tmp:

@@ -2,15 +2,18 @@
 oracle (oracle/gdn_oracle.c, itself pinned bit-exact to the reference's
 c_impl/gdn_model.cpp decode by tests/test_oracle_golden.py).
 
-Modes compared (see tests/oracle_lib.py):
-  engine default   exact BF16 products, FP32 state, BF16 boundaries
-                   vs oracle ENGINE_MODE: logits rel-L2 <= 1e-2, state <= 1e-3
-  FP32 control     engine with FP32 boundaries vs oracle FP32_CONTROL:
-                   logits rel-L2 <= 1e-4, state <= 1e-4
-  reference mode   vs oracle REFERENCE_MODE (the reference's own arithmetic:
-                   BF16-rounded products, BF16 state): logits rel-L2 <= 1e-2
-Argmax must agree wherever the oracle's top-2 margin exceeds 4x the logit
-error (tests/parity.py).
+Contracts compared (see tests/oracle_lib.py):
+  c_impl (default) the reference's own arithmetic (BF16-rounded products, BF16
+                   state, BF16 boundaries) vs oracle REFERENCE_MODE: logits,
+                   final hidden vector, recurrent state and conv tails equal
+                   bit for bit (the fast packed-BF16 product and the exact
+                   emulation both)
+  engine           exact BF16 products, FP32 state, BF16 boundaries vs oracle
+                   ENGINE_MODE: bit for bit
+  FP32 control     FP32 boundaries vs oracle FP32_CONTROL: logits rel-L2 <=
+                   1e-4, state <= 1e-4
+The gates of tests/parity.py (logits rel-L2 1e-2, state 1e-3, argmax wherever
+the oracle's top-2 margin exceeds 4x the logit error) are asserted as well.
 """
 import numpy as np
 import pytest
@@ -56,15 +59,18 @@ def full(lib):
     return model, oracle
 
 
-ENGINE = (True, False, False)      # engine default numerics (gdn_b200_set_numerics)
-CIMPL = (True, True, True)         # the c_impl's own arithmetic
+ENGINE = (True, False, False)      # exact products, FP32 state (gdn_b200_set_numerics)
+CIMPL = (True, True, True)         # the c_impl's own arithmetic (the default)
 FP32 = (False, False, False)       # FP32 control
 
 
-def run_parity(model, oracle, steps, mode, numerics, state_seed, tol_logits, tol_state, use_loop=False):
+def run_parity(model, oracle, steps, mode, numerics, state_seed, tol_logits, tol_state, use_loop=False,
+               bitexact=False, exact_products=False):
     oracle.reset_state(state_seed)
     rs = gdn.RunState(model)
     rs.set_numerics(*numerics)
+    if exact_products:
+        rs.force_exact_products(True)
     if state_seed:
         rs.load_state(oracle.rec, oracle.conv)
     tokens = [oracle.token(STREAM_SEED, 0, i) for i in range(steps)]
@@ -80,6 +86,10 @@ def run_parity(model, oracle, steps, mode, numerics, state_seed, tol_logits, tol
         err = parity.rel_l2(logits, ref.logits)
         worst = max(worst, err)
         assert err <= tol_logits, f"step {i}: logits rel-L2 {err:.3e} > {tol_logits}"
+        if bitexact:
+            np.testing.assert_array_equal(logits.view(np.uint32), ref.logits.view(np.uint32), err_msg=f"step {i} logits")
+            np.testing.assert_array_equal(hidden.view(np.uint32), ref.hidden.view(np.uint32), err_msg=f"step {i} hidden")
+            assert pick == ref.argmax
         assert pick == parity.argmax_first(logits), "kernel argmax != argmax of its own logits"
         assert parity.argmax_agrees(logits, ref.logits, pick), f"step {i}: argmax {pick} vs oracle {ref.argmax}"
     rec, conv = rs.read_state()
@@ -87,6 +97,9 @@ def run_parity(model, oracle, steps, mode, numerics, state_seed, tol_logits, tol
     c_err = parity.rel_l2(conv, oracle.conv)
     assert s_err <= tol_state, f"recurrent state rel-L2 {s_err:.3e} > {tol_state}"
     assert c_err <= tol_logits, f"conv tails rel-L2 {c_err:.3e}"
+    if bitexact:
+        np.testing.assert_array_equal(rec.view(np.uint32), oracle.rec.view(np.uint32))
+        np.testing.assert_array_equal(conv.view(np.uint32), oracle.conv.view(np.uint32))
     rs.free()
     return worst, s_err
 
@@ -94,7 +107,7 @@ def run_parity(model, oracle, steps, mode, numerics, state_seed, tol_logits, tol
 @pytest.mark.parametrize("state_seed", [0, 7])
 def test_small_engine_mode(small, state_seed):
     model, oracle = small
-    run_parity(model, oracle, 8, ol.ENGINE_MODE, ENGINE, state_seed, parity.LOGITS_BF16, parity.STATE)
+    run_parity(model, oracle, 8, ol.ENGINE_MODE, ENGINE, state_seed, parity.LOGITS_BF16, parity.STATE, bitexact=True)
 
 
 @pytest.mark.parametrize("state_seed", [0, 7])
@@ -103,9 +116,37 @@ def test_small_fp32_control(small, state_seed):
     run_parity(model, oracle, 6, ol.FP32_CONTROL, FP32, state_seed, parity.LOGITS_FP32, parity.LOGITS_FP32)
 
 
-def test_small_reference_mode(small):
+@pytest.mark.parametrize("state_seed", [0, 7])
+def test_small_reference_mode(small, state_seed):
     model, oracle = small
-    run_parity(model, oracle, 6, ol.REFERENCE_MODE, CIMPL, 7, parity.LOGITS_BF16, parity.STATE)
+    run_parity(model, oracle, 8, ol.REFERENCE_MODE, CIMPL, state_seed, parity.LOGITS_BF16, parity.STATE, bitexact=True)
+
+
+def test_small_reference_mode_exact_products(small):
+    """The exact emulation of the reference's BF16 product (special values,
+    DAZ, FTZ), which phases use when an input could produce a product below
+    the normal range, gives the same bits as the packed BF16 multiply."""
+    model, oracle = small
+    run_parity(model, oracle, 4, ol.REFERENCE_MODE, CIMPL, 7, parity.LOGITS_BF16, parity.STATE, bitexact=True,
+               exact_products=True)
+
+
+def test_default_is_reference_contract(small):
+    """A run state decodes in the reference's own arithmetic unless told
+    otherwise (gdn_decode_step_host as a drop-in returns the reference's
+    results)."""
+    model, oracle = small
+    oracle.reset_state(0)
+    rs = gdn.RunState(model)
+    tok = oracle.token(STREAM_SEED, 4, 0)
+    pick = rs.step(tok)
+    logits, _ = rs.outputs()
+    ref = oracle.step(tok, ol.REFERENCE_MODE)
+    np.testing.assert_array_equal(logits.view(np.uint32), ref.logits.view(np.uint32))
+    assert pick == ref.argmax
+    with pytest.raises(RuntimeError, match="not a contract"):
+        rs.set_numerics(True, True, False)
+    rs.free()
 
 
 def test_small_device_loop_matches_host_steps(small):
@@ -204,11 +245,12 @@ def test_state_roundtrip_and_gdnstate_file(small, tmp_path):
 
 def test_full_engine_and_reference_modes(full):
     """GDN-1.3B shape: 3 teacher-forced steps from a
-    seeded state in the engine mode, then against the reference's own
-    arithmetic (BF16 products, BF16 state)."""
+    seeded state in the engine contract, then in the reference's own
+    arithmetic (BF16 products, BF16 state), both bit for bit."""
     model, oracle = full
-    run_parity(model, oracle, 3, ol.ENGINE_MODE, ENGINE, 7, parity.LOGITS_BF16, parity.STATE)
-    run_parity(model, oracle, 2, ol.REFERENCE_MODE, CIMPL, 7, parity.LOGITS_BF16, parity.STATE, use_loop=True)
+    run_parity(model, oracle, 3, ol.ENGINE_MODE, ENGINE, 7, parity.LOGITS_BF16, parity.STATE, bitexact=True)
+    run_parity(model, oracle, 3, ol.REFERENCE_MODE, CIMPL, 7, parity.LOGITS_BF16, parity.STATE, use_loop=True,
+               bitexact=True)
 
 
 def test_full_fp32_control(full):

@@ -3,8 +3,10 @@ gdn_b200_decode_tokens: two run states of one model decode the same two
 calls in a row (a teacher-forced call, then a greedy one), one through each
 entry point; every step's argmax, the token line and the recurrent state and
 conv tails must agree bit for bit after each call. Also: a call longer than
-the 4096-token scratch is rejected with an error naming the limit. The file
-is named so that it is collected last."""
+the 4096-token scratch is rejected with an error naming the limit, and a
+call on a fresh run state, longer than any call before it, leaves the
+device's free memory unchanged (the property the entry point exists for).
+The file is named so that it is collected last."""
 import numpy as np
 import pytest
 
@@ -54,4 +56,34 @@ def test_noalloc_rejects_oversized_call(model):
         with pytest.raises(RuntimeError, match="at most 4096 tokens"):
             s.decode_noalloc([1] * 4097)
     finally:
+        s.free()
+
+
+def test_noalloc_allocates_nothing(model):
+    import ctypes
+    free_b, total_b = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    cudart = None
+    for name in ("libcudart.so.12", "libcudart.so"):
+        try:
+            cudart = ctypes.CDLL(name)
+            break
+        except OSError:
+            continue
+    if cudart is None:
+        import torch
+        mem_get_info = lambda: torch.cuda.mem_get_info(0)[0]  # noqa: E731
+    else:
+        def mem_get_info():
+            assert cudart.cudaMemGetInfo(ctypes.byref(free_b), ctypes.byref(total_b)) == 0
+            return free_b.value
+    warm = gdn.RunState(model)
+    s = gdn.RunState(model)
+    try:
+        warm.decode_noalloc([1, 2, 3])  # the scratch's address is looked up once per device
+        before = mem_get_info()
+        s.decode_noalloc(list(range(100, 100 + 1500)))
+        after = mem_get_info()
+        assert after == before, f"free device memory changed by {before - after} bytes"
+    finally:
+        warm.free()
         s.free()
