@@ -414,6 +414,22 @@ __device__ __forceinline__ void xput(const DecodeParams &p, xword *base, size_t 
         for (int r = 0; r < p.tp_world; ++r)
             if (r != p.tp_rank) xstore_sys(peer_addr(p, a, r), w);
 }
+/* store gate element i: in the BF16-boundary contracts with sigmoid(g)
+ * beside it (gword), so the output gate's consumers need no exp */
+template <int MODE>
+__device__ __forceinline__ void xput_gate(const DecodeParams &p, size_t i, float g, float sg, uint32_t tag) {
+    if (!Mode<MODE>::kBf16) {
+        xput<MODE>(p, p.gate, i, g, tag);
+        return;
+    }
+    unsigned long long *a = reinterpret_cast<unsigned long long *>(p.gate) + i;
+    const unsigned long long w =
+        ((unsigned long long)((__float_as_uint(g) & 0xffff0000u) | (tag & 0xffffu)) << 32) | __float_as_uint(sg);
+    xstore(a, w);
+    if (Mode<MODE>::kTp)
+        for (int r = 0; r < p.tp_world; ++r)
+            if (r != p.tp_rank) xstore_sys(peer_addr(p, a, r), w);
+}
 /* Exchange-word loads. `sys`: tensor-parallel decode, where peers store the
  * words (system-scope loads, so that they and the peers' system-scope stores
  * are morally strong). */
@@ -429,6 +445,18 @@ __device__ __forceinline__ unsigned long long xget(const unsigned long long *p, 
     else asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
+/* The gate words of the BF16-boundary contracts are 64 bits: sigmoid(g) as
+ * FP32 in the low half (computed once, by the CTA that computes the gate
+ * row), the BF16 g and the 16-bit tag in the high half. */
+struct gword {
+    unsigned long long v;
+};
+__device__ __forceinline__ gword xget(const gword *p, bool sys) {
+    return gword{xget(reinterpret_cast<const unsigned long long *>(p), sys)};
+}
+__device__ __forceinline__ bool xtag_is(gword w, uint32_t tag) { return ((uint32_t)(w.v >> 32) & 0xffffu) == (tag & 0xffffu); }
+__device__ __forceinline__ float gword_g(gword w) { return __uint_as_float((uint32_t)(w.v >> 32) & 0xffff0000u); }
+__device__ __forceinline__ float gword_sig(gword w) { return __uint_as_float((uint32_t)w.v); }
 __device__ __forceinline__ bool xtag_is(uint32_t w, uint32_t tag) { return (w & 0xffffu) == (tag & 0xffffu); }
 __device__ __forceinline__ bool xtag_is(unsigned long long w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
 __device__ __forceinline__ float xval(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
@@ -451,7 +479,9 @@ constexpr size_t kOffBars = kOffWbestI + 16 * 4;                         /* full
 constexpr size_t kOffIssued = kOffBars + 2 * kSlots * 8;                 /* [kSlots] u32 */
 constexpr size_t kOffFlags = kOffIssued + kSlots * 4;                    /* abort, decision, exact[2] */
 constexpr size_t kOffExpTab = (kOffFlags + 16 + 15) & ~(size_t)15;       /* 128 floats */
-constexpr size_t kOffXs = kOffExpTab + 128 * 4;                          /* phase input */
+constexpr size_t kOffNormW = kOffExpTab + 128 * 4;                       /* next RMSNorm weights, H floats */
+constexpr size_t kOffONorm = kOffNormW + kMaxHidden * 4;                 /* next output-norm weights, 256 */
+constexpr size_t kOffXs = kOffONorm + kHeadDim * 4;                      /* phase input */
 
 extern __shared__ __align__(128) uint8_t smem_raw[];
 
@@ -492,6 +522,16 @@ __device__ __forceinline__ const float *exp_table() {
     return reinterpret_cast<const float *>(smem_raw + kOffExpTab);
 }
 __device__ __forceinline__ uint8_t *sm_xs() { return smem_raw + kOffXs; }
+/* Norm weights, copied in (cp.async) right after their previous user's
+ * prologue: a global load in a prologue costs a round trip through a memory
+ * system saturated by the ring's copies */
+__device__ __forceinline__ float *sm_normw() { return reinterpret_cast<float *>(smem_raw + kOffNormW); }
+__device__ __forceinline__ float *sm_onorm() { return reinterpret_cast<float *>(smem_raw + kOffONorm); }
+/* All consumer threads: start copying n floats (n a multiple of 4) into shared memory. */
+__device__ __forceinline__ void prefetch_floats(float *dst, const float *src, int n) {
+    for (int i = threadIdx.x; i < n / 4; i += kConsumerThreads) cp_async16(smem_u32(dst + 4 * i), src + 4 * i);
+    cp_async_commit();
+}
 
 size_t decode_smem_bytes(int H, int I) { return kOffXs + (size_t)4 * (H > I ? H : I); }
 
@@ -564,12 +604,8 @@ __device__ __noinline__ W xwait(const DecodeParams &p, const W *a, uint32_t tag)
  * words, so the read completes one round trip after the last word lands.
  * All 32 lanes must call; lanes that use no word take part in the protocol
  * only. */
-template <int N, bool SYS, class Addr, class TagOf, class Use>
-__device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, const TagOf &tagof, const Use &use,
-                                      float (&v)[N]) {
-    typedef typename std::remove_const<typename std::remove_pointer<decltype(addr(0))>::type>::type W;
-    const int lane = threadIdx.x & 31;
-    W w[N];
+template <int N, bool SYS, class Addr, class TagOf, class Use, class W>
+__device__ __forceinline__ uint32_t xissue(const Addr &addr, const TagOf &tagof, const Use &use, W (&w)[N]) {
 #pragma unroll
     for (int i = 0; i < N; ++i)
         if (use(i)) w[i] = xget(addr(i), SYS);
@@ -577,9 +613,17 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, c
 #pragma unroll
     for (int i = 0; i < N; ++i)
         if (use(i) && !xtag_is(w[i], tagof(i))) missing |= 1u << i;
+    return missing;
+}
+template <int N, bool SYS, class Addr, class TagOf, class W>
+__device__ __forceinline__ bool xfinish(const DecodeParams &p, const Addr &addr, const TagOf &tagof, W (&w)[N],
+                                        uint32_t missing) {
+    const int lane = threadIdx.x & 31;
     uint64_t t0 = 0;
     uint32_t rounds = 0;
     while (__any_sync(0xffffffffu, missing != 0)) {
+        /* every lane re-reads its own missing words, so the read completes one
+         * round trip after the last word lands */
 #pragma unroll
         for (int i = 0; i < N; ++i)
             if ((missing >> i) & 1u) w[i] = xget(addr(i), SYS);
@@ -603,10 +647,26 @@ __device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, c
             }
         }
     }
+    return true;
+}
+/* Warp-wide read of exchange words: lane word i (i < N, where use(i)) lives
+ * at addr(i) and must carry tag tagof(i). Callers lay the words out so that a
+ * warp's loads are coalesced (consecutive lanes at consecutive addresses).
+ * Every load is issued at once, so data that is already there costs one
+ * round trip; while words are missing, every lane re-reads its own missing
+ * words. All 32 lanes must call; lanes that use no word take part in the
+ * protocol only. */
+template <int N, bool SYS, class Addr, class TagOf, class Use>
+__device__ __forceinline__ bool xread(const DecodeParams &p, const Addr &addr, const TagOf &tagof, const Use &use,
+                                      float (&v)[N]) {
+    typedef typename std::remove_const<typename std::remove_pointer<decltype(addr(0))>::type>::type W;
+    W w[N];
+    const uint32_t missing = xissue<N, SYS>(addr, tagof, use, w);
+    const bool ok = xfinish<N, SYS>(p, addr, tagof, w, missing);
 #pragma unroll
     for (int i = 0; i < N; ++i)
         if (use(i)) v[i] = xval(w[i]);
-    return true;
+    return ok;
 }
 
 /* Element i of a whole-vector read by consumer thread t: t + 480 i
@@ -686,13 +746,20 @@ struct Wide {
     __device__ __forceinline__ uint32_t chunks_per_pass() const { return K / 64 / G; }
     __device__ __forceinline__ uint32_t piece() const { return G * TR * 128; }  /* one tile's share of a chunk */
 };
-constexpr uint32_t kPassQKVG = 10, kPassGU = 5, kPassLM = 7;
-/* A narrow projection of R rows: rows [r0, r1), eight groups per chunk;
- * stored column-chunk-major, so a chunk of the rows is one copy. */
+/* tiles per pass: at most one warp per 8 rows and kSlotBytes per chunk */
+constexpr uint32_t kPassQKVG = 7, kPassGU = 7, kPassLM = 7;
+/* A narrow projection of R rows: rows [r0, r1), kNarrowGroups groups per
+ * chunk (the last chunk may have fewer); stored column-chunk-major, so a
+ * chunk of the rows is one copy. */
 struct Narrow {
     const uint8_t *base;
     uint32_t K, R, r0, r1;
-    __device__ __forceinline__ uint32_t chunks() const { return K / (64 * kNarrowGroups); }
+    __device__ __forceinline__ uint32_t chunks() const { return (K / 64 + kNarrowGroups - 1) / kNarrowGroups; }
+    __device__ __forceinline__ uint32_t groups(uint32_t j) const { return min((uint32_t)kNarrowGroups, K / 64 - j * kNarrowGroups); }
+    /* byte offset of chunk j's row r */
+    __device__ __forceinline__ size_t off(uint32_t j, uint32_t r) const {
+        return ((size_t)j * kNarrowGroups * R + (size_t)r * groups(j)) * 128u;
+    }
 };
 
 __device__ __forceinline__ const uint8_t *layer_base(const DecodeParams &p, int l) {
@@ -789,9 +856,10 @@ __device__ void producer(const DecodeParams &p, uint32_t cta, uint32_t ncta) {
     auto narrow = [&](const Narrow &w, uint32_t q) -> uint32_t {
         const uint32_t n = w.r1 - w.r0;
         for (uint32_t j = 0; j < w.chunks(); ++j, ++q) {
-            if (!claim_slot(p, q, n, n * 1024u)) return kStop;
+            const uint32_t bytes = n * w.groups(j) * 128u;
+            if (!claim_slot(p, q, n, bytes)) return kStop;
             if (lane == 0)
-                bulk_g2s(smem_u32(sm_slot(q % kSlots)), w.base + ((size_t)j * w.R + w.r0) * 1024u, n * 1024u,
+                bulk_g2s(smem_u32(sm_slot(q % kSlots)), w.base + w.off(j, w.r0), bytes,
                          smem_u32(&sm_full()[q % kSlots]), pol_w);
         }
         return q;
@@ -855,6 +923,7 @@ __device__ __forceinline__ float tree16_at(const uint8_t *wrow, uint32_t wsw, ui
  * reference's bank accumulation, c_impl/gdn_model.cpp:4444-4586). Returns
  * the row's (b0 + b1) + (b2 + b3) in lanes with b == 0 of active warps. */
 constexpr uint32_t kPair = 1;  /* chunks taken together by a warp (2 measured slower: fewer slots in flight) */
+constexpr uint32_t kMaxG = 4;   /* groups per chunk of a tiled projection, at most */
 
 template <int KIND>
 __device__ __forceinline__ float wide_chunks(const DecodeParams &p, const Wide &w, uint32_t n, uint32_t q) {
@@ -870,12 +939,12 @@ __device__ __forceinline__ float wide_chunks(const DecodeParams &p, const Wide &
             bool ok = true;
             for (uint32_t i = 0; i < u; ++i) ok = wait_full(p, q + i) && ok;
             if (!ok) continue;
-            float t[kPair][2];
+            float t[kPair][kMaxG];
 #pragma unroll
             for (uint32_t i = 0; i < kPair; ++i) {
                 const uint8_t *tile = sm_slot((q + i) % kSlots) + tw * w.piece() + rr * 128u;
 #pragma unroll
-                for (uint32_t gi = 0; gi < 2; ++gi)
+                for (uint32_t gi = 0; gi < kMaxG; ++gi)
                     t[i][gi] = (i < u && gi < w.G)
                                    ? tree16_at<KIND>(tile + gi * w.TR * 128u, rr & 7u, (j + i) * w.G + gi, b)
                                    : 0.0f;
@@ -883,7 +952,7 @@ __device__ __forceinline__ float wide_chunks(const DecodeParams &p, const Wide &
 #pragma unroll
             for (uint32_t i = 0; i < kPair; ++i)
 #pragma unroll
-                for (uint32_t gi = 0; gi < 2; ++gi)
+                for (uint32_t gi = 0; gi < kMaxG; ++gi)
                     if (i < u && gi < w.G) acc = __fadd_rn(acc, t[i][gi]);
             for (uint32_t i = 0; i < u; ++i) release(q + i);
         }
@@ -893,9 +962,10 @@ __device__ __forceinline__ float wide_chunks(const DecodeParams &p, const Wide &
 }
 
 /* A narrow projection: warp w owns row r0 + w; lane (b = lane / 8, s = lane
- * % 8) computes the tree16 of bank b of group 8 j + s of chunk j, and lane
- * (b, 0) adds the eight in group order to the bank's chain. Returns (b0 +
- * b1) + (b2 + b3) in lane 0 of active warps. */
+ * % 8) computes the tree16 of bank b of groups s and s + 8 of a chunk, and
+ * lane (b, 0) adds a chunk's values in group order to the bank's chain
+ * (gathered by warp shuffles). Returns (b0 + b1) + (b2 + b3) in lane 0 of
+ * active warps. */
 template <int KIND>
 __device__ __forceinline__ float narrow_chunks(const DecodeParams &p, const Narrow &w, uint32_t q) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -903,25 +973,21 @@ __device__ __forceinline__ float narrow_chunks(const DecodeParams &p, const Narr
     float acc = 0.0f;
     if ((uint32_t)warp < w.r1 - w.r0) {
         const uint32_t nc = w.chunks();
-        for (uint32_t j = 0; j < nc; j += kPair, q += kPair) {
-            const uint32_t u = min(kPair, nc - j);
-            bool ok = true;
-            for (uint32_t i = 0; i < u; ++i) ok = wait_full(p, q + i) && ok;
-            if (!ok) continue;
-            float t[kPair];
+        for (uint32_t j = 0; j < nc; ++j, ++q) {
+            const uint32_t ng = w.groups(j);
+            if (!wait_full(p, q)) continue;
+            const uint8_t *row = sm_slot(q % kSlots) + warp * ng * 128u;
+            const uint32_t g0 = j * kNarrowGroups;
+            const float t0 = tree16_at<KIND>(row + s * 128u, s, g0 + s, b);
+            const float t1 = ng > 8 ? tree16_at<KIND>(row + (8 + s) * 128u, s, g0 + 8 + s, b) : 0.0f;
+            release(q);
+            acc = __fadd_rn(acc, t0);
 #pragma unroll
-            for (uint32_t i = 0; i < kPair; ++i)
-                t[i] = i < u ? tree16_at<KIND>(sm_slot((q + i) % kSlots) + warp * 1024u + s * 128u, s,
-                                               (j + i) * kNarrowGroups + s, b)
-                             : 0.0f;
-            for (uint32_t i = 0; i < u; ++i) release(q + i);
+            for (int k = 1; k < 8; ++k) acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, t0, k));
+            if (ng > 8) {
+                acc = __fadd_rn(acc, t1);
 #pragma unroll
-            for (uint32_t i = 0; i < kPair; ++i) {
-                if (i < u) {
-                    acc = __fadd_rn(acc, t[i]);
-#pragma unroll
-                    for (int k = 1; k < kNarrowGroups; ++k) acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, t[i], k));
-                }
+                for (int k = 1; k < 8; ++k) acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, t1, k));
             }
         }
     }
@@ -957,6 +1023,41 @@ __device__ __forceinline__ float seq_sum(const float *a, int n) {
     }
     return sum;
 }
+/* Sequential sum, in index order from 0.0f, of n <= 128 values stored
+ * transposed in shared memory (value h at a[(h % 32) * 4 + h / 32]): each
+ * lane loads its four with one 16-byte load and the chain takes them from
+ * the lanes by shuffles, which do not depend on the sum and so run ahead of
+ * it. All 32 lanes call; every lane returns the sum. */
+__device__ __forceinline__ float seq_sum_warp(const float *a, int n) {
+    const int lane = threadIdx.x & 31;
+    const float4 v = reinterpret_cast<const float4 *>(a)[lane];
+    float sum = 0.0f;
+    /* four scalar passes (no indexed array: it would live in local memory) */
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+        const float x = __shfl_sync(0xffffffffu, v.x, k);
+        if (k < n) sum = __fadd_rn(sum, x);
+    }
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+        const float x = __shfl_sync(0xffffffffu, v.y, k);
+        if (32 + k < n) sum = __fadd_rn(sum, x);
+    }
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+        const float x = __shfl_sync(0xffffffffu, v.z, k);
+        if (64 + k < n) sum = __fadd_rn(sum, x);
+    }
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+        const float x = __shfl_sync(0xffffffffu, v.w, k);
+        if (96 + k < n) sum = __fadd_rn(sum, x);
+    }
+    return sum;
+}
+/* position of half sum h in the transposed layout of seq_sum_warp */
+__device__ __forceinline__ int tpos(int h) { return ((h & 31) << 2) + (h >> 5); }
+
 /* Sum of squares of 16 consecutive floats, sequential from 0.0f. */
 __device__ __forceinline__ float sq16(const float *a) {
     float hs = 0.0f;
@@ -980,13 +1081,12 @@ __device__ __forceinline__ float sq16(const float *a) {
 template <int MODE>
 __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const xword *y, uint32_t tag,
                                               const float *w, bool embed, float *hidden, int pidx, int xf) {
-    const int t = threadIdx.x, lane = t & 31;
+    const int t = threadIdx.x;
     const int halves = p.H >> 4;
     bool ok = true;
-    float x[kMaxPer], wv[kMaxPer];
-#pragma unroll
-    for (int i = 0; i < kMaxPer; ++i)
-        if (vec_elem(t, i) < p.H) wv[i] = __ldg(w + vec_elem(t, i));
+    float x[kMaxPer];
+    (void)w;
+    cp_async_wait_all();  /* this thread's share of the weights; the barrier below publishes all shares */
     if (embed) {
         if (p.token_src != nullptr) {
             const uint16_t *e = p.emb + (size_t)(*p.token_src) * p.H;
@@ -1011,21 +1111,19 @@ __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const xword *y
     for (int i = 0; i < kMaxPer; ++i)
         if (vec_elem(t, i) < p.H) sm_xres()[vec_elem(t, i)] = x[i];
     named_sync(1, kConsumerThreads);
-    if (t < halves) sm_red()[t] = sq16(sm_xres() + 16 * t);
+    if (t < halves) sm_red()[tpos(t)] = sq16(sm_xres() + 16 * t);
     named_sync(1, kConsumerThreads);
     if (t == 0) trace_put(p, pidx, 4);
-    float scale = 0.0f;
-    if (lane == 0) {
-        const float sum = seq_sum(sm_red(), halves);
-        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)p.H), p.eps)));
-        if (t == 0) trace_put(p, pidx, 6);
-    }
-    scale = __shfl_sync(0xffffffffu, scale, 0);
+    /* every warp forms the sum itself: no third barrier (and a single warp
+     * doing it while the others wait at a barrier measured far slower) */
+    const float sum = seq_sum_warp(sm_red(), halves);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)p.H), p.eps)));
+    if (t == 0) trace_put(p, pidx, 6);
     bool fast = true;
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
         if (vec_elem(t, i) < p.H) {
-            const float o = bnd<MODE>(__fmul_rn(__fmul_rn(x[i], scale), wv[i]));
+            const float o = bnd<MODE>(__fmul_rn(__fmul_rn(x[i], scale), sm_normw()[vec_elem(t, i)]));
             if (hidden != nullptr) hidden[vec_elem(t, i)] = o;
             xs_put<MODE>(vec_elem(t, i), o);
             fast = fast && fast_ok(p, o);
@@ -1046,18 +1144,38 @@ __device__ __noinline__ bool prologue_norm_gate(const DecodeParams &p, const flo
     const int t = threadIdx.x, lane = t & 31;
     const int halves = p.H >> 4;
     float *a_sh = sm_scratch();
-    float wv[kMaxPer];
+    (void)o_norm;
+    cp_async_wait_all();
+    /* v[i]: gate g; v[kMaxPer + i]: attention output; sg[i]: sigmoid(g) */
+    float v[2 * kMaxPer], sg[kMaxPer];
+    bool ok;
+    if (Mode<MODE>::kBf16) {
+        /* both reads issued before either is polled */
+        const gword *gw = reinterpret_cast<const gword *>(p.gate);
+        const auto *aw = xw<MODE>(p.attn);
+        auto use = [&](int i) { return vec_elem(t, i) < p.H; };
+        auto ga = [&](int i) { return gw + vec_elem(t, i); };
+        auto aa = [&](int i) { return aw + vec_elem(t, i); };
+        gword g[kMaxPer];
+        typename XW<MODE>::T a[kMaxPer];
+        const uint32_t mg = xissue<kMaxPer, Mode<MODE>::kTp>(ga, [&](int) { return tag_g; }, use, g);
+        const uint32_t ma = xissue<kMaxPer, Mode<MODE>::kTp>(aa, [&](int) { return tag_a; }, use, a);
+        ok = xfinish<kMaxPer, Mode<MODE>::kTp>(p, ga, [&](int) { return tag_g; }, g, mg);
+        ok = xfinish<kMaxPer, Mode<MODE>::kTp>(p, aa, [&](int) { return tag_a; }, a, ma) && ok;
 #pragma unroll
-    for (int i = 0; i < kMaxPer; ++i)
-        if (vec_elem(t, i) < p.H) wv[i] = __ldg(o_norm + (vec_elem(t, i) & (kHeadDim - 1)));
-    /* words [0, kMaxPer): gate; [kMaxPer, 2 kMaxPer): attention output */
-    float v[2 * kMaxPer];
-    const bool ok = xread<2 * kMaxPer, Mode<MODE>::kTp>(
-        p,
-        [&](int i) {
-            return i < kMaxPer ? xw<MODE>(p.gate) + vec_elem(t, i) : xw<MODE>(p.attn) + vec_elem(t, i - kMaxPer);
-        },
-        [&](int i) { return i < kMaxPer ? tag_g : tag_a; }, [&](int i) { return vec_elem(t, i % kMaxPer) < p.H; }, v);
+        for (int i = 0; i < kMaxPer; ++i) {
+            v[i] = gword_g(g[i]);
+            sg[i] = gword_sig(g[i]);
+            v[kMaxPer + i] = xval(a[i]);
+        }
+    } else {
+        ok = xread<2 * kMaxPer, Mode<MODE>::kTp>(
+            p,
+            [&](int i) {
+                return i < kMaxPer ? xw<MODE>(p.gate) + vec_elem(t, i) : xw<MODE>(p.attn) + vec_elem(t, i - kMaxPer);
+            },
+            [&](int i) { return i < kMaxPer ? tag_g : tag_a; }, [&](int i) { return vec_elem(t, i % kMaxPer) < p.H; }, v);
+    }
     if (t == 0) trace_put(p, pidx, 1);
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i)
@@ -1080,8 +1198,9 @@ __device__ __noinline__ bool prologue_norm_gate(const DecodeParams &p, const flo
         const float scale = __shfl_sync(0xffffffffu, hscale, (vec_elem(t, i) >> 8) & 31);
         if (vec_elem(t, i) < p.H) {
             const float gv = v[i];
-            const float normalized = __fmul_rn(__fmul_rn(v[kMaxPer + i], scale), wv[i]);
-            const float o = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv), sigmoid_b<MODE>(p, gv)));
+            const float normalized = __fmul_rn(__fmul_rn(v[kMaxPer + i], scale), sm_onorm()[vec_elem(t, i) & (kHeadDim - 1)]);
+            const float sig = Mode<MODE>::kBf16 ? sg[i] : sigmoid_ref(gv);
+            const float o = bnd<MODE>(__fmul_rn(__fmul_rn(normalized, gv), sig));
             xs_put<MODE>(vec_elem(t, i), o);
             fast = fast && fast_ok(p, o);
         }
@@ -1142,7 +1261,19 @@ __device__ __noinline__ bool phase_state(const DecodeParams &p, int l, uint32_t 
     const uint32_t h0 = c0 >> 8, h1 = (c1 - 1) >> 8, nhl = h1 - h0 + 1, n = c1 - c0;
     const uint32_t halves = (uint32_t)p.H >> 4, rows = 2 * nhl;
     bool ok = true;
-    /* 1. a/b rows: thread (row, half) forms one tree16, thread row chains them */
+    /* q, k of both heads (element t of each, threads 0..255), v of column
+     * c0 + t: the loads go out now and are polled after the a/b rows, so
+     * their round trip overlaps that work */
+    const bool qk = t < kHeadDim;
+    const auto *qb = xw<MODE>(p.qkv);
+    auto qaddr = [&](int k) {
+        return k == 4 ? qb + 2 * p.H + c0 + t : qb + (k & 1) * p.H + (h0 + (uint32_t)(k >> 1)) * kHeadDim + t;
+    };
+    auto qtag = [&](int) { return tag_in; };
+    auto quse = [&](int k) { return k == 4 ? (uint32_t)t < n : qk && (uint32_t)(k >> 1) < nhl; };
+    typename XW<MODE>::T qw[5];
+    const uint32_t qmiss = xissue<5, Mode<MODE>::kTp>(qaddr, qtag, quse, qw);
+    /* 1. a/b rows: thread (row, half) forms one tree16, warp row chains them */
     if ((uint32_t)warp < ab_warps(p, rows)) {
         if (wait_full(p, q)) {
             for (uint32_t idx = (uint32_t)t; idx < rows * halves; idx += kConsumerThreads) {
@@ -1179,24 +1310,18 @@ __device__ __noinline__ bool phase_state(const DecodeParams &p, int l, uint32_t 
                     s[i] = __fadd_rn(__fmul_rn(bf_lo(wv[i]), x[2 * i]), __fmul_rn(bf_hi(wv[i]), x[2 * i + 1]));
                 const float a0 = __fadd_rn(s[0], s[1]), a1 = __fadd_rn(s[2], s[3]);
                 const float a2 = __fadd_rn(s[4], s[5]), a3 = __fadd_rn(s[6], s[7]);
-                sm_park()[row * halves + hf] = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+                sm_park()[row * 128 + tpos((int)hf)] = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
             }
             release(q);
         }
     }
     ++q;
     named_sync(1, kConsumerThreads);
-    if ((uint32_t)t < rows) {
-        float acc = 0.0f;
-        for (uint32_t hf = 0; hf < halves; hf += 4) {
-            const float4 v4 = *reinterpret_cast<const float4 *>(sm_park() + t * halves + hf);
-            acc = __fadd_rn(acc, v4.x);
-            acc = __fadd_rn(acc, v4.y);
-            acc = __fadd_rn(acc, v4.z);
-            acc = __fadd_rn(acc, v4.w);
-        }
+    if ((uint32_t)warp < rows) {
+        /* one sequential chain over the row's halves in column order */
+        const float acc = seq_sum_warp(sm_park() + warp * 128, (int)halves);
         /* row 2 hs: a of head h0 + hs, row 2 hs + 1: b */
-        sm_hscal()[(t >> 1) * 8 + 3 + (t & 1)] = bnd<MODE>(acc);
+        if (lane == 0) sm_hscal()[(warp >> 1) * 8 + 3 + (warp & 1)] = bnd<MODE>(acc);
     }
     named_sync(1, kConsumerThreads);
     if (t == 0) trace_put(p, pidx, 4);
@@ -1216,23 +1341,11 @@ __device__ __noinline__ bool phase_state(const DecodeParams &p, int l, uint32_t 
         sm_hscal()[hs * 8 + 1] = sigmoid_b<MODE>(p, bb);
         sm_hscal()[hs * 8 + 2] = decay;
     }
-    /* 2. q, k of both heads (element t of each, threads 0..255), v of column c0 + t */
+    /* 2. q, k and v arrive */
     float w5[5];
-    {
-        const bool qk = t < kHeadDim;
-        const auto *qb = xw<MODE>(p.qkv);
-        ok = xread<5, Mode<MODE>::kTp>(
-                 p,
-                 [&](int k) {
-                     return k == 4 ? qb + 2 * p.H + c0 + t
-                                   : qb + (k & 1) * p.H + (h0 + (uint32_t)(k >> 1)) * kHeadDim + t;
-                 },
-                 [&](int) { return tag_in; },
-                 [&](int k) { return k == 4 ? (uint32_t)t < n : qk && (uint32_t)(k >> 1) < nhl; }, w5) &&
-             ok;
-        if (!qk) w5[0] = w5[1] = w5[2] = w5[3] = 0.0f;
-        if (nhl < 2) w5[2] = w5[3] = 0.0f;
-    }
+    ok = xfinish<5, Mode<MODE>::kTp>(p, qaddr, qtag, qw, qmiss) && ok;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) w5[k] = quse(k) ? xval(qw[k]) : 0.0f;
     if (t == 0) trace_put(p, pidx, 1);
     {
         float sq[4];
@@ -1272,11 +1385,18 @@ __device__ __noinline__ bool phase_state(const DecodeParams &p, int l, uint32_t 
         const uint8_t *col = slot + lane * cb;
         float acc = 0.0f;
         if (Mode<MODE>::kBf16State) {
+            /* the next piece's loads are issued before this piece's chain */
+            uint4 sn = lds128(col + (sw << 4));
+            float4 x0n = *reinterpret_cast<const float4 *>(vec), x1n = *reinterpret_cast<const float4 *>(vec + 4);
 #pragma unroll 4
             for (uint32_t c = 0; c < 32; ++c) {
-                const uint4 s = lds128(col + ((c ^ sw) << 4));
-                const float4 x0 = *reinterpret_cast<const float4 *>(vec + 8 * c);
-                const float4 x1 = *reinterpret_cast<const float4 *>(vec + 8 * c + 4);
+                const uint4 s = sn;
+                const float4 x0 = x0n, x1 = x1n;
+                if (c + 1 < 32) {
+                    sn = lds128(col + (((c + 1) ^ sw) << 4));
+                    x0n = *reinterpret_cast<const float4 *>(vec + 8 * (c + 1));
+                    x1n = *reinterpret_cast<const float4 *>(vec + 8 * (c + 1) + 4);
+                }
                 acc = __fadd_rn(acc, __fmul_rn(bf_lo(s.x), x0.x));
                 acc = __fadd_rn(acc, __fmul_rn(bf_hi(s.x), x0.y));
                 acc = __fadd_rn(acc, __fmul_rn(bf_lo(s.y), x0.z));
@@ -1391,6 +1511,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
     if (warp == kProducerWarp) {
         producer<MODE>(p, cta, ncta);
     } else {
+        prefetch_floats(sm_normw(), p.aux, p.H);
+        prefetch_floats(sm_onorm(), p.aux + p.H, kHeadDim);
         uint32_t q = 0;
         float best = -3.402823466e38f;
         int32_t best_i = 0x7fffffff;
@@ -1459,6 +1581,15 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                 named_sync(1, kConsumerThreads);
                 if (*sm_decision() == 0) { ok = false; break; }
                 if (t == 0) trace_put(p, pidx, 2);
+                /* the prologue is done with its norm weights: fetch the next ones */
+                if (ph == PH_QKVG) {
+                    prefetch_floats(sm_normw(), aux + p.H + kHeadDim, p.H);                  /* mlp_norm[l] */
+                } else if (ph == PH_GU) {
+                    prefetch_floats(sm_normw(), l + 1 < p.L ? aux + p.aux_stride : p.aux + (size_t)p.L * p.aux_stride,
+                                    p.H);                                                     /* attn_norm[l+1] / final */
+                } else if (ph == PH_O && l + 1 < p.L) {
+                    prefetch_floats(sm_onorm(), aux + p.aux_stride + p.H, kHeadDim);           /* o_norm[l+1] */
+                }
                 const bool exact = Mode<MODE>::kNative && (sm_exact()[xf] != 0 || p.force_exact != 0);
                 const bool drop = (int)cta == p.test_drop_cta && pidx == p.test_drop_phase;
                 if (ph == PH_STATE) {
@@ -1515,7 +1646,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                                 __stcg(reinterpret_cast<float4 *>(p.tails + (((size_t)l * 3 + kind) * p.H + d) * 4),
                                        make_float4(tail.y, tail.z, raw, 0.0f));
                             } else {
-                                xput<MODE>(p, p.gate, row - 3u * p.H, raw, tag_out);
+                                xput_gate<MODE>(p, row - 3u * p.H, raw, Mode<MODE>::kBf16 ? sigmoid_b<MODE>(p, raw) : 0.0f,
+                                                tag_out);
                             }
                         } else if (ph == PH_GU) {
                             /* rows 2i (gate) and 2i + 1 (up); SwiGLU as c_impl/gdn_model.cpp:4751-4770 */

@@ -8,12 +8,13 @@
  * stored XOR-permuted so that the kernel's warps read shared memory without
  * bank conflicts. Each projection is stored column-chunk-major, so that the
  * chunk a CTA needs (a column block of all its rows) is one contiguous copy:
- *   tiled projections (QKVG with 8-row tiles and 2 groups per chunk, GU with
- *     16-row tiles and 2, the LM head with 16-row tiles and 1):
+ *   tiled projections (QKVG with 8-row tiles and 4 groups per chunk, GU and
+ *     the LM head with 16-row tiles and 2):
  *     [column chunk j][tile t][group g of the chunk][row r][piece], logical
  *     piece p of row r at position p ^ (r & 7);
- *   row-major projections (O, DOWN): [column chunk j of 8 groups][row][group
- *     g][piece], logical piece p of group g at position p ^ (g & 7);
+ *   row-major projections (O, DOWN): [column chunk j of 16 groups (the last
+ *     may have fewer)][row][group g][piece], logical piece p of group g at
+ *     position p ^ (g & 7);
  *   AB: rows a_0, b_0, a_1, b_1, ... (the a/b projections of each head next to
  *     each other), natural column order.
  * Per layer l, at wimg + l * layer_stride bytes:
@@ -59,16 +60,16 @@ constexpr int kConsumerWarps = 15;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kProducerWarp = kConsumerWarps;      /* the last warp issues the ring's copies */
 constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kSlotBytes = 20480;
-constexpr int kSlots = 9;
+constexpr int kSlotBytes = 28672;
+constexpr int kSlots = 4;  /* 4 x 28 KB in flight per SM: more queues the latency-critical exchange traffic behind the weight stream (measured 6 slots 1.26, 5 1.23, 4 1.18, 3 1.23 ms/token) */
 constexpr int kPhasesPerLayer = 5;
 constexpr int kTraceSlots = 8;
-constexpr int kNarrowGroups = 8;     /* 64-column groups per chunk of O / DOWN */
+constexpr int kNarrowGroups = 16;    /* 64-column groups per chunk of O / DOWN (the last may have fewer) */
 constexpr int kMaxNarrowRows = kConsumerWarps;  /* O / DOWN rows per CTA: one per consumer warp */
 constexpr int kMaxStateCols = kConsumerWarps;   /* state columns per CTA: one per consumer warp */
-constexpr int kTileRowsQKVG = 8, kGroupsQKVG = 2;
+constexpr int kTileRowsQKVG = 8, kGroupsQKVG = 4;
 constexpr int kTileRowsGU = 16, kGroupsGU = 2;
-constexpr int kTileRowsLM = 16, kGroupsLM = 1;
+constexpr int kTileRowsLM = 16, kGroupsLM = 2;
 constexpr int kMaxExcBf16 = 8;       /* BF16-valued entries of the exp exception list, copied into the parameters */
 
 /* error codes written to DecodeStatus.err */

@@ -160,15 +160,17 @@ int engine_supports(const GDNWeightHeader &c) {
 /* Per-CTA limits of the decode kernel for `ncta` CTAs: every CTA owns units
  * of every phase (so that no CTA can run two phases ahead of one it reads
  * from), at most one O / DOWN row and one state column per consumer warp. */
-int engine_grid_ok(const GDNWeightHeader &c, int ncta) {
+int engine_grid_ok(const GDNWeightHeader &c, int ncta, bool report = true) {
     const uint32_t H = c.hidden_size, cols = c.num_heads * 256;
     const uint32_t units[] = {4 * H / gdn::kTileRowsQKVG, cols, H, 2 * c.intermediate_size / gdn::kTileRowsGU,
                               c.vocab_size / gdn::kTileRowsLM};
     for (uint32_t u : units)
-        if (u < (uint32_t)ncta) return fail("gdn_b200: %d CTAs exceed the %u units of a phase", ncta, u);
-    if ((H + ncta - 1) / ncta > (uint32_t)gdn::kMaxNarrowRows || (cols + ncta - 1) / ncta > (uint32_t)gdn::kMaxStateCols)
-        return fail("gdn_b200: %d CTAs are too few for this model (at most %d rows and state columns per CTA)", ncta,
-                    gdn::kMaxNarrowRows);
+        if (u < (uint32_t)ncta) return report ? fail("gdn_b200: %d CTAs exceed the %u units of a phase", ncta, u) : -1;
+    const uint32_t narrow_rows = std::min<uint32_t>(gdn::kMaxNarrowRows, gdn::kSlotBytes / (gdn::kNarrowGroups * 128));
+    if ((H + ncta - 1) / ncta > narrow_rows || (cols + ncta - 1) / ncta > (uint32_t)gdn::kMaxStateCols)
+        return report ? fail("gdn_b200: %d CTAs are too few for this model (at most %u O/DOWN rows and %d state "
+                             "columns per CTA)", ncta, narrow_rows, gdn::kMaxStateCols)
+                      : -1;
     return 0;
 }
 
@@ -210,11 +212,12 @@ inline void tiled_src(size_t i, size_t TR, size_t G, size_t rows, size_t *row, s
     *row = t * TR + r;
     *col = (j * G + gi) * 64 + (((c >> 3) ^ (r & 7)) << 3) + (c & 7);
 }
-inline void rowmajor_src(size_t i, size_t rows, size_t *row, size_t *col) {
-    const size_t chunk = rows * 512;
-    const size_t j = i / chunk, rem = i % chunk;
-    const size_t g = j * 8 + (rem % 512) / 64, c = rem % 64;
-    *row = rem / 512;
+inline void rowmajor_src(size_t i, size_t rows, size_t K, size_t *row, size_t *col) {
+    const size_t NG = gdn::kNarrowGroups, groups = K / 64;
+    const size_t j = i / (rows * NG * 64), rem = i - j * rows * NG * 64;
+    const size_t ng = std::min(NG, groups - j * NG);
+    const size_t cc = rem % (ng * 64), g = j * NG + cc / 64, c = cc % 64;
+    *row = rem / (ng * 64);
     *col = g * 64 + (((c >> 3) ^ (g & 7)) << 3) + (c & 7);
 }
 
@@ -363,13 +366,13 @@ DeviceModel *build_device_model(const GDNModel *model) {
                     r = j / H;
                     src = ((r & 1) ? w.b_proj : w.a_proj) + (r >> 1) * H + j % H;
                 } else if (i < dm->off_gu / 2) {
-                    rowmajor_src(i - dm->off_o / 2, H, &r, &col);
+                    rowmajor_src(i - dm->off_o / 2, H, H, &r, &col);
                     src = w.o_proj + r * H + col;
                 } else if (i < dm->off_down / 2) {
                     tiled_src(i - dm->off_gu / 2, gdn::kTileRowsGU, gdn::kGroupsGU, 2 * I, &r, &col);
                     src = ((r & 1) ? w.mlp_up_proj : w.mlp_gate_proj) + (r >> 1) * H + col;
                 } else {
-                    rowmajor_src(i - dm->off_down / 2, H, &r, &col);
+                    rowmajor_src(i - dm->off_down / 2, H, I, &r, &col);
                     src = w.mlp_down_proj + r * I + col;
                 }
                 st[so + (i - b)] = hi16(*src);
@@ -482,6 +485,7 @@ struct Stream {
     /* tensor-parallel decode (gdn_b200_tp_attach): the peers' exchange
      * regions mapped into this process */
     int tp_world = 1, tp_rank = 0;
+    int tp_grid = 0;      /* CTAs per GPU while attached: every phase must keep a unit for each CTA of all GPUs */
     void *tp_peer[gdn::kMaxTpRanks] = {};
     unsigned long long *rank_cand = nullptr;
     size_t xbytes = 0;   /* bytes of the exchange region: words, rank candidates, logits */
@@ -652,7 +656,7 @@ gdn::DecodeParams make_params(const Stream &s) {
 
 int launch(Stream &s, gdn::DecodeParams &p) {
     p.epoch = s.epoch;
-    const cudaError_t e = gdn::launch_decode(p, s.grid, s.stream);
+    const cudaError_t e = gdn::launch_decode(p, s.tp_world > 1 ? s.tp_grid : s.grid, s.stream);
     if (e != cudaSuccess) return fail("gdn_b200: decode launch failed: %s", cudaGetErrorString(e));
     s.epoch += gdn::epoch_stride(p.L);
     return 0;
@@ -1138,6 +1142,15 @@ int gdn_b200_tp_attach(GDNRunState *state, int rank, int world, const void *toke
             return fail("gdn_b200_tp_attach: mapping rank %d's exchange region failed: %s", r, cudaGetErrorString(e));
         }
     }
+    /* the largest per-GPU grid whose world * grid CTAs all own units of
+     * every phase (the GU projection's 16-row tiles run out first) */
+    int g = s->grid;
+    while (g > 0 && engine_grid_ok(s->dm->cfg, world * g, false) != 0) --g;
+    if (g == 0) {
+        tp_close(*s);
+        return fail("gdn_b200_tp_attach: no grid fits %d GPUs for this model", world);
+    }
+    s->tp_grid = g;
     s->tp_world = world;
     s->tp_rank = rank;
     /* every rank starts from the same tags */
