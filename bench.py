@@ -20,7 +20,11 @@ tokens, then exactly K timed tokens of the cyclic teacher-forced stream.
            reference arithmetic) on a bounded sample, rank 0 at N=1.
 
 N > 1 (torchrun): one process per GPU, each decoding its own stream with no
-collective (weak scaling); value = N * K / max-over-ranks time.
+collective (weak scaling); value = N * K / max-over-ranks time. Beside it
+the line carries `tp` (one stream decoded by all N GPUs
+together, its speed-up over one GPU and a bit-equality check against a
+one-GPU decode of the same tokens) and, at every N, `streams` (config[3]:
+64 streams per GPU, and 64 in total at N > 1, through gdn_b200_batch_*).
 
 --impl reference: the reference's own CPU decode (c_impl/gdn_model.cpp built
 natively by oracle/Makefile into oracle/_ref/gdn_ref_driver) timed on the host
@@ -43,7 +47,7 @@ sys.path.insert(0, REPO)
 METRIC = "GDN-1.3B batch-1 decode ms/token (inner+outer) & % HBM roofline; streams tok/s"
 WORKLOAD_TEXT = ("BASELINE config[2]: GDN-1.3B batch-1 sustained decode, seeded BF16 weights, seeded prompt then a "
                  "cyclic seeded 4096-token teacher stream")
-FPGA_INNER_MS = 8.141  # reference-published inner ms/token (Alveo U55C)
+FPGA_INNER_MS = 8.141  # the reference's published kernel ms/token on its Alveo U55C (c_impl/doc/architecture.md:37)
 from gateddeltanet_b200.workload import (PROMPT_OFFSET, SEED, SHAPE, STREAM_SEED, job_tokens_per_s,  # noqa: E402
                                          max_over_ranks, rank_streams, token_stream)
 
@@ -448,22 +452,121 @@ def sustained_window(rs, teacher, start, seconds, device, idle_w, barrier):
                     "gdn_decode_step_host per token with host buffers (wall clock)"}
 
 
-def contract_timing(model, teacher, numerics, device):
+def contract_timing(model, teacher, numerics, steps, warmup):
     """ms/token and roofline of another numeric contract on its own run state
-    (zero state, 64 warm-up and 1024 timed tokens)."""
+    (zero state; up to 64 warm-up and 1024 timed tokens, no more than the
+    headline's own)."""
     import gateddeltanet_b200 as gdn
+    n_w, n = min(warmup, 64), max(1, min(steps, 1024))
     rs = gdn.RunState(model)
     rs.set_numerics(*NUMERICS[numerics])
-    rs.decode([teacher[i] for i in range(64)])
-    _, ms = rs.decode([teacher[(64 + i) % 4096] for i in range(1024)])
+    if n_w:
+        rs.decode([teacher[i] for i in range(n_w)])
+    _, ms = rs.decode([teacher[(n_w + i) % 4096] for i in range(n)])
     rs.free()
-    ms_tok = ms / 1024
+    ms_tok = ms / n
     alg = algorithmic_bytes_per_token(numerics=numerics)
     peak, peak_kind = peaks()
     return {"numerics": numerics, "ms_per_token": round(ms_tok, 5), "tokens_per_s": round(1000.0 / ms_tok, 2),
             "roofline": {"achieved": round(alg / (ms_tok / 1000.0) / 1e9, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(alg / (ms_tok / 1000.0) / 1e9 / peak, 4), "algorithmic_bytes_per_launch": alg,
                          "kernel": f"gdn_decode_kernel<{KERNEL_MODE[numerics]}>"}}
+
+
+def tp_record(model, teacher, args, world, rank, barrier):
+    """BASELINE config[4] beside the stream-DP line at N > 1: one stream (the
+    seeded teacher stream from zero state) decoded by all N GPUs together
+    (gdn_b200_tp_attach; the kernel's row and column partitions over every
+    GPU's CTAs, peer stores over NVLink, no NCCL call on the data path),
+    max-over-ranks device time. Rank 0 then decodes the same tokens on one
+    GPU: tokens and final logits must be bit-identical on every rank, and so
+    must each rank's owned part of the recurrent state and conv tails."""
+    import hashlib
+    import torch.distributed as dist
+    import gateddeltanet_b200 as gdn
+    from gateddeltanet_b200 import tensor_parallel as tp
+    from gateddeltanet_b200.workload import max_over_ranks
+    n_w, n = min(args.warmup, 64), min(args.steps, 1024)
+    toks = [teacher[i % 4096] for i in range(n_w + n)]
+    dims = dict(SHAPE)
+    rs = gdn.RunState(model)
+    rs.set_numerics(*NUMERICS[args.numerics])
+    tp.attach(rs)
+    rs.decode(toks[:n_w])
+    barrier()
+    picks, ms = rs.decode(toks[n_w:])
+    barrier()
+    ms = max_over_ranks(ms, device="cuda")
+    logits, _ = rs.outputs()
+    rec, conv, grid, _, _ = rs.read_state_part()
+    rs.tp_detach()
+    barrier()
+    rs.free()
+    mine = (hashlib.sha256(tp.owned_values(rec, conv, dims, grid, rank, world)).hexdigest(),
+            hashlib.sha256(picks.tobytes()).hexdigest(), hashlib.sha256(logits.tobytes()).hexdigest())
+    seen = [None] * world
+    dist.all_gather_object(seen, mine)
+    rec_d = None
+    if rank == 0:
+        ref = gdn.RunState(model)
+        ref.set_numerics(*NUMERICS[args.numerics])
+        ref.decode(toks[:n_w])
+        r_picks, r_ms = ref.decode(toks[n_w:])
+        r_logits, _ = ref.outputs()
+        r_rec, r_conv = ref.read_state()
+        ref.free()
+        want = [(hashlib.sha256(tp.owned_values(r_rec, r_conv, dims, grid, r, world)).hexdigest(),
+                 hashlib.sha256(r_picks.tobytes()).hexdigest(), hashlib.sha256(r_logits.tobytes()).hexdigest())
+                for r in range(world)]
+        rec_d = {"gpus": world, "grid_per_gpu": grid, "steps": n, "warmup": n_w,
+                 "ms_per_token": round(ms / n, 5), "tokens_per_s": round(1000.0 * n / ms, 2),
+                 "one_gpu_ms_per_token": round(r_ms / n, 5), "speedup_vs_one_gpu": round(r_ms / ms, 3),
+                 "bit_identical_to_one_gpu": seen == want,
+                 "checked": "every rank's tokens, final logits and owned state part vs a one-GPU decode of the same "
+                            "tokens (SHA-256)",
+                 "numerics": args.numerics,
+                 "workload": "BASELINE config[4]: one GDN-1.3B stream over all GPUs from zero state, seeded "
+                             "teacher-forced tokens",
+                 "exchange": "row-split partitions over all GPUs' CTAs; every output stored into every GPU's "
+                             "exchange region by peer stores over NVLink (no NCCL call on the data path)",
+                 "timing": "CUDA events on each rank's stream, max over ranks"}
+    barrier()
+    return rec_d
+
+
+def streams_record(model, args, world, rank, barrier, per_gpu: int = 64, steps: int = 32, warmup: int = 4):
+    """BASELINE config[3] beside the batch-1 line: independent streams from
+    zero state advanced together (gdn_b200_batch_*, tcgen05 projections),
+    sharded over the ranks with no collective. weak: `per_gpu` streams on
+    every GPU; strong: `per_gpu` streams in total (split over the GPUs)."""
+    import numpy as np
+    import gateddeltanet_b200 as gdn
+    from gateddeltanet_b200.workload import max_over_ranks
+    out = {}
+    peak, peak_kind = peaks()
+    for kind, total in (("weak", per_gpu * world), ("strong", per_gpu)):
+        if (kind == "strong" and world == 1) or total % world:
+            continue
+        per = total // world
+        batch = gdn.Batch(model, per)
+        ids = rank_streams(rank, world, per)
+        toks = np.array([token_stream(i, warmup + steps, SHAPE["vocab"]) for i in ids], dtype=np.int32).T.copy()
+        batch.decode(toks[:warmup])
+        barrier()
+        _, ms = batch.decode(toks[warmup:])
+        barrier()
+        ms = max_over_ranks(ms, device="cuda")
+        launches = batch.launches_per_step
+        batch.free()
+        alg = step_bytes_streams(per)
+        out[kind] = {"streams": total, "streams_per_gpu": per, "steps": steps, "warmup": warmup,
+                     "ms_per_step": round(ms / steps, 5), "tokens_per_s": round(total * steps / (ms / 1000.0), 1),
+                     "roofline_frac": round(alg / (ms / steps / 1000.0) / 1e9 / peak, 4),
+                     "algorithmic_bytes_per_gpu_step": alg, "launches_per_step": launches}
+    out["config"] = ("BASELINE config[3]: independent GDN-1.3B streams from zero fp32 state, seeded teacher-forced "
+                     "tokens per stream, FP32-boundary numerics, tcgen05 tile GEMMs; one CUDA graph per step; "
+                     f"CUDA events, max over ranks; peak {peak_kind}")
+    return out
 
 
 def main():
@@ -480,6 +583,8 @@ def main():
     ap.add_argument("--sustain-s", type=float, default=20.0,
                     help="length of the sustained window (config[2], energy per token); 0 skips it")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="leave out the tp (N > 1) and streams sub-records beside the headline")
     ap.add_argument("--workload", default="decode", choices=["decode", "delta_rule", "streams", "prefill", "tp"],
                     help="decode: the headline batch-1 decode (default); delta_rule: BASELINE config[1]; "
                          "streams: BASELINE config[3] multi-stream decode; tp: BASELINE config[4], one stream "
@@ -573,7 +678,7 @@ def main():
     # engine contract (exact products, FP32 state) on its own run state
     other = None
     if not tp_mode and args.numerics == "cimpl":
-        other = contract_timing(model, teacher, "engine", local)
+        other = contract_timing(model, teacher, "engine", args.steps, args.warmup)
     ms_per_tok = kernel_ms / args.steps
     streams_in_job = 1 if tp_mode else world
     value = job_tokens_per_s(streams_in_job, args.steps, kernel_ms / 1000.0)
@@ -619,10 +724,6 @@ def main():
                                 "launch per token)")},
         "gpu_launches": args.steps,
         "clocks": sampler.summary(),
-        **({"tp": {"gpus": world, "exchange": "row-split partitions over all GPUs' CTAs; every output stored into "
-                                            "every GPU's exchange region by peer stores over NVLink (no NCCL call "
-                                            "on the data path)",
-                   "bit_identical_to_one_gpu": True}} if tp_mode else {}),
         "energy": energy_line(window, args.steps, idle_w),
         **({"sustained": sustained} if sustained is not None else {}),
         **({"other_contract": other} if other is not None else {}),
@@ -637,6 +738,12 @@ def main():
         rs.tp_detach()  # every rank unmaps its peers before any rank frees its region
         barrier()
     rs.free()
+    # beside the headline: config[4] (one stream over all GPUs) at N > 1 and
+    # config[3] (64 streams per GPU, and 64 in total at N > 1)
+    if world > 1 and not args.no_extra:
+        line["tp"] = tp_record(model, teacher if tp_mode else token_stream(0, 4096, V), args, world, rank, barrier)
+    if not tp_mode and not args.no_extra:
+        line["streams"] = streams_record(model, args, world, rank, barrier)
     model.free()
     if rank == 0:
         print(json.dumps(line))

@@ -137,6 +137,7 @@ EXPORTS = [
      [ctypes.c_uint32, _FP, _FP, _FP, _FP, _FP, _FP, _FP, ctypes.c_uint32, _FP]),
     ("gdn_b200_test_drop_outputs", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int, ctypes.c_int]),
     ("gdn_b200_test_force_exact_products", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int]),
+    ("gdn_b200_test_set_epoch", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_uint32]),
     ("gdn_b200_grid_size", ctypes.c_int, []),
     ("gdn_b200_batch_create", ctypes.c_void_p, [ctypes.POINTER(GDNModel), ctypes.c_uint32]),
     ("gdn_b200_batch_free", None, [ctypes.c_void_p]),
@@ -163,6 +164,10 @@ EXPORTS = [
     ("gdn_b200_tp_token", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_void_p]),
     ("gdn_b200_tp_attach", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int, ctypes.c_int, ctypes.c_char_p]),
     ("gdn_b200_tp_detach", ctypes.c_int, [ctypes.POINTER(GDNRunState)]),
+    ("gdn_b200_tp_state_download_part", ctypes.c_int,
+     [ctypes.POINTER(GDNRunState), ctypes.POINTER(ctypes.c_float), ctypes.c_size_t, ctypes.POINTER(ctypes.c_float),
+      ctypes.c_size_t, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32),
+      ctypes.POINTER(ctypes.c_int32)]),
 ]
 
 GDN_B200_TP_TOKEN_BYTES = 128
@@ -369,6 +374,30 @@ class RunState:
         check(self.lib.gdn_b200_state_download(ctypes.byref(self.s), _fptr(rec), rec.size, _fptr(conv), conv.size),
               "gdn_b200_state_download")
         return rec, conv
+
+    def save_state(self, path: str, seed_token: int = 0) -> None:
+        """gdn_b200_state_save_file: the state as a .gdnstate file."""
+        check(self.lib.gdn_b200_state_save_file(ctypes.byref(self.s), os.fsencode(path), int(seed_token)),
+              "gdn_b200_state_save_file")
+
+    def load_state_file(self, path: str) -> int:
+        """gdn_b200_state_load_file; returns the file's seed token."""
+        tok = ctypes.c_int32()
+        check(self.lib.gdn_b200_state_load_file(ctypes.byref(self.s), os.fsencode(path), ctypes.byref(tok)),
+              "gdn_b200_state_load_file")
+        return tok.value
+
+    def read_state_part(self):
+        """gdn_b200_tp_state_download_part: this rank's part of a
+        tensor-parallel state and the attachment it came from, as
+        (rec, conv, grid, rank, world) for tensor_parallel.merge_state."""
+        rec = np.empty(self.rec_floats, dtype=np.float32)
+        conv = np.empty(self.conv_floats, dtype=np.float32)
+        g, r, w = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        check(self.lib.gdn_b200_tp_state_download_part(ctypes.byref(self.s), _fptr(rec), rec.size, _fptr(conv),
+                                                       conv.size, ctypes.byref(g), ctypes.byref(r),
+                                                       ctypes.byref(w)), "gdn_b200_tp_state_download_part")
+        return rec, conv, g.value, r.value, w.value
 
     def tp_token(self) -> bytes:
         """gdn_b200_tp_token: what the peers of a tensor-parallel decode need to map this run state."""

@@ -486,6 +486,10 @@ struct Stream {
      * regions mapped into this process */
     int tp_world = 1, tp_rank = 0;
     int tp_grid = 0;      /* CTAs per GPU while attached: every phase must keep a unit for each CTA of all GPUs */
+    /* the state holds one rank's part since a tensor-parallel step (until a
+     * full upload); part_* is the attachment that step ran under */
+    bool tp_part = false;
+    int part_grid = 0, part_rank = 0, part_world = 1;
     void *tp_peer[gdn::kMaxTpRanks] = {};
     unsigned long long *rank_cand = nullptr;
     size_t xbytes = 0;   /* bytes of the exchange region: words, rank candidates, logits */
@@ -654,7 +658,22 @@ gdn::DecodeParams make_params(const Stream &s) {
     return p;
 }
 
+/* A run state that holds one rank's part of a tensor-parallel state. */
+int refuse_part(const Stream &s, const char *what) {
+    return fail("gdn_b200: %s: the run state holds rank %d's part of a tensor-parallel state (%s); join the "
+                "ranks' parts (gdn_b200_tp_state_download_part, tensor_parallel.merge_state) and upload the full "
+                "state first",
+                what, s.part_rank, s.tp_world > 1 ? "attached" : "since its last tensor-parallel step");
+}
+
 int launch(Stream &s, gdn::DecodeParams &p) {
+    if (s.tp_world == 1 && s.tp_part) return refuse_part(s, "single-GPU decode");
+    if (s.tp_world > 1) {
+        s.tp_part = true;
+        s.part_grid = s.tp_grid;
+        s.part_rank = s.tp_rank;
+        s.part_world = s.tp_world;
+    }
     p.epoch = s.epoch;
     const cudaError_t e = gdn::launch_decode(p, s.tp_world > 1 ? s.tp_grid : s.grid, s.stream);
     if (e != cudaSuccess) return fail("gdn_b200: decode launch failed: %s", cudaGetErrorString(e));
@@ -752,6 +771,7 @@ int host_device() { return g_device; }
 int host_state_begin(GDNRunState *state, float **S, float **tails, int *device, cudaStream_t *stream) {
     Stream *s = find_stream(state);
     if (s == nullptr) return fail("gdn_b200: unknown run state");
+    if (s->tp_world > 1 || s->tp_part) return refuse_part(*s, "prefill");
     const GDNWeightHeader &c = s->dm->cfg;
     const size_t cols = (size_t)c.num_layers * c.num_heads * 256;
     CUDA_OK(cudaSetDevice(s->device));
@@ -1222,6 +1242,9 @@ int gdn_b200_set_numerics(GDNRunState *state, int bf16_boundary, int bf16_produc
         return fail("gdn_b200: numerics (%d, %d, %d) is not a contract of this engine: (1, 1, 1) the reference's "
                     "own (c_impl), (1, 0, 0) exact products with FP32 state, (0, 0, 0) the FP32 control",
                     boundary, products, bstate);
+    if (s->tp_world > 1)
+        return fail("gdn_b200: numerics cannot change while the run state is attached for tensor parallelism "
+                    "(every rank must run the same contract): detach every rank first");
     CUDA_OK(cudaSetDevice(s->device));
     if (bstate != s->bf16_state) {
         /* the state changes storage (BF16 <-> FP32): convert it in place */
@@ -1253,6 +1276,13 @@ int gdn_b200_test_force_exact_products(GDNRunState *state, int on) {
     Stream *s = find_stream(state);
     if (s == nullptr) return fail("gdn_b200: unknown run state");
     s->force_exact = on ? 1 : 0;
+    return 0;
+}
+
+int gdn_b200_test_set_epoch(GDNRunState *state, uint32_t epoch) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    s->epoch = epoch;
     return 0;
 }
 
@@ -1627,7 +1657,9 @@ int gdn_b200_state_upload(GDNRunState *state, const float *rec, size_t rec_float
     const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
     if (rec_floats != L * nh * 256 * 256 || conv_floats != L * 3 * 3 * H)
         return fail("gdn_b200: state sizes do not match the model (rec %zu, conv %zu)", rec_floats, conv_floats);
-    return upload_state(*s, rec, conv);
+    if (upload_state(*s, rec, conv) != 0) return -1;
+    s->tp_part = false;  /* a full state again */
+    return 0;
 }
 
 int gdn_b200_state_download(GDNRunState *state, float *rec, size_t rec_floats, float *conv, size_t conv_floats) {
@@ -1637,7 +1669,26 @@ int gdn_b200_state_download(GDNRunState *state, float *rec, size_t rec_floats, f
     const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
     if (rec_floats != L * nh * 256 * 256 || conv_floats != L * 3 * 3 * H)
         return fail("gdn_b200: state sizes do not match the model");
+    if (s->tp_world > 1 || s->tp_part) return refuse_part(*s, "state download");
     return download_state(*s, rec, conv);
+}
+
+int gdn_b200_tp_state_download_part(GDNRunState *state, float *rec, size_t rec_floats, float *conv,
+                                    size_t conv_floats, int32_t *tp_grid, int32_t *tp_rank, int32_t *tp_world) {
+    Stream *s = find_stream(state);
+    if (s == nullptr) return fail("gdn_b200: unknown run state");
+    const GDNWeightHeader &c = s->dm->cfg;
+    const size_t L = c.num_layers, nh = c.num_heads, H = c.hidden_size;
+    if (rec_floats != L * nh * 256 * 256 || conv_floats != L * 3 * 3 * H)
+        return fail("gdn_b200: state sizes do not match the model");
+    if (!s->tp_part)
+        return fail("gdn_b200: the run state took no tensor-parallel step since its last full upload "
+                    "(gdn_b200_state_download gives its state)");
+    if (download_state(*s, rec, conv) != 0) return -1;
+    if (tp_grid != nullptr) *tp_grid = s->part_grid;
+    if (tp_rank != nullptr) *tp_rank = s->part_rank;
+    if (tp_world != nullptr) *tp_world = s->part_world;
+    return 0;
 }
 
 int gdn_b200_state_load_file(GDNRunState *state, const char *path, int32_t *seed_token) {

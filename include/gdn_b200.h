@@ -142,6 +142,13 @@ int gdn_b200_test_drop_outputs(GDNRunState *state, int cta, int phase);
  * can fall below the normal range. Results are identical either way. */
 int gdn_b200_test_force_exact_products(GDNRunState *state, int on);
 
+/* Test hook (no counterpart in the reference): the exchange tag base of the
+ * next launch of `state` (the host advances it by 5 L + 1 per launch; in the
+ * BF16-boundary contracts only its low 16 bits reach the exchange words).
+ * Lets a test start launches whose tags wrap past 0xffff, the tag of a word
+ * that was never written since the exchange buffers were last refilled. */
+int gdn_b200_test_set_epoch(GDNRunState *state, uint32_t epoch);
+
 /* Reference-ABI compatibility for the run states created afterwards (also
  * GDN_B200_ABI_COMPAT=1 in the environment): gdn_run_state_init then builds
  * the reference's host images (32 packed shards with the BF16 state stripes,
@@ -171,12 +178,28 @@ int gdn_b200_grid_size(void);
  *      tokens in rank order, then a barrier before the first step;
  *   3. every rank makes the same decode calls with the same tokens, in step.
  * Ranks must sit on distinct devices with the same SM count. A rank that does
- * not take part lets the others' waits run out (2 s): the step returns -1. */
+ * not take part lets the others' waits run out (2 s): the step returns -1;
+ * attaching every rank again (step 2) and reloading the state recovers.
+ * After the first tensor-parallel step a run state holds one rank's part of
+ * the state until a full state is uploaded (gdn_b200_state_upload): while it
+ * does, gdn_b200_state_download, gdn_b200_state_save_file, gdn_b200_prefill
+ * and (after gdn_b200_tp_detach) single-GPU decode return -1. The parts come
+ * out through gdn_b200_tp_state_download_part; the Python layer's
+ * tensor_parallel.merge_state joins them into the full state. */
 #define GDN_B200_TP_TOKEN_BYTES 128
 int gdn_b200_tp_token(GDNRunState *state, void *token);
 int gdn_b200_tp_attach(GDNRunState *state, int rank, int world, const void *tokens);
-/* back to single-GPU decode (the state this rank does not own is stale) */
+/* back to single-GPU decode (the state stays partial: see above) */
 int gdn_b200_tp_detach(GDNRunState *state);
+/* This rank's part of a tensor-parallel state in the gdn_b200_state_download
+ * layout (the columns and conv channels other ranks own hold stale values),
+ * with the attachment it came from: *tp_grid CTAs per GPU, *tp_rank of
+ * *tp_world GPUs (unit u of a phase with `total` units belongs to global CTA
+ * c when c * total / (world * grid) <= u < (c + 1) * total / (world * grid),
+ * and global CTA c to rank c / grid). -1 if the run state never took a
+ * tensor-parallel step since its last full upload. */
+int gdn_b200_tp_state_download_part(GDNRunState *state, float *rec, size_t rec_floats, float *conv,
+                                    size_t conv_floats, int32_t *tp_grid, int32_t *tp_rank, int32_t *tp_world);
 
 /* ---------------------------------------------------- multi-stream decode
  * Several independent decode streams on one GPU (no

@@ -1,8 +1,9 @@
 """Host logic of tensor-parallel decode, on the CPU.
 
 * owner_rank / unit_owner reproduce the decode kernel's unit partition over
-  the global CTAs (c * total // ncta, gdn_decode.cu geom_compute) for every
-  phase size of GDN-1.3B at 2..8 GPUs, and give every rank a share;
+  the global CTAs (c * total // ncta, gdn_decode.cu span_of) for every phase
+  of GDN-1.3B at 2..8 GPUs with the grid the library picks (tp_grid), and
+  give every rank a share;
 * merge_state rebuilds the full recurrent state and conv tails from ranks that
   each hold only their own columns and channels (the rest garbage);
 * attach() over two gloo ranks gathers the tokens in rank order, hands each
@@ -29,11 +30,11 @@ def _kernel_partition(total, ncta):
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_owner_matches_the_kernel_partition(world):
-    grid = 148
+    grid = tp.tp_grid(FULL, world, 148)
+    assert grid == (88 if world == 8 else 148)  # 704 gate/up tiles bind at 8 GPUs
     ncta = grid * world
-    H, nh, I, V = FULL["hidden"], FULL["heads"], FULL["inter"], FULL["vocab"]
-    for total in (4 * H + 2 * nh, nh * 256, H, I, V):
-        assert total >= ncta  # no CTA of GDN-1.3B is left without units at <= 8 GPUs
+    for name, total in tp.phase_units(FULL).items():
+        assert total >= ncta, name
         owner = tp.unit_owner(np.arange(total), total, ncta)
         for c, (u0, u1) in enumerate(_kernel_partition(total, ncta)):
             assert (owner[u0:u1] == c).all()
@@ -44,13 +45,15 @@ def test_owner_matches_the_kernel_partition(world):
 
 @pytest.mark.parametrize("world", [2, 3])
 def test_merge_state_takes_each_unit_from_its_owner(world):
-    dims, grid = SMALL, 148
+    dims = SMALL
+    grid = tp.tp_grid(dims, world, 148)
     L, nh, dk, H = dims["layers"], dims["heads"], dims["head_dim"], dims["hidden"]
     rng = np.random.default_rng(1)
     rec = rng.standard_normal(L * nh * dk * dk).astype(np.float32)
     conv = rng.standard_normal(L * 3 * 3 * H).astype(np.float32)
     col_rank = tp.owner_rank(np.arange(nh * dk), nh * dk, grid, world).reshape(nh, dk)
-    ch_rank = tp.owner_rank(np.arange(3 * H), 4 * H + 2 * nh, grid, world).reshape(3, H)
+    # conv channel of row r: the owner of r's 8-row QKVG tile
+    ch_rank = tp.owner_rank(np.arange(3 * H) // 8, 4 * H // 8, grid, world).reshape(3, H)
     parts = []
     for r in range(world):
         pr = np.full((L, nh, dk, dk), np.nan, dtype=np.float32)
@@ -59,9 +62,12 @@ def test_merge_state_takes_each_unit_from_its_owner(world):
         pr[m] = rec.reshape(pr.shape)[m]
         mc = np.broadcast_to((ch_rank == r)[None, :, None, :], pc.shape)
         pc[mc] = conv.reshape(pc.shape)[mc]
-        parts.append((pr.reshape(-1), pc.reshape(-1)))
-    m_rec, m_conv = tp.merge_state(parts, dims, grid)
+        parts.append((pr.reshape(-1), pc.reshape(-1), grid, r, world))
+    m_rec, m_conv = tp.merge_state(parts, dims)
     assert np.array_equal(m_rec, rec) and np.array_equal(m_conv, conv)
+    # the grid travels with the parts; parts from another attachment are refused
+    with pytest.raises(ValueError):
+        tp.merge_state([(a, b, grid, (r + 1) % world, world) for r, (a, b, *_) in enumerate(parts)], dims)
 
 
 class _FakeRunState:

@@ -6,7 +6,11 @@ state to the others (gateddeltanet_b200.tensor_parallel.attach) and decodes a
 teacher-forced stream, then a greedy continuation. Rank 0 then decodes the
 same tokens on one GPU with a run state of its own and compares: tokens,
 logits and the merged recurrent state and conv tails must be identical bit
-for bit. The verdict goes to --out as JSON.
+for bit. Each rank also records that the library refuses whole-state reads,
+saves, prefill and (after detaching) single-GPU decode of its partial state.
+With --failure, rank 1 then sits out one step: rank 0's step must fail with
+the exchange-wait timeout, and after every rank attaches again the decode
+must again equal the single-GPU decode. The verdict goes to --out as JSON.
 """
 from __future__ import annotations
 
@@ -39,6 +43,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=12)
     ap.add_argument("--greedy", type=int, default=6)
     ap.add_argument("--out", required=True)
+    ap.add_argument("--failure", action="store_true", help="also run the failure-path check")
     args = ap.parse_args()
     dims = DIMS[args.dims]
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -63,24 +68,38 @@ def main() -> int:
         out, ms = state.decode(teacher)
         logits, _ = state.outputs()
         greedy, _ = state.decode([int(out[-1])] * args.greedy, greedy=True)
-        rec, conv = state.read_state()
-        return out, ms, logits, greedy, rec, conv
+        return out, ms, logits, greedy
+
+    def refused(fn) -> bool:
+        try:
+            fn()
+        except RuntimeError as e:
+            return "tensor-parallel state" in str(e)
+        return False
 
     tp.attach(rs)
-    out, ms, logits, greedy, rec, conv = run(rs, True)
-    grid = L.gdn_b200_grid_size()
+    out, ms, logits, greedy = run(rs, True)
+    # while attached, the state is this rank's part only: whole-state reads,
+    # .gdnstate saves and prefill are refused
+    guards = {"download_refused": refused(rs.read_state),
+              "save_refused": refused(lambda: rs.save_state(os.devnull)),
+              "prefill_refused": refused(lambda: rs.prefill([1, 2, 3]))}
+    part = rs.read_state_part()
     parts = [None] * world if rank == 0 else None
-    dist.gather_object((rec, conv), parts, dst=0)
+    dist.gather_object(part, parts, dst=0)
     seen = [None] * world
     dist.all_gather_object(seen, (out.tolist(), greedy.tolist(), logits.tobytes()))
     rs.tp_detach()
+    guards["single_gpu_decode_refused"] = refused(lambda: rs.step(int(teacher[0])))
     dist.barrier()
+    res = {}
     if rank == 0:
         ref = gdn.RunState(model)
-        r_out, r_ms, r_logits, r_greedy, r_rec, r_conv = run(ref, False)
-        m_rec, m_conv = tp.merge_state(parts, dims, grid)
+        r_out, r_ms, r_logits, r_greedy = run(ref, False)
+        r_rec, r_conv = ref.read_state()
+        m_rec, m_conv = tp.merge_state(parts, dims)
         res = {
-            "world": world, "grid": grid, "dims": args.dims,
+            "world": world, "grid": part[2], "dims": args.dims,
             "tokens_equal": bool(np.array_equal(out, r_out)),
             "greedy_equal": bool(np.array_equal(greedy, r_greedy)),
             "logits_bitwise_equal": bool(np.array_equal(logits.view(np.uint32), r_logits.view(np.uint32))),
@@ -90,9 +109,43 @@ def main() -> int:
             "tp_ms_per_token": ms / args.steps, "one_gpu_ms_per_token": r_ms / args.steps,
             "tokens": out.tolist(), "greedy": greedy.tolist(),
         }
+        ref.free()
+    # every rank's guards, gathered on rank 0
+    all_guards = [None] * world if rank == 0 else None
+    dist.gather_object(guards, all_guards, dst=0)
+    if rank == 0:
+        res["guards"] = all_guards
+    if args.failure:
+        # failure path: rank 1 sits out one step between steps (no kernel of
+        # its own in flight); rank 0's bounded exchange waits run out and its
+        # step returns -1. Then every rank attaches again, reloads the state
+        # and the decode equals the single-GPU decode bit for bit.
+        tp.attach(rs)
+        rs.load_state(rec0, conv0)
+        dist.barrier()
+        err = ""
+        if rank == 0:
+            try:
+                rs.step(int(teacher[0]))
+            except RuntimeError as e:
+                err = str(e)
+        dist.barrier()  # rank 0's failed step has ended before anyone re-attaches
+        tp.attach(rs)
+        out2, _, logits2, greedy2 = run(rs, True)
+        if rank == 0:
+            res["failure"] = {
+                "step_error": err,
+                "timed_out": "exchange wait timeout" in err,
+                "tokens_equal_after_reattach": bool(np.array_equal(out2, out)),
+                "logits_bitwise_equal_after_reattach": bool(np.array_equal(logits2.view(np.uint32),
+                                                                           logits.view(np.uint32))),
+                "greedy_equal_after_reattach": bool(np.array_equal(greedy2, greedy)),
+            }
+        rs.tp_detach()
+        dist.barrier()
+    if rank == 0:
         with open(args.out, "w") as f:
             json.dump(res, f)
-        ref.free()
     dist.barrier()
     rs.free()
     model.free()
