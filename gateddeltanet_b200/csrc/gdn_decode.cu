@@ -478,7 +478,8 @@ constexpr size_t kOffWbestI = kOffWbest + 16 * 4;                        /* 16 i
 constexpr size_t kOffBars = kOffWbestI + 16 * 4;                         /* full[kSlots], empty[kSlots] */
 constexpr size_t kOffIssued = kOffBars + 2 * kSlots * 8;                 /* [kSlots] u32 */
 constexpr size_t kOffFlags = kOffIssued + kSlots * 4;                    /* abort, decision, exact[2] */
-constexpr size_t kOffExpTab = (kOffFlags + 16 + 15) & ~(size_t)15;       /* 128 floats */
+constexpr size_t kOffSched = (kOffFlags + 16 + 15) & ~(size_t)15;        /* the CTA's Sched (256 bytes) */
+constexpr size_t kOffExpTab = kOffSched + 256;                           /* 128 floats */
 constexpr size_t kOffNormW = kOffExpTab + 128 * 4;                       /* next RMSNorm weights, H floats */
 constexpr size_t kOffONorm = kOffNormW + kMaxHidden * 4;                 /* next output-norm weights, 256 */
 constexpr size_t kOffXs = kOffONorm + kHeadDim * 4;                      /* phase input */
@@ -530,6 +531,16 @@ __device__ __forceinline__ float *sm_onorm() { return reinterpret_cast<float *>(
 /* All consumer threads: start copying n floats (n a multiple of 4) into shared memory. */
 __device__ __forceinline__ void prefetch_floats(float *dst, const float *src, int n) {
     for (int i = threadIdx.x; i < n / 4; i += kConsumerThreads) cp_async16(smem_u32(dst + 4 * i), src + 4 * i);
+    cp_async_commit();
+}
+/* The same by the consumer warps from w0 on (the warps a GEMV leaves idle:
+ * the copy then costs the working warps nothing); all of them when w0 is
+ * past the last consumer warp. */
+__device__ __forceinline__ void prefetch_floats_idle(float *dst, const float *src, int n, uint32_t w0) {
+    if (w0 >= (uint32_t)kConsumerWarps) w0 = 0;
+    const int i0 = (int)threadIdx.x - (int)(w0 * 32u), nthr = (kConsumerWarps - (int)w0) * 32;
+    if (i0 < 0) return;
+    for (int i = i0; i < n / 4; i += nthr) cp_async16(smem_u32(dst + 4 * i), src + 4 * i);
     cp_async_commit();
 }
 
@@ -732,8 +743,13 @@ __device__ __forceinline__ void release(uint32_t q) {
 struct Span {
     uint32_t u0, u1;
 };
+/* a * b / c, in 32 bits when the product fits */
+__device__ __forceinline__ uint32_t mul_div(uint32_t a, uint32_t b, uint32_t c) {
+    const uint64_t m = (uint64_t)a * b;
+    return (m >> 32) ? (uint32_t)(m / c) : (uint32_t)m / c;
+}
 __device__ __forceinline__ Span span_of(uint32_t total, uint32_t cta, uint32_t ncta) {
-    return Span{(uint32_t)(((uint64_t)cta * total) / ncta), (uint32_t)(((uint64_t)(cta + 1) * total) / ncta)};
+    return Span{mul_div(cta, total, ncta), mul_div(cta + 1, total, ncta)};
 }
 
 /* A tiled (wide) projection: T tiles of TR rows, G 64-column groups per
@@ -830,64 +846,142 @@ __device__ __forceinline__ bool claim_slot(const DecodeParams &p, uint32_t q, ui
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-/* The producer warp: walks the CTA's schedule (per layer A, B = {a/b rows,
- * state columns}, C, D, E; then the LM head), one chunk per slot, each
- * chunk's copies spread over the warp's lanes. */
+/* The CTA's chunk schedule, in the order the consumers take the chunks: per
+ * layer the QKVG chunks, the a/b rows of its heads, its state columns, the
+ * O chunks, the gate/up chunks, the DOWN chunks; then the LM head's. Built
+ * once per launch (the partitions do not depend on the layer: chunk
+ * addresses of layer l are layer 0's plus l * layer_stride), so the producer
+ * walks it with a few multiplies per chunk. */
+struct Chunk {
+    const uint8_t *src;
+    uint32_t bytes, active;  /* copy size; consumer warps that take part */
+    bool state;              /* a state chunk (kept in L2 across tokens) */
+};
+struct Sched {
+    Wide qkvg, gu, lm;
+    Narrow o, down;
+    uint32_t h0, ab_rows, c0, ncols, cb;
+};
+struct Cursor {
+    int l;
+    uint32_t seg, k;
+};
+constexpr uint32_t kSegsPerLayer = 6;
+
+static_assert(sizeof(Sched) <= 256, "the schedule's shared-memory region holds 256 bytes");
+/* The CTA's schedule, built once per launch (gdn_decode_kernel's start) */
+__device__ __forceinline__ Sched *sm_sched() { return reinterpret_cast<Sched *>(smem_raw + kOffSched); }
+/* Lane 0 of consumer warps 0..5 each fill one part (the partitions' divisions
+ * run in parallel and once per launch, not in every phase's setup). */
+template <int MODE>
+__device__ __forceinline__ void build_sched(const DecodeParams &p, uint32_t cta, uint32_t ncta) {
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) != 0 || warp > 5) return;
+    Sched *s = sm_sched();
+    switch (warp) {
+    case 0: s->qkvg = wide_qkvg(p, 0, cta, ncta); break;
+    case 1: s->gu = wide_gu(p, 0, cta, ncta); break;
+    case 2: s->lm = wide_lm(p, cta, ncta); break;
+    case 3: s->o = narrow_o(p, 0, cta, ncta); break;
+    case 4: s->down = narrow_down(p, 0, cta, ncta); break;
+    default: {
+        const Span sc = span_of((uint32_t)p.nh * kHeadDim, cta, ncta);
+        s->h0 = sc.u0 >> 8;
+        s->ab_rows = 2u * (((sc.u1 - 1) >> 8) - s->h0 + 1);
+        s->c0 = sc.u0;
+        s->ncols = sc.u1 - sc.u0;
+        s->cb = state_col_bytes<MODE>();
+    }
+    }
+}
+__device__ __forceinline__ uint32_t wide_count(const Wide &w) { return w.passes() * w.chunks_per_pass(); }
+__device__ __forceinline__ Chunk wide_chunk(const Wide &w, size_t shift, uint32_t k) {
+    const uint32_t cpp = w.chunks_per_pass(), pass = k / cpp, j = k - pass * cpp;
+    const uint32_t pt0 = w.t0 + pass * w.P, n = min(w.P, w.t1 - pt0);
+    return Chunk{w.base + shift + ((size_t)j * w.T + pt0) * w.piece(), n * w.piece(), n * (w.TR / 8), false};
+}
+__device__ __forceinline__ Chunk narrow_chunk(const Narrow &w, size_t shift, uint32_t j) {
+    const uint32_t n = w.r1 - w.r0;
+    return Chunk{w.base + shift + w.off(j, w.r0), n * w.groups(j) * 128u, n, false};
+}
+/* Chunk c of the schedule, advancing c; false past the end. */
+__device__ __forceinline__ bool sched_next(const DecodeParams &p, const Sched &s, Cursor &c, Chunk &out) {
+    while (c.l <= p.L) {
+        const size_t shift = (size_t)c.l * p.layer_stride;
+        uint32_t count;
+        if (c.l == p.L) {
+            count = wide_count(s.lm);
+            if (c.k < count) { out = wide_chunk(s.lm, 0, c.k++); return true; }
+        } else {
+            switch (c.seg) {
+            case 0: count = wide_count(s.qkvg); if (c.k < count) { out = wide_chunk(s.qkvg, shift, c.k++); return true; } break;
+            case 1:
+                if (c.k == 0) {
+                    ++c.k;
+                    out = Chunk{layer_base(p, c.l) + p.off_ab + (size_t)2 * s.h0 * p.H * 2, s.ab_rows * p.H * 2,
+                                ab_warps(p, s.ab_rows), false};
+                    return true;
+                }
+                break;
+            case 2:
+                if (c.k == 0) {
+                    ++c.k;
+                    out = Chunk{reinterpret_cast<const uint8_t *>(p.S) + ((size_t)c.l * p.nh * kHeadDim + s.c0) * s.cb,
+                                s.ncols * s.cb, state_warps(s.ncols), true};
+                    return true;
+                }
+                break;
+            case 3: count = s.o.chunks(); if (c.k < count) { out = narrow_chunk(s.o, shift, c.k++); return true; } break;
+            case 4: count = wide_count(s.gu); if (c.k < count) { out = wide_chunk(s.gu, shift, c.k++); return true; } break;
+            default: count = s.down.chunks(); if (c.k < count) { out = narrow_chunk(s.down, shift, c.k++); return true; } break;
+            }
+        }
+        c.k = 0;
+        if (c.l == p.L || ++c.seg == kSegsPerLayer) { c.seg = 0; ++c.l; }
+    }
+    return false;
+}
+
+/* L2 lookahead of the producer, bytes per CTA: the chunks that follow the
+ * ones in the ring, up to this far ahead, are prefetched into L2 as the ring
+ * advances, so HBM keeps streaming while the consumers wait at a phase's
+ * exchange and the ring's copies then come from L2. */
+#ifndef GDN_PF_BYTES
+#define GDN_PF_BYTES 0
+#endif
+constexpr uint32_t kPrefetchBytes = GDN_PF_BYTES;
+
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+/* The producer warp: walks the CTA's schedule, one chunk per ring slot
+ * (lane 0 issues the copy); with a lookahead, lane 0 also prefetches the
+ * chunks up to kPrefetchBytes past the last one copied. */
 template <int MODE>
 __device__ void producer(const DecodeParams &p, uint32_t cta, uint32_t ncta) {
     const int lane = threadIdx.x & 31;
     const uint64_t pol_w = policy_evict_first(), pol_s = policy_evict_last();
-    constexpr uint32_t kStop = 0xffffffffu;
-    /* each helper takes the chunk counter by value and returns the next one
-     * (kStop on abort): a counter shared by reference would live in local
-     * memory */
-    auto wide = [&](const Wide &w, uint32_t q) -> uint32_t {
-        for (uint32_t pass = 0; pass < w.passes(); ++pass) {
-            const uint32_t pt0 = w.t0 + pass * w.P, n = min(w.P, w.t1 - pt0);
-            for (uint32_t j = 0; j < w.chunks_per_pass(); ++j, ++q) {
-                if (!claim_slot(p, q, n * (w.TR / 8), n * w.piece())) return kStop;
-                if (lane == 0)
-                    bulk_g2s(smem_u32(sm_slot(q % kSlots)), w.base + ((size_t)j * w.T + pt0) * w.piece(),
-                             n * w.piece(), smem_u32(&sm_full()[q % kSlots]), pol_w);
+    (void)cta;
+    (void)ncta;
+    const Sched s = *sm_sched();
+    Cursor d{0, 0, 0}, f{0, 0, 0};
+    uint64_t dbytes = 0, fbytes = 0;
+    Chunk ch, fc;
+    for (uint32_t q = 0; sched_next(p, s, d, ch); ++q) {
+        dbytes += ch.bytes;
+        if (kPrefetchBytes != 0 && lane == 0) {
+            /* chunks that start before dbytes are already in a copy */
+            while (fbytes < dbytes + kPrefetchBytes && sched_next(p, s, f, fc)) {
+                if (fbytes >= dbytes) prefetch_l2(fc.src, fc.bytes);
+                fbytes += fc.bytes;
             }
         }
-        return q;
-    };
-    auto narrow = [&](const Narrow &w, uint32_t q) -> uint32_t {
-        const uint32_t n = w.r1 - w.r0;
-        for (uint32_t j = 0; j < w.chunks(); ++j, ++q) {
-            const uint32_t bytes = n * w.groups(j) * 128u;
-            if (!claim_slot(p, q, n, bytes)) return kStop;
-            if (lane == 0)
-                bulk_g2s(smem_u32(sm_slot(q % kSlots)), w.base + w.off(j, w.r0), bytes,
-                         smem_u32(&sm_full()[q % kSlots]), pol_w);
-        }
-        return q;
-    };
-    const Span sc = span_of((uint32_t)p.nh * kHeadDim, cta, ncta);
-    const uint32_t h0 = sc.u0 >> 8, h1 = (sc.u1 - 1) >> 8;
-    const uint32_t ab_rows = 2u * (h1 - h0 + 1);
-    const uint32_t cb = state_col_bytes<MODE>();
-    uint32_t q = 0;
-    for (int l = 0; l < p.L; ++l) {
-        if ((q = wide(wide_qkvg(p, l, cta, ncta), q)) == kStop) return;
-        /* phase B: the a/b rows of the CTA's heads, then its state columns */
-        if (!claim_slot(p, q, ab_warps(p, ab_rows), ab_rows * p.H * 2)) return;
+        if (!claim_slot(p, q, ch.active, ch.bytes)) return;
         if (lane == 0)
-            bulk_g2s(smem_u32(sm_slot(q % kSlots)), layer_base(p, l) + p.off_ab + (size_t)2 * h0 * p.H * 2,
-                     ab_rows * p.H * 2, smem_u32(&sm_full()[q % kSlots]), pol_w);
-        ++q;
-        if (!claim_slot(p, q, state_warps(sc.u1 - sc.u0), (sc.u1 - sc.u0) * cb)) return;
-        if (lane == 0)
-            bulk_g2s(smem_u32(sm_slot(q % kSlots)),
-                     reinterpret_cast<const uint8_t *>(p.S) + ((size_t)l * p.nh * kHeadDim + sc.u0) * cb,
-                     (sc.u1 - sc.u0) * cb, smem_u32(&sm_full()[q % kSlots]), pol_s);
-        ++q;
-        if ((q = narrow(narrow_o(p, l, cta, ncta), q)) == kStop) return;
-        if ((q = wide(wide_gu(p, l, cta, ncta), q)) == kStop) return;
-        if ((q = narrow(narrow_down(p, l, cta, ncta), q)) == kStop) return;
+            bulk_g2s(smem_u32(sm_slot(q % kSlots)), ch.src, ch.bytes, smem_u32(&sm_full()[q % kSlots]),
+                     ch.state ? pol_s : pol_w);
     }
-    wide(wide_lm(p, cta, ncta), q);
 }
 
 /* ---------------------------------------------------- consumer GEMVs */
@@ -1023,40 +1117,30 @@ __device__ __forceinline__ float seq_sum(const float *a, int n) {
     }
     return sum;
 }
-/* Sequential sum, in index order from 0.0f, of n <= 128 values stored
- * transposed in shared memory (value h at a[(h % 32) * 4 + h / 32]): each
- * lane loads its four with one 16-byte load and the chain takes them from
- * the lanes by shuffles, which do not depend on the sum and so run ahead of
- * it. All 32 lanes call; every lane returns the sum. */
-__device__ __forceinline__ float seq_sum_warp(const float *a, int n) {
-    const int lane = threadIdx.x & 31;
-    const float4 v = reinterpret_cast<const float4 *>(a)[lane];
+/* Sequential sum, in index order from 0.0f, of the n floats at a (shared
+ * memory, 16-byte aligned). Every lane of the calling warp forms it and
+ * returns it. */
+__device__ __forceinline__ float seq_sum_bcast(const float *a, int n) {
+    /* every lane reads the same 16 bytes (one shared-memory wavefront): the
+     * shuffle unit, which all warps of the SM share, stays out of the chain */
+    const float4 *a4 = reinterpret_cast<const float4 *>(a);
     float sum = 0.0f;
-    /* four scalar passes (no indexed array: it would live in local memory) */
+    int k = 0;
+    for (; k + 8 <= (n >> 2); k += 8) {
+        float4 v[8];
 #pragma unroll
-    for (int k = 0; k < 32; ++k) {
-        const float x = __shfl_sync(0xffffffffu, v.x, k);
-        if (k < n) sum = __fadd_rn(sum, x);
-    }
+        for (int i = 0; i < 8; ++i) v[i] = a4[k + i];
 #pragma unroll
-    for (int k = 0; k < 32; ++k) {
-        const float x = __shfl_sync(0xffffffffu, v.y, k);
-        if (32 + k < n) sum = __fadd_rn(sum, x);
+        for (int i = 0; i < 8; ++i) {
+            sum = __fadd_rn(sum, v[i].x);
+            sum = __fadd_rn(sum, v[i].y);
+            sum = __fadd_rn(sum, v[i].z);
+            sum = __fadd_rn(sum, v[i].w);
+        }
     }
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-        const float x = __shfl_sync(0xffffffffu, v.z, k);
-        if (64 + k < n) sum = __fadd_rn(sum, x);
-    }
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-        const float x = __shfl_sync(0xffffffffu, v.w, k);
-        if (96 + k < n) sum = __fadd_rn(sum, x);
-    }
+    for (int i = 4 * k; i < n; ++i) sum = __fadd_rn(sum, a[i]);
     return sum;
 }
-/* position of half sum h in the transposed layout of seq_sum_warp */
-__device__ __forceinline__ int tpos(int h) { return ((h & 31) << 2) + (h >> 5); }
 
 /* Sum of squares of 16 consecutive floats, sequential from 0.0f. */
 __device__ __forceinline__ float sq16(const float *a) {
@@ -1111,12 +1195,12 @@ __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const xword *y
     for (int i = 0; i < kMaxPer; ++i)
         if (vec_elem(t, i) < p.H) sm_xres()[vec_elem(t, i)] = x[i];
     named_sync(1, kConsumerThreads);
-    if (t < halves) sm_red()[tpos(t)] = sq16(sm_xres() + 16 * t);
+    if (t < halves) sm_red()[t] = sq16(sm_xres() + 16 * t);
     named_sync(1, kConsumerThreads);
     if (t == 0) trace_put(p, pidx, 4);
     /* every warp forms the sum itself: no third barrier (and a single warp
      * doing it while the others wait at a barrier measured far slower) */
-    const float sum = seq_sum_warp(sm_red(), halves);
+    const float sum = seq_sum_bcast(sm_red(), halves);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum, (float)p.H), p.eps)));
     if (t == 0) trace_put(p, pidx, 6);
     bool fast = true;
@@ -1226,8 +1310,10 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int N>
 __device__ __forceinline__ void block_sum8(float (&v)[N], float *red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (warp < 8) {  /* the other warps' values are not part of the sums */
 #pragma unroll
-    for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
+        for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
+    }
     if (lane == 0 && warp < 8) {
 #pragma unroll
         for (int i = 0; i < N; ++i) red[warp * 8 + i] = v[i];
@@ -1310,7 +1396,7 @@ __device__ __noinline__ bool phase_state(const DecodeParams &p, int l, uint32_t 
                     s[i] = __fadd_rn(__fmul_rn(bf_lo(wv[i]), x[2 * i]), __fmul_rn(bf_hi(wv[i]), x[2 * i + 1]));
                 const float a0 = __fadd_rn(s[0], s[1]), a1 = __fadd_rn(s[2], s[3]);
                 const float a2 = __fadd_rn(s[4], s[5]), a3 = __fadd_rn(s[6], s[7]);
-                sm_park()[row * 128 + tpos((int)hf)] = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+                sm_park()[row * 128 + hf] = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
             }
             release(q);
         }
@@ -1319,7 +1405,7 @@ __device__ __noinline__ bool phase_state(const DecodeParams &p, int l, uint32_t 
     named_sync(1, kConsumerThreads);
     if ((uint32_t)warp < rows) {
         /* one sequential chain over the row's halves in column order */
-        const float acc = seq_sum_warp(sm_park() + warp * 128, (int)halves);
+        const float acc = seq_sum_bcast(sm_park() + warp * 128, (int)halves);
         /* row 2 hs: a of head h0 + hs, row 2 hs + 1: b */
         if (lane == 0) sm_hscal()[(warp >> 1) * 8 + 3 + (warp & 1)] = bnd<MODE>(acc);
     }
@@ -1506,6 +1592,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
         sm_exact()[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    build_sched<MODE>(p, cta, ncta);
     __syncthreads();
 
     if (warp == kProducerWarp) {
@@ -1517,7 +1604,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
         float best = -3.402823466e38f;
         int32_t best_i = 0x7fffffff;
         bool ok = true;
-        const Span sc = span_of((uint32_t)p.nh * kHeadDim, cta, ncta);
+        const Span sc{sm_sched()->c0, sm_sched()->c0 + sm_sched()->ncols};
         /* the layer and phase loops stay rolled: unrolled, every phase kind
          * gets its own copy of the chunk code and the kernel outgrows the
          * instruction caches */
@@ -1583,12 +1670,17 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                 if (t == 0) trace_put(p, pidx, 2);
                 /* the prologue is done with its norm weights: fetch the next ones */
                 if (ph == PH_QKVG) {
-                    prefetch_floats(sm_normw(), aux + p.H + kHeadDim, p.H);                  /* mlp_norm[l] */
+                    const Wide &g = sm_sched()->qkvg;
+                    prefetch_floats_idle(sm_normw(), aux + p.H + kHeadDim, p.H,
+                                         min(g.P, g.t1 - g.t0) * (g.TR / 8));                 /* mlp_norm[l] */
                 } else if (ph == PH_GU) {
-                    prefetch_floats(sm_normw(), l + 1 < p.L ? aux + p.aux_stride : p.aux + (size_t)p.L * p.aux_stride,
-                                    p.H);                                                     /* attn_norm[l+1] / final */
+                    const Wide &g = sm_sched()->gu;
+                    prefetch_floats_idle(sm_normw(),
+                                         l + 1 < p.L ? aux + p.aux_stride : p.aux + (size_t)p.L * p.aux_stride, p.H,
+                                         min(g.P, g.t1 - g.t0) * (g.TR / 8));                 /* attn_norm[l+1] / final */
                 } else if (ph == PH_O && l + 1 < p.L) {
-                    prefetch_floats(sm_onorm(), aux + p.aux_stride + p.H, kHeadDim);           /* o_norm[l+1] */
+                    prefetch_floats_idle(sm_onorm(), aux + p.aux_stride + p.H, kHeadDim,
+                                         sm_sched()->o.r1 - sm_sched()->o.r0);                /* o_norm[l+1] */
                 }
                 const bool exact = Mode<MODE>::kNative && (sm_exact()[xf] != 0 || p.force_exact != 0);
                 const bool drop = (int)cta == p.test_drop_cta && pidx == p.test_drop_phase;
@@ -1596,7 +1688,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     phase_state<MODE>(p, l, q, sc.u0, sc.u1, tag_base + PH_QKVG, tag_out, pidx);
                     q += 2;
                 } else if (ph == PH_O || ph == PH_DOWN) {
-                    const Narrow w = ph == PH_O ? narrow_o(p, l, cta, ncta) : narrow_down(p, l, cta, ncta);
+                    Narrow w = ph == PH_O ? sm_sched()->o : sm_sched()->down;
+                    w.base += (size_t)l * p.layer_stride;
                     const uint32_t q0 = q;
                     const float total = gemv_dispatch<MODE>(
                         exact, [&, q0](auto K) { return narrow_chunks<decltype(K)::value>(p, w, q0); });
@@ -1604,8 +1697,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     if (!drop && lane == 0 && (uint32_t)warp < w.r1 - w.r0)
                         xput<MODE>(p, ph == PH_O ? p.y_o : p.y_down, w.r0 + warp, bnd<MODE>(total), tag_out);
                 } else {
-                    const Wide w = ph == PH_QKVG ? wide_qkvg(p, l, cta, ncta)
-                                                 : ph == PH_GU ? wide_gu(p, l, cta, ncta) : wide_lm(p, cta, ncta);
+                    Wide w = ph == PH_QKVG ? sm_sched()->qkvg : ph == PH_GU ? sm_sched()->gu : sm_sched()->lm;
+                    if (ph != PH_LM) w.base += (size_t)l * p.layer_stride;
                     const uint32_t wpt = w.TR / 8, tw = (uint32_t)warp / wpt;
                     const uint32_t rr = ((uint32_t)warp % wpt) * 8u + ((uint32_t)lane >> 2);
                     const bool head = (lane & 3) == 0;
@@ -1618,8 +1711,10 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                          * chunk loop they would spill) */
                         float4 *tw_sh = reinterpret_cast<float4 *>(sm_scratch()) + 2 * (warp * 8 + (lane >> 2));
                         const bool conv_row = ph == PH_QKVG && active && head && row < 3u * p.H;
+                        /* q, k or v row (no division: a compare per kind) */
+                        const uint32_t kind = (uint32_t)(row >= (uint32_t)p.H) + (uint32_t)(row >= 2u * p.H);
+                        const uint32_t d = row - kind * (uint32_t)p.H;
                         if (conv_row) {
-                            const uint32_t kind = row / (uint32_t)p.H, d = row - kind * p.H;
                             cp_async16(smem_u32(tw_sh), p.tails + (((size_t)l * 3 + kind) * p.H + d) * 4);
                             cp_async16(smem_u32(tw_sh + 1), aux + 2 * p.H + kHeadDim + ((size_t)kind * p.H + d) * 4);
                             cp_async_commit();
@@ -1642,7 +1737,6 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                                               __fmul_rn(tail.z, cw.z)),
                                     __fmul_rn(raw, cw.w));
                                 xput<MODE>(p, p.qkv, row, silu_conv<MODE>(p, sum), tag_out);
-                                const uint32_t kind = row / (uint32_t)p.H, d = row - kind * p.H;
                                 __stcg(reinterpret_cast<float4 *>(p.tails + (((size_t)l * 3 + kind) * p.H + d) * 4),
                                        make_float4(tail.y, tail.z, raw, 0.0f));
                             } else {
