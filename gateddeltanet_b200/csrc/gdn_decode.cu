@@ -11,10 +11,11 @@
  *   - grid = one CTA per SM, launched cooperatively; each CTA owns a fixed
  *     slice of every phase's rows and of the recurrent state's columns;
  *   - warp 15 of every CTA is the producer: one lane walks the CTA's whole
- *     token schedule and streams each chunk (up to 20 KB) into a 9-slot
- *     shared-memory ring with cp.async.bulk copies (mbarrier completion,
- *     evict-first L2 policy for weights). Weights do not depend on
- *     activations, so it runs ahead across phase boundaries while the
+ *     token schedule (built once per launch in shared memory) and streams
+ *     each chunk (up to 28 KB) into a 4-slot shared-memory ring with one
+ *     cp.async.bulk copy per chunk (mbarrier completion, evict-first L2
+ *     policy for weights, evict-last for the state). Weights do not depend
+ *     on activations, so it runs ahead across phase boundaries while the
  *     consumers wait for inputs;
  *   - warps 0..14 consume every chunk together, each on its own rows, so a
  *     slot is held only while the CTA works on it. A chunk holds a column
@@ -29,7 +30,9 @@
  * state columns (gated delta rule), C O rows, D gate/up row pairs (SwiGLU),
  * E down rows; after the last layer the LM head. There is no grid barrier: a
  * phase's outputs travel as words that carry the phase's tag next to the
- * value, and each consumer CTA polls the words it needs. A CTA cannot run
+ * value (32-bit {BF16, 16-bit tag} words in the BF16-boundary contracts,
+ * 64-bit {FP32, 32-bit tag} in the FP32 one), and each consumer CTA polls the
+ * words it needs. A CTA cannot run
  * more than one phase ahead of any CTA it reads from, so exchange buffers are
  * reused every layer without write-after-read hazards; the residual stream
  * lives in each CTA's shared memory (every CTA computes it identically).

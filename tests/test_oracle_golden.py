@@ -96,3 +96,22 @@ def test_decode_matches_reference(full_oracle, case):
         assert top.tolist() == ref["top5_index"]
     assert sha(o.rec) == case["rec_sha256"]
     assert sha(o.conv) == case["conv_sha256"]
+
+
+def test_config0_trajectory_starts_as_the_zero_state_goldens():
+    """The 256-step config[0] digests (tests/golden/reference_config0_256.json,
+    checked against the GPU in tests/test_gpu_config0.py) come from the same
+    reference build, seed and token stream as the zero-state trajectory here:
+    their first steps must agree digest for digest, and the stream's tokens are
+    the seeded stream's."""
+    c0 = json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "reference_config0_256.json")))
+    zero = next(c for c in GOLD["decode"] if c["name"] == "zero_state")
+    assert (c0["seed"], c0["stream_seed"], c0["stream"], c0["state_seed"]) == \
+        (zero["seed"], zero["stream_seed"], zero["stream"], zero["state_seed"])
+    assert c0["steps"] == len(c0["steps_out"]) == 256
+    for i, ref in enumerate(zero["steps_out"]):
+        got = c0["steps_out"][i]
+        for key in ("token", "argmax", "logits_sha256", "hidden_sha256", "top5_index"):
+            assert got[key] == ref[key], (i, key)
+    from gateddeltanet_b200.workload import token_stream
+    assert [s["token"] for s in c0["steps_out"]] == token_stream(c0["stream"], 256, 32000, seed=c0["stream_seed"])
