@@ -10,14 +10,20 @@
  *   S'[k][v] = decay S[k][v] + k[k] delta[v]     (:2268-2300)
  *
  * S is stored as the decode engine keeps it, [v][k] (column v of the
- * reference's S[k][v] is 1 KB contiguous). One CTA per 64-column block of a
- * slice: the 64 columns are staged in shared memory by 1 KB bulk copies into
- * rows padded by 16 bytes (so a lane per column reads conflict-free), two
- * warps run the r chains and two the p chains, then all four update the block
- * and store it with coalesced 16-byte stores. S crosses HBM once each way;
- * three CTAs fit an SM, so one block's copy overlaps another's chains.
- * (Measured slower: a persistent CTA per SM with a three-block ring, fed by
- * bulk or by cp.async copies -- four warps per SM leave the chains exposed.)
+ * reference's S[k][v] is 1 KB contiguous). The step is a pipeline: one CTA
+ * per SM walks its contiguous range of 32-column blocks. A producer warp
+ * stages each block (one 1 KB bulk copy per column, into rows padded by 16
+ * bytes so that a lane per column reads without bank conflicts) with the
+ * slice's q and k into a 4-slot ring; two warps run the block's r and p
+ * chains (a lane per column); four warps load the block's scalars and v
+ * ahead, form alpha, delta and the outputs, then update the block and store
+ * it with coalesced 16-byte stores while the chain warps are already on the
+ * next block. S crosses HBM once each way. (Measured slower: one 32 KB copy
+ * per block with the chain lanes skewed against bank conflicts, eight 4 KB
+ * copies of padded four-column groups with two pairs of chain warps, six
+ * slots.)
+ * Every wait is bounded: a CTA whose copy does not land in 2 s records the
+ * error and leaves.
  */
 #include "gdn_engine.h"
 
@@ -28,157 +34,226 @@ namespace gdn {
 
 namespace {
 
-constexpr int kDK = 256, kDV = 256, kCols = 64, kBlocksPerSlice = kDV / kCols;
-constexpr int kThreadsDR = 128;
+constexpr int kDK = 256, kDV = 256;
+constexpr int kColsB = 32, kBlocksPerSlice = kDV / kColsB;  /* 32-column blocks */
+constexpr int kSlotsDR = 4;
+constexpr int kRowB = kDK + 4;                               /* padded column stride, floats (1040 bytes) */
+/* warps: 0 the r chains, 1 the p chains, 2..5 alpha / delta / update, 6 the producer */
+constexpr int kChainWarps = 2, kUpdWarps = 4, kUpdThreads = kUpdWarps * 32;
+constexpr int kThreadsDR = (kChainWarps + kUpdWarps + 1) * 32;
+constexpr int kProdWarpDR = kChainWarps + kUpdWarps;
+__host__ __device__ constexpr size_t col_off(int c) { return (size_t)c * kRowB * 4; }
 
-__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-/* shared memory: S block [64][256 + 4] | q [256] | k [256] | r [64] | p [64] | delta [64] | warp partials [4] */
-constexpr int kRow = kDK + 4;  /* padded column stride in floats (1040 bytes) */
-constexpr size_t kOffS = 0;
-constexpr size_t kOffQ = kOffS + (size_t)kCols * kRow * 4;
-constexpr size_t kOffK = kOffQ + kDK * 4;
-constexpr size_t kOffR = kOffK + kDK * 4;
-constexpr size_t kOffP = kOffR + kCols * 4;
-constexpr size_t kOffD = kOffP + kCols * 4;
-constexpr size_t kOffW = kOffD + kCols * 4;
-constexpr size_t kOffBar = (kOffW + 4 * 4 + 7) & ~(size_t)7;
-constexpr size_t kSmemDR = kOffBar + 8;
+/* slot: S block [32][260] | q [256] | k [256] | r [32] | p [32] | delta [32] | alpha partials [4] */
+constexpr size_t kSlotS = 0;
+constexpr size_t kSlotQ = kSlotS + (size_t)kColsB * kRowB * 4;
+constexpr size_t kSlotK = kSlotQ + kDK * 4;
+constexpr size_t kSlotR = kSlotK + kDK * 4;
+constexpr size_t kSlotP = kSlotR + kColsB * 4;
+constexpr size_t kSlotD = kSlotP + kColsB * 4;
+constexpr size_t kSlotW = kSlotD + kColsB * 4;
+constexpr size_t kSlotBytesDR = (kSlotW + 4 * 4 + 127) & ~(size_t)127;
+constexpr size_t kOffBarsDR = kSlotsDR * kSlotBytesDR;  /* full[4] | chains[4] | empty[4] | abort flag */
+constexpr size_t kSmemDR = kOffBarsDR + 3 * kSlotsDR * 8 + 16;
 constexpr uint64_t kWaitNsDR = 2000000000ull;
 
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ uint64_t now_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred q;\n mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2, %3;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(20000u)
+        : "memory");
+    return ok != 0;
+}
+/* Warp-wide wait for phase `parity` of a barrier (every lane observes the
+ * completion); false on abort, decided by lane 0 for the whole warp: the
+ * limit ran out here, or another warp raised the flag. */
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                               const DeltaRuleParams &p) {
+    const uint64_t t0 = now_ns();
+    bool done = mbar_test(bar, parity);
+    while (!__all_sync(0xffffffffu, done)) {
+        int stop = 0;
+        if ((threadIdx.x & 31) == 0) {
+            if (*abort_flag) {
+                stop = 1;
+            } else if (now_ns() - t0 > kWaitNsDR) {
+                *abort_flag = 1;
+                atomicExch(p.status, 1);
+                stop = 1;
+            }
+        }
+        if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+        if (!done) done = mbar_test(bar, parity);
+    }
+    return true;
+}
+__device__ __forceinline__ void mbar_arrive1(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+/* barrier of the update warps that also ORs a predicate over them */
+__device__ __forceinline__ bool upd_sync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n barrier.red.or.pred b, 1, %2, a;\n selp.u32 %0, 1, 0, b;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(kUpdThreads)
+        : "memory");
+    return r != 0;
+}
 
-__global__ void __launch_bounds__(kThreadsDR) delta_rule_kernel(const __grid_constant__ DeltaRuleParams p) {
+__global__ void __launch_bounds__(kThreadsDR, 1) delta_rule_kernel(const __grid_constant__ DeltaRuleParams p) {
     extern __shared__ __align__(128) uint8_t dsm[];
-    float *sb = reinterpret_cast<float *>(dsm + kOffS);
-    float *qs = reinterpret_cast<float *>(dsm + kOffQ);
-    float *ks = reinterpret_cast<float *>(dsm + kOffK);
-    float *rs = reinterpret_cast<float *>(dsm + kOffR);
-    float *ps = reinterpret_cast<float *>(dsm + kOffP);
-    float *ds = reinterpret_cast<float *>(dsm + kOffD);
-    float *ws = reinterpret_cast<float *>(dsm + kOffW);
-    uint64_t *bar = reinterpret_cast<uint64_t *>(dsm + kOffBar);
+    uint64_t *full = reinterpret_cast<uint64_t *>(dsm + kOffBarsDR);
+    uint64_t *chains = full + kSlotsDR, *empty = chains + kSlotsDR;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kSlotsDR);
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const uint32_t slice = blockIdx.x / kBlocksPerSlice, cb = blockIdx.x % kBlocksPerSlice;
-    /* the block: columns cb*64 .. cb*64+63 of the slice, 1 KB each */
-    float *S = p.S + (size_t)slice * kDK * kDV + (size_t)cb * kCols * kDK;
-
+    const uint32_t nb = p.slices * kBlocksPerSlice;
+    const uint32_t b0 = (uint32_t)(((uint64_t)blockIdx.x * nb) / gridDim.x);
+    const uint32_t b1 = (uint32_t)(((uint64_t)(blockIdx.x + 1) * nb) / gridDim.x);
     if (t == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)) : "memory");
+        for (int i = 0; i < kSlotsDR; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[i])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 2;" ::"r"(smem_addr(&chains[i])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(&empty[i])), "r"(kUpdWarps)
+                         : "memory");
+        }
+        *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (warp == 0) {
-        /* lane 0 posts the byte count, then every lane copies two columns */
-        if (lane == 0)
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-                         "r"((uint32_t)(kCols * kDK * 4))
-                         : "memory");
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < kCols / 32; ++j) {
-            const int c = lane + 32 * j;
+
+    if (warp == kProdWarpDR) {
+        /* producer: 32 column copies (a lane each) plus q and k per block */
+        for (uint32_t b = b0; b < b1; ++b) {
+            const uint32_t i = b - b0, slot = i % kSlotsDR, n = i / kSlotsDR;
+            uint8_t *sl = dsm + slot * kSlotBytesDR;
+            if (n > 0 && !mbar_wait_warp(smem_addr(&empty[slot]), (n - 1) & 1u, abort_flag, p)) return;
+            const uint32_t slice = b / kBlocksPerSlice, cb = b % kBlocksPerSlice;
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(&full[slot])),
+                             "r"((uint32_t)((kColsB + 2) * kDK * 4))
+                             : "memory");
+            __syncwarp();
+            /* a column (1 KB, into its padded row) per lane; lanes 0, 1 also q and k */
+            const float *src = p.S + ((size_t)slice * kDV + (size_t)cb * kColsB + lane) * kDK;
             asm volatile(
                 "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                    smem_addr(sb + (size_t)c * kRow)),
-                "l"(S + (size_t)c * kDK), "r"((uint32_t)(kDK * 4)), "r"(smem_addr(bar))
+                    smem_addr(sl + kSlotS + col_off(lane))),
+                "l"(src), "r"((uint32_t)(kDK * 4)), "r"(smem_addr(&full[slot]))
                 : "memory");
+            if (lane < 2)
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        smem_addr(sl + (lane == 0 ? kSlotQ : kSlotK))),
+                    "l"((lane == 0 ? p.q : p.k) + (size_t)slice * kDK), "r"((uint32_t)(kDK * 4)),
+                    "r"(smem_addr(&full[slot]))
+                    : "memory");
         }
+        return;
     }
-    /* q, k of the slice, and alpha = tree256(q (.) k): thread t holds elements
-     * 2t and 2t+1 (first tree level), the warp butterfly the next five, then
-     * (w0 + w1) + (w2 + w3) */
-    const float2 q2 = reinterpret_cast<const float2 *>(p.q + (size_t)slice * kDK)[t];
-    const float2 k2 = reinterpret_cast<const float2 *>(p.k + (size_t)slice * kDK)[t];
-    reinterpret_cast<float2 *>(qs)[t] = q2;
-    reinterpret_cast<float2 *>(ks)[t] = k2;
-    float a = __fadd_rn(__fmul_rn(q2.x, k2.x), __fmul_rn(q2.y, k2.y));
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-    if (lane == 0) ws[warp] = a;
-    __syncthreads();
-    const float alpha = __fadd_rn(__fadd_rn(ws[0], ws[1]), __fadd_rn(ws[2], ws[3]));
-
-    /* wait for the block; bounded: after the limit the CTA records the error
-     * and leaves (a bulk copy that has not landed in 2 s is not waited for
-     * any longer) */
-    {
-        const uint64_t t0 = now_ns();
-        uint32_t done = 0;
-        bool timed_out = false;
-        while (true) {
-            asm volatile(
-                "{\n .reg .pred q;\n mbarrier.try_wait.parity.shared::cta.b64 q, [%1], 0;\n selp.u32 %0, 1, 0, q;\n}\n"
-                : "=r"(done)
-                : "r"(smem_addr(bar))
-                : "memory");
-            if (done) break;
-            if (now_ns() - t0 > kWaitNsDR) {
-                timed_out = true;
-                break;
+    if (warp < kChainWarps) {
+        /* warp 0: r = S k, warp 1: p = S q; lane = column, sequential in k */
+        const bool is_r = warp == 0;
+        for (uint32_t b = b0; b < b1; ++b) {
+            const uint32_t i = b - b0, slot = i % kSlotsDR, n = i / kSlotsDR;
+            uint8_t *sl = dsm + slot * kSlotBytesDR;
+            if (!mbar_wait_warp(smem_addr(&full[slot]), n & 1u, abort_flag, p)) return;
+            const float4 *col = reinterpret_cast<const float4 *>(sl + kSlotS + col_off(lane));
+            const float4 *vec4 = reinterpret_cast<const float4 *>(sl + (is_r ? kSlotK : kSlotQ));
+            float acc = 0.0f;
+#pragma unroll 4
+            for (int k4 = 0; k4 < kDK / 4; ++k4) {
+                const float4 sv = col[k4], xv = vec4[k4];
+                acc = __fadd_rn(acc, __fmul_rn(sv.x, xv.x));
+                acc = __fadd_rn(acc, __fmul_rn(sv.y, xv.y));
+                acc = __fadd_rn(acc, __fmul_rn(sv.z, xv.z));
+                acc = __fadd_rn(acc, __fmul_rn(sv.w, xv.w));
             }
+            reinterpret_cast<float *>(sl + (is_r ? kSlotR : kSlotP))[lane] = acc;
+            __syncwarp();
+            if (lane == 0) mbar_arrive1(smem_addr(&chains[slot]));
         }
-        if (__syncthreads_or(timed_out)) {
-            if (t == 0) atomicExch(p.status, 1);
-            return;
-        }
+        return;
     }
-
-    /* read pass: warps 0-1 the r chains, warps 2-3 the p chains, lane = column */
-    {
-        const int c = t & (kCols - 1);
-        const float4 *col = reinterpret_cast<const float4 *>(sb + (size_t)c * kRow);
-        const float4 *vec4 = reinterpret_cast<const float4 *>((warp < 2) ? ks : qs);
-        float acc = 0.0f;
+    /* warps 2..5: alpha, delta, outputs and the update of every block */
+    const int u = t - kChainWarps * 32, uw = u >> 5;
+    for (uint32_t b = b0; b < b1; ++b) {
+        const uint32_t i = b - b0, slot = i % kSlotsDR, n = i / kSlotsDR;
+        uint8_t *sl = dsm + slot * kSlotBytesDR;
+        const uint32_t slice = b / kBlocksPerSlice, cb = b % kBlocksPerSlice;
+        const float *qs = reinterpret_cast<const float *>(sl + kSlotQ);
+        const float *ks = reinterpret_cast<const float *>(sl + kSlotK);
+        float *ws = reinterpret_cast<float *>(sl + kSlotW);
+        float *ds = reinterpret_cast<float *>(sl + kSlotD);
+        /* the block's scalars and v: loaded before the waits, so the round
+         * trip overlaps the copy and the chains */
+        const size_t vi = (size_t)slice * kDV + (size_t)cb * kColsB + (u & (kColsB - 1));
+        const float decay = __ldg(p.decay + slice), beta = __ldg(p.beta + slice), vv = __ldg(p.v + vi);
+        bool ok = mbar_wait_warp(smem_addr(&full[slot]), n & 1u, abort_flag, p);
+        if (upd_sync_or(!ok)) return;
+        /* alpha = tree256(q (.) k): thread u holds elements 2u and 2u+1 (the
+         * first level), the warp butterfly the next five, then
+         * (w0 + w1) + (w2 + w3) */
+        const float2 q2 = reinterpret_cast<const float2 *>(qs)[u], k2 = reinterpret_cast<const float2 *>(ks)[u];
+        float a = __fadd_rn(__fmul_rn(q2.x, k2.x), __fmul_rn(q2.y, k2.y));
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane == 0) ws[uw] = a;
+        ok = mbar_wait_warp(smem_addr(&chains[slot]), n & 1u, abort_flag, p);
+        if (upd_sync_or(!ok)) return;
+        const float alpha = __fadd_rn(__fadd_rn(ws[0], ws[1]), __fadd_rn(ws[2], ws[3]));
+        if (u < kColsB) {
+            const float r = reinterpret_cast<const float *>(sl + kSlotR)[u];
+            const float pp = reinterpret_cast<const float *>(sl + kSlotP)[u];
+            const float delta = __fmul_rn(beta, __fsub_rn(vv, __fmul_rn(decay, r)));
+            p.o[vi] = __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, pp), __fmul_rn(alpha, delta)));
+            ds[u] = delta;
+        }
+        upd_sync_or(false);
+        /* update and store: thread u its 16 bytes k = 4 (u & 63) .. +3 of
+         * columns (u >> 6) + 2 j -- 512-byte warp stores */
+        const int k4 = u & 63;
+        const float4 kk = reinterpret_cast<const float4 *>(ks)[k4];
+        float *S = p.S + ((size_t)slice * kDV + (size_t)cb * kColsB) * kDK;
 #pragma unroll 4
-        for (int k4 = 0; k4 < kDK / 4; ++k4) {
-            const float4 sv = col[k4], xv = vec4[k4];
-            acc = __fadd_rn(acc, __fmul_rn(sv.x, xv.x));
-            acc = __fadd_rn(acc, __fmul_rn(sv.y, xv.y));
-            acc = __fadd_rn(acc, __fmul_rn(sv.z, xv.z));
-            acc = __fadd_rn(acc, __fmul_rn(sv.w, xv.w));
+        for (int c = u >> 6; c < kColsB; c += kUpdThreads / 64) {
+            const float4 s4 = reinterpret_cast<const float4 *>(sl + kSlotS + col_off(c))[k4];
+            const float d = ds[c];
+            float4 n4;
+            n4.x = __fadd_rn(__fmul_rn(decay, s4.x), __fmul_rn(kk.x, d));
+            n4.y = __fadd_rn(__fmul_rn(decay, s4.y), __fmul_rn(kk.y, d));
+            n4.z = __fadd_rn(__fmul_rn(decay, s4.z), __fmul_rn(kk.z, d));
+            n4.w = __fadd_rn(__fmul_rn(decay, s4.w), __fmul_rn(kk.w, d));
+            __stcs(reinterpret_cast<float4 *>(S + (size_t)c * kDK) + k4, n4);
         }
-        ((warp < 2) ? rs : ps)[c] = acc;
-    }
-    __syncthreads();
-    const float decay = p.decay[slice], beta = p.beta[slice];
-    if (t < kCols) {
-        const size_t vi = (size_t)slice * kDV + (size_t)cb * kCols + t;
-        const float delta = __fmul_rn(beta, __fsub_rn(p.v[vi], __fmul_rn(decay, rs[t])));
-        p.o[vi] = __fmul_rn(0.0625f, __fadd_rn(__fmul_rn(decay, ps[t]), __fmul_rn(alpha, delta)));
-        ds[t] = delta;
-    }
-    __syncthreads();
-    /* update and store: thread t its 16 bytes k = 4 (t & 63) .. +3 of columns
-     * (t >> 6) + 2 i -- 512-byte warp stores */
-    const int k4 = t & 63;
-    const float4 kk = reinterpret_cast<const float4 *>(ks)[k4];
-#pragma unroll 4
-    for (int c = t >> 6; c < kCols; c += kThreadsDR / 64) {
-        const float4 s4 = reinterpret_cast<const float4 *>(sb + (size_t)c * kRow)[k4];
-        const float d = ds[c];
-        float4 n4;
-        n4.x = __fadd_rn(__fmul_rn(decay, s4.x), __fmul_rn(kk.x, d));
-        n4.y = __fadd_rn(__fmul_rn(decay, s4.y), __fmul_rn(kk.y, d));
-        n4.z = __fadd_rn(__fmul_rn(decay, s4.z), __fmul_rn(kk.z, d));
-        n4.w = __fadd_rn(__fmul_rn(decay, s4.w), __fmul_rn(kk.w, d));
-        __stcs(reinterpret_cast<float4 *>(S + (size_t)c * kDK) + k4, n4);
+        __syncwarp();
+        if (lane == 0) mbar_arrive1(smem_addr(&empty[slot]));
     }
 }
+
 
 }  // namespace
 
 size_t delta_rule_smem_bytes() { return kSmemDR; }
 
 cudaError_t launch_delta_rule(const DeltaRuleParams &p, cudaStream_t stream) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(delta_rule_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemDR);
+    cudaError_t e = cudaFuncSetAttribute(delta_rule_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemDR);
     if (e != cudaSuccess) return e;
-    delta_rule_kernel<<<p.slices * kBlocksPerSlice, kThreadsDR, kSmemDR, stream>>>(p);
+    int dev = 0, sms = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    /* one CTA per SM, at most one per block */
+    const uint32_t nb = p.slices * kBlocksPerSlice;
+    const uint32_t grid = (uint32_t)sms < nb ? (uint32_t)sms : nb;
+    delta_rule_kernel<<<grid, kThreadsDR, kSmemDR, stream>>>(p);
     return cudaGetLastError();
 }
 

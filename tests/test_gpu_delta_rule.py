@@ -55,9 +55,11 @@ def lib():
     return L
 
 
-@pytest.mark.parametrize("steps", [1, 3])
-def test_delta_rule_matches_oracle(lib, steps):
-    S, q, k, v, decay, beta = inputs(24, seed=11 + steps)
+@pytest.mark.parametrize("slices,steps", [(24, 1), (24, 3), (192, 2)])
+def test_delta_rule_matches_oracle(lib, slices, steps):
+    """24 slices: one or two 32-column blocks per CTA; 192 (config[1]'s 24 x 8):
+    ten or eleven per CTA, so the staging ring wraps around several times."""
+    S, q, k, v, decay, beta = inputs(slices, seed=11 + steps)
     # the engine keeps S as [v][k]; the oracle's per-head rule works on [k][v]
     S_gpu, o_gpu, ms = gdn.delta_rule_step(S.transpose(0, 2, 1), q, k, v, decay, beta, steps=steps)
     S_ref, o_ref = oracle_steps(S, q, k, v, decay, beta, steps)
