@@ -11,9 +11,9 @@ tokens, then exactly K timed tokens of the cyclic teacher-forced stream.
            CUDA events on the engine's stream, max over ranks. Weights
            (2.8 GB/token) exceed L2, so no flush is needed between steps.
   e2e      the same metric through the reference-facing C ABI,
-           gdn_decode_step_host per token: FP32 embedding row copied from
-           pinned host memory (8 KB H2D), kernel, token line + status read
-           back (192 B D2H), host wall clock.
+           gdn_decode_step_host per token: the token id as a kernel argument
+           (the kernel gathers its embedding row), the 128-byte status block
+           with the token line read back, host wall clock.
   roofline algorithmic bytes per token / measured time per token against
            MEASURED_PEAKS.json hbm_gbs.
   cpu_baseline  the CPU oracle port (multi-threaded restatement of the
@@ -713,8 +713,10 @@ def main():
                    "parallelism": f"tp{world}" if tp_mode else f"stream-dp{world}"},
         "inner_ms_per_token": round(ms_per_tok, 5),
         "outer_ms_per_token": round(e2e_ms, 5),
-        "e2e": {"value": round(e2e_value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * SHAPE["hidden"],
-                "d2h_bytes_per_step": 64 + 128, "api": "gdn_decode_step_host (C ABI), synchronous per token"},
+        "e2e": {"value": round(e2e_value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 128,
+                "api": "gdn_decode_step_host (C ABI), synchronous per token: the token id travels as a kernel "
+                       "argument, the 128-byte status block (token line + error word) comes back"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(),
                      "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg,

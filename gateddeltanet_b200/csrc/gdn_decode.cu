@@ -44,6 +44,7 @@
 #include "gdn_engine.h"
 #include "gdn_math.h"
 
+#include <atomic>
 #include <cuda_runtime.h>
 #include <type_traits>
 #include <stdint.h>
@@ -1175,8 +1176,9 @@ __device__ __noinline__ bool prologue_norm(const DecodeParams &p, const xword *y
     (void)w;
     cp_async_wait_all();  /* this thread's share of the weights; the barrier below publishes all shares */
     if (embed) {
-        if (p.token_src != nullptr) {
-            const uint16_t *e = p.emb + (size_t)(*p.token_src) * p.H;
+        if (p.token_src != nullptr || p.token_imm >= 0) {
+            const int32_t tok = p.token_src != nullptr ? *p.token_src : p.token_imm;
+            const uint16_t *e = p.emb + (size_t)tok * p.H;
 #pragma unroll
             for (int i = 0; i < kMaxPer; ++i)
                 if (vec_elem(t, i) < p.H) x[i] = bnd<MODE>(__uint_as_float((uint32_t)__ldg(e + vec_elem(t, i)) << 16));
@@ -1632,8 +1634,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                 switch (ph) {
                 case PH_QKVG:
                     if (l == 0) {
-                        if (p.token_src != nullptr) {
-                            const int32_t tok = *p.token_src;
+                        if (p.token_src != nullptr || p.token_imm >= 0) {
+                            const int32_t tok = p.token_src != nullptr ? *p.token_src : p.token_imm;
                             if (tok < 0 || tok >= p.V) {
                                 /* every consumer thread reads the same token: uniform exit */
                                 if (t == 0) raise_error(p, kErrBadToken, (uint32_t)tok);
@@ -1856,9 +1858,18 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
 template <int MODE>
 static cudaError_t launch_mode(const DecodeParams &p, int grid, cudaStream_t stream, size_t smem) {
     void *args[] = {const_cast<DecodeParams *>(&p)};
-    const cudaError_t e =
-        cudaFuncSetAttribute(gdn_decode_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    /* the shared-memory opt-in, once per device and size (it costs a driver
+     * call per launch otherwise) */
+    static std::atomic<size_t> smem_set[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    std::atomic<size_t> &done = smem_set[dev & 63];
+    if (dev >= 64 || done.load(std::memory_order_acquire) < smem) {
+        e = cudaFuncSetAttribute(gdn_decode_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) done.store(smem, std::memory_order_release);
+    }
     return cudaLaunchCooperativeKernel((const void *)gdn_decode_kernel<MODE>, dim3(grid), dim3(kThreads), args, smem,
                                        stream);
 }

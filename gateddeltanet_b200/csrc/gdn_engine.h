@@ -138,6 +138,7 @@ struct DecodeParams {
     float *logits, *hidden_out;
     const float *x_embed;      /* FP32 embedding row, used when token_src == nullptr */
     const int32_t *token_src;  /* device token id: gather the embedding row on device */
+    int32_t token_imm;         /* >= 0 (and token_src null): the token id itself, gathered the same way */
     float *cand_val;
     int32_t *cand_idx;
     int32_t *token_out;        /* optional: receives the step's argmax token */

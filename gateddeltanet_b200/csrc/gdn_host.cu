@@ -191,6 +191,8 @@ struct DeviceModel {
     uint32_t *exp_exc = nullptr;    /* the host library's expf exceptions, device copy */
     uint32_t exp_exc_n = 0;
     float fast_x_min = INFINITY;    /* DecodeParams.fast_x_min */
+    uint32_t exp_exc_bf16[gdn::kMaxExcBf16] = {};  /* the BF16-valued entries of exp_exc */
+    uint32_t exp_exc_bf16_n = 0;
     bool model_alive = true;
 };
 
@@ -428,6 +430,15 @@ DeviceModel *build_device_model(const GDNModel *model) {
     });
     const std::vector<uint32_t> &exc = host_exp_exceptions();
     dm->exp_exc_n = (uint32_t)exc.size();
+    for (uint32_t u : exc) {
+        if ((u & 0xffffu) != 0) continue;
+        if (dm->exp_exc_bf16_n == (uint32_t)gdn::kMaxExcBf16) {
+            fail("gdn_b200: the host library's exp has more than %d exceptions at BF16 inputs", gdn::kMaxExcBf16);
+            free_device_model(dm);
+            return nullptr;
+        }
+        dm->exp_exc_bf16[dm->exp_exc_bf16_n++] = u;
+    }
     float wmin = INFINITY;
     bool wbad = false;
     gemv_weight_range(model, &wmin, &wbad);
@@ -621,12 +632,8 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.decay_tab = dm.decay_tab;
     p.exp_exc = dm.exp_exc;
     p.exp_exc_n = dm.exp_exc_n;
-    {
-        /* the BF16-valued entries of the exception list (a handful) */
-        const std::vector<uint32_t> &exc = host_exp_exceptions();
-        for (uint32_t u : exc)
-            if ((u & 0xffffu) == 0 && p.exp_exc_bf16_n < (uint32_t)gdn::kMaxExcBf16) p.exp_exc_bf16[p.exp_exc_bf16_n++] = u;
-    }
+    p.exp_exc_bf16_n = dm.exp_exc_bf16_n;
+    for (uint32_t i = 0; i < dm.exp_exc_bf16_n; ++i) p.exp_exc_bf16[i] = dm.exp_exc_bf16[i];
     p.fast_x_min = dm.fast_x_min;
     p.force_exact = s.force_exact;
     p.S = s.S;
@@ -641,6 +648,7 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.hidden_out = s.hidden;
     p.x_embed = s.x_embed;
     p.token_src = nullptr;
+    p.token_imm = -1;
     p.cand_val = s.cand_val;
     p.cand_idx = s.cand_idx;
     p.token_out = nullptr;
@@ -1299,23 +1307,31 @@ int gdn_b200_test_drop_outputs(GDNRunState *state, int cta, int phase) {
 
 /* One step from the FP32 embedding row in workspace[X]: the body of the
  * reference's gdn_forward (c_impl/gdn_model.cpp:3719-3897). */
-static int forward_from_workspace(Stream &st) {
+static int forward_from_workspace(Stream &st, int32_t token = -1) {
     Stream *s = &st;
     const GDNWeightHeader &c = s->dm->cfg;
     const size_t H = c.hidden_size;
     CUDA_OK(cudaSetDevice(s->device));
     if (s->compat && s->host_dirty && compat_pull(*s) != 0) return -1;
-    CUDA_OK(cudaMemcpyAsync(s->x_embed, s->ws + GDN_WS_OFF_X, H * sizeof(float), cudaMemcpyHostToDevice, s->stream));
     gdn::DecodeParams p = make_params(*s);
+    if (token >= 0) {
+        /* workspace[X] holds that token's embedding row: the kernel gathers
+         * the same row from its own copy, given the id as an argument */
+        p.token_imm = token;
+    } else {
+        CUDA_OK(cudaMemcpyAsync(s->x_embed, s->ws + GDN_WS_OFF_X, H * sizeof(float), cudaMemcpyHostToDevice,
+                                s->stream));
+    }
     if (launch(*s, p) != 0) return -1;
-    /* token line -> workspace[X_NORM] (64 bytes, c_impl/host.cpp:1011-1017) */
-    CUDA_OK(cudaMemcpyAsync(s->ws + GDN_WS_OFF_X_NORM, s->status->token_line, 64, cudaMemcpyDeviceToHost, s->stream));
     if (g_debug_hidden != nullptr)
         CUDA_OK(cudaMemcpyAsync(g_debug_hidden, s->hidden, H * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
     if (g_debug_logits != nullptr)
         CUDA_OK(cudaMemcpyAsync(g_debug_logits, s->logits, c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost,
                                 s->stream));
+    /* the status block's read-back carries the token line: workspace[X_NORM]
+     * (64 bytes, c_impl/host.cpp:1011-1017) */
     const int rc = sync_and_check(*s);
+    memcpy(s->ws + GDN_WS_OFF_X_NORM, s->status_host->token_line, 64);
     if (rc != 0) return rc;
     return s->compat ? compat_push(*s) : 0;
 }
@@ -1328,7 +1344,7 @@ int gdn_decode_step_host(const GDNModel *model, GDNRunState *state, const int32_
     /* the host writes the FP32 embedding row into workspace[X]
      * (c_impl/gdn_model.cpp:3906-3908; c_impl/host.cpp:955-960) */
     memcpy(state->x, model->embeddings + (size_t)*token * H, H * sizeof(float));
-    return forward_from_workspace(*s);
+    return forward_from_workspace(*s, *token);
 }
 
 /* The SLR-partitioned C model of the reference computes the same step
