@@ -265,6 +265,11 @@ class RunState:
         c = model.config
         self.rec_floats = c.num_layers * c.num_heads * c.head_dim * c.head_dim
         self.conv_floats = c.num_layers * 3 * (c.conv_size - 1) * c.hidden_size
+        # per-step call objects, built once (step() is on the timed e2e path)
+        self._tok = ctypes.c_int32(0)
+        self._mref, self._sref, self._tref = ctypes.byref(model.m), ctypes.byref(self.s), ctypes.byref(self._tok)
+        self._step = self.lib.gdn_decode_step_host
+        self._ws = ctypes.cast(self.s.workspace, _FP)
 
     def workspace(self, offset: int, count: int) -> np.ndarray:
         ptr = ctypes.cast(self.s.workspace, _FP)
@@ -272,10 +277,11 @@ class RunState:
 
     def step(self, token: int) -> int:
         """gdn_decode_step_host; returns the kernel's greedy token (workspace[X_NORM] lane 0)."""
-        t = ctypes.c_int32(int(token))
-        check(self.lib.gdn_decode_step_host(ctypes.byref(self.model.m), ctypes.byref(self.s), ctypes.byref(t)),
-              "gdn_decode_step_host")
-        return int(self.workspace(GDN_WS_OFF_X_NORM, 1)[0])
+        t = self._tok
+        t.value = int(token)
+        if self._step(self._mref, self._sref, self._tref) != 0:
+            raise RuntimeError(f"gdn_decode_step_host failed: {last_error()}")
+        return int(self._ws[GDN_WS_OFF_X_NORM])
 
     def decode(self, tokens: Sequence[int], greedy: bool = False):
         """Device-resident loop; returns (argmax per step, device ms for all steps)."""
