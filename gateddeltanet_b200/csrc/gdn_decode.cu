@@ -946,22 +946,10 @@ __device__ __forceinline__ bool sched_next(const DecodeParams &p, const Sched &s
     return false;
 }
 
-/* L2 lookahead of the producer, bytes per CTA: the chunks that follow the
- * ones in the ring, up to this far ahead, are prefetched into L2 as the ring
- * advances, so HBM keeps streaming while the consumers wait at a phase's
- * exchange and the ring's copies then come from L2. */
-#ifndef GDN_PF_BYTES
-#define GDN_PF_BYTES 0
-#endif
-constexpr uint32_t kPrefetchBytes = GDN_PF_BYTES;
-
-__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 /* The producer warp: walks the CTA's schedule, one chunk per ring slot
- * (lane 0 issues the copy); with a lookahead, lane 0 also prefetches the
- * chunks up to kPrefetchBytes past the last one copied. */
+ * (lane 0 issues the copy). (Measured slower: prefetching the chunks past
+ * the ring into L2 with cp.async.bulk.prefetch.L2, continuously 128-512 KB
+ * ahead or only while the consumers wait for inputs.) */
 template <int MODE>
 __device__ void producer(const DecodeParams &p, uint32_t cta, uint32_t ncta) {
     const int lane = threadIdx.x & 31;
@@ -969,18 +957,9 @@ __device__ void producer(const DecodeParams &p, uint32_t cta, uint32_t ncta) {
     (void)cta;
     (void)ncta;
     const Sched s = *sm_sched();
-    Cursor d{0, 0, 0}, f{0, 0, 0};
-    uint64_t dbytes = 0, fbytes = 0;
-    Chunk ch, fc;
+    Cursor d{0, 0, 0};
+    Chunk ch;
     for (uint32_t q = 0; sched_next(p, s, d, ch); ++q) {
-        dbytes += ch.bytes;
-        if (kPrefetchBytes != 0 && lane == 0) {
-            /* chunks that start before dbytes are already in a copy */
-            while (fbytes < dbytes + kPrefetchBytes && sched_next(p, s, f, fc)) {
-                if (fbytes >= dbytes) prefetch_l2(fc.src, fc.bytes);
-                fbytes += fc.bytes;
-            }
-        }
         if (!claim_slot(p, q, ch.active, ch.bytes)) return;
         if (lane == 0)
             bulk_g2s(smem_u32(sm_slot(q % kSlots)), ch.src, ch.bytes, smem_u32(&sm_full()[q % kSlots]),
