@@ -12,7 +12,7 @@
  *     slice of every phase's rows and of the recurrent state's columns;
  *   - warp 15 of every CTA is the producer: one lane walks the CTA's whole
  *     token schedule (built once per launch in shared memory) and streams
- *     each chunk (up to 28 KB) into a 4-slot shared-memory ring with one
+ *     each chunk (up to 32 KB) into a 4-slot shared-memory ring with one
  *     cp.async.bulk copy per chunk (mbarrier completion, evict-first L2
  *     policy for weights, evict-last for the state). Weights do not depend
  *     on activations, so it runs ahead across phase boundaries while the
@@ -487,6 +487,7 @@ constexpr size_t kOffExpTab = kOffSched + 256;                           /* 128 
 constexpr size_t kOffNormW = kOffExpTab + 128 * 4;                       /* next RMSNorm weights, H floats */
 constexpr size_t kOffONorm = kOffNormW + kMaxHidden * 4;                 /* next output-norm weights, 256 */
 constexpr size_t kOffXs = kOffONorm + kHeadDim * 4;                      /* phase input */
+constexpr size_t kSplitBytes = 28672;  /* tensor-parallel launches: split GEMV tree16 values, after xs */
 
 extern __shared__ __align__(128) uint8_t smem_raw[];
 
@@ -527,6 +528,10 @@ __device__ __forceinline__ const float *exp_table() {
     return reinterpret_cast<const float *>(smem_raw + kOffExpTab);
 }
 __device__ __forceinline__ uint8_t *sm_xs() { return smem_raw + kOffXs; }
+__device__ __forceinline__ size_t xs_bytes(int H, int I) { return ((size_t)4 * (H > I ? H : I) + 15) & ~(size_t)15; }
+__device__ __forceinline__ float *sm_split(const DecodeParams &p) {
+    return reinterpret_cast<float *>(smem_raw + kOffXs + xs_bytes(p.H, p.I));
+}
 /* Norm weights, copied in (cp.async) right after their previous user's
  * prologue: a global load in a prologue costs a round trip through a memory
  * system saturated by the ring's copies */
@@ -548,7 +553,10 @@ __device__ __forceinline__ void prefetch_floats_idle(float *dst, const float *sr
     cp_async_commit();
 }
 
-size_t decode_smem_bytes(int H, int I) { return kOffXs + (size_t)4 * (H > I ? H : I); }
+size_t decode_smem_bytes(int H, int I, bool tp) {
+    const size_t xs = ((size_t)4 * (H > I ? H : I) + 15) & ~(size_t)15;
+    return kOffXs + xs + (tp ? kSplitBytes : 0);
+}
 
 /* Phase input x in shared memory, element e: BF16 (2 bytes) in the
  * BF16-boundary contracts, FP32 in the FP32 control; per 64-column group g,
@@ -759,15 +767,29 @@ __device__ __forceinline__ Span span_of(uint32_t total, uint32_t cta, uint32_t n
 /* A tiled (wide) projection: T tiles of TR rows, G 64-column groups per
  * chunk, at most P tiles (one warp per 8 rows, at most kSlotBytes) per pass.
  * Stored column-chunk-major, so the chunk of tiles [a, b) is one copy. */
+/* Parts a tiled GEMV pass of `units` 8-row units splits into: 1 (each
+ * unit's warp works every group) unless splitting is on and the units leave
+ * at least half of the consumer warps idle; then part k of a unit forms the
+ * tree16 values of the unit's groups g with g % parts == k into shared
+ * memory, and the unit's own warp adds them in group order. `items`: groups
+ * per row; `bytes`: the values' size per unit. (The O / DOWN rows are not
+ * split: a warp's share of a row is a few hundred cycles, less than the
+ * split's two barriers and chain.) */
+__device__ __forceinline__ uint32_t split_parts(uint32_t on, uint32_t units, uint32_t items, uint32_t bytes) {
+    if (!on || units == 0 || 2u * units > (uint32_t)kConsumerWarps || units * bytes > kSplitBytes) return 1u;
+    return min((uint32_t)kConsumerWarps / units, items);
+}
 struct Wide {
     const uint8_t *base;
     uint32_t TR, G, P, K, T, t0, t1;
     __device__ __forceinline__ uint32_t passes() const { return (t1 - t0 + P - 1) / P; }
     __device__ __forceinline__ uint32_t chunks_per_pass() const { return K / 64 / G; }
     __device__ __forceinline__ uint32_t piece() const { return G * TR * 128; }  /* one tile's share of a chunk */
+    /* parts of a pass of n tiles (on: DecodeParams.split) */
+    __device__ __forceinline__ uint32_t parts(uint32_t on, uint32_t n) const {
+        return split_parts(on, n * (TR / 8), K / 64, K / 64 * 128);
+    }
 };
-/* tiles per pass: at most one warp per 8 rows and kSlotBytes per chunk */
-constexpr uint32_t kPassQKVG = 7, kPassGU = 7, kPassLM = 7;
 /* A narrow projection of R rows: rows [r0, r1), kNarrowGroups groups per
  * chunk (the last chunk may have fewer); stored column-chunk-major, so a
  * chunk of the rows is one copy. */
@@ -780,25 +802,37 @@ struct Narrow {
     __device__ __forceinline__ size_t off(uint32_t j, uint32_t r) const {
         return ((size_t)j * kNarrowGroups * R + (size_t)r * groups(j)) * 128u;
     }
+    /* the same in a tensor-parallel image of NG groups per chunk (DecodeParams.ng_narrow) */
+    __device__ __forceinline__ uint32_t chunks_ng(uint32_t NG) const { return (K / 64 + NG - 1) / NG; }
+    __device__ __forceinline__ uint32_t groups_ng(uint32_t NG, uint32_t j) const { return min(NG, K / 64 - j * NG); }
+    __device__ __forceinline__ size_t off_ng(uint32_t NG, uint32_t j, uint32_t r) const {
+        return ((size_t)j * NG * R + (size_t)r * groups_ng(NG, j)) * 128u;
+    }
 };
 
 __device__ __forceinline__ const uint8_t *layer_base(const DecodeParams &p, int l) {
     return p.wimg + (size_t)l * p.layer_stride;
 }
+/* TP: a tensor-parallel launch, whose image has the groups per chunk of
+ * DecodeParams (g_qkvg, g_gu, g_lm, ng_narrow) */
+template <bool TP>
 __device__ __forceinline__ Wide wide_qkvg(const DecodeParams &p, int l, uint32_t cta, uint32_t ncta) {
     const uint32_t T = 4u * p.H / kTileRowsQKVG;
     const Span s = span_of(T, cta, ncta);
-    return Wide{layer_base(p, l), kTileRowsQKVG, kGroupsQKVG, kPassQKVG, (uint32_t)p.H, T, s.u0, s.u1};
+    return Wide{layer_base(p, l), kTileRowsQKVG, TP ? p.g_qkvg : kGroupsQKVG, kPassTiles, (uint32_t)p.H, T, s.u0, s.u1};
 }
+template <bool TP>
 __device__ __forceinline__ Wide wide_gu(const DecodeParams &p, int l, uint32_t cta, uint32_t ncta) {
     const uint32_t T = 2u * p.I / kTileRowsGU;
     const Span s = span_of(T, cta, ncta);
-    return Wide{layer_base(p, l) + p.off_gu, kTileRowsGU, kGroupsGU, kPassGU, (uint32_t)p.H, T, s.u0, s.u1};
+    return Wide{layer_base(p, l) + p.off_gu, kTileRowsGU, TP ? p.g_gu : kGroupsGU, kPassTiles, (uint32_t)p.H, T, s.u0,
+                s.u1};
 }
+template <bool TP>
 __device__ __forceinline__ Wide wide_lm(const DecodeParams &p, uint32_t cta, uint32_t ncta) {
     const uint32_t T = (uint32_t)p.V / kTileRowsLM;
     const Span s = span_of(T, cta, ncta);
-    return Wide{p.w_lm, kTileRowsLM, kGroupsLM, kPassLM, (uint32_t)p.H, T, s.u0, s.u1};
+    return Wide{p.w_lm, kTileRowsLM, TP ? p.g_lm : kGroupsLM, kPassTiles, (uint32_t)p.H, T, s.u0, s.u1};
 }
 __device__ __forceinline__ Narrow narrow_o(const DecodeParams &p, int l, uint32_t cta, uint32_t ncta) {
     const Span s = span_of((uint32_t)p.H, cta, ncta);
@@ -883,9 +917,9 @@ __device__ __forceinline__ void build_sched(const DecodeParams &p, uint32_t cta,
     if ((threadIdx.x & 31) != 0 || warp > 5) return;
     Sched *s = sm_sched();
     switch (warp) {
-    case 0: s->qkvg = wide_qkvg(p, 0, cta, ncta); break;
-    case 1: s->gu = wide_gu(p, 0, cta, ncta); break;
-    case 2: s->lm = wide_lm(p, cta, ncta); break;
+    case 0: s->qkvg = wide_qkvg<Mode<MODE>::kTp>(p, 0, cta, ncta); break;
+    case 1: s->gu = wide_gu<Mode<MODE>::kTp>(p, 0, cta, ncta); break;
+    case 2: s->lm = wide_lm<Mode<MODE>::kTp>(p, cta, ncta); break;
     case 3: s->o = narrow_o(p, 0, cta, ncta); break;
     case 4: s->down = narrow_down(p, 0, cta, ncta); break;
     default: {
@@ -899,26 +933,39 @@ __device__ __forceinline__ void build_sched(const DecodeParams &p, uint32_t cta,
     }
 }
 __device__ __forceinline__ uint32_t wide_count(const Wide &w) { return w.passes() * w.chunks_per_pass(); }
-__device__ __forceinline__ Chunk wide_chunk(const Wide &w, size_t shift, uint32_t k) {
+template <bool TP>
+__device__ __forceinline__ Chunk wide_chunk(const DecodeParams &p, const Wide &w, size_t shift, uint32_t k) {
     const uint32_t cpp = w.chunks_per_pass(), pass = k / cpp, j = k - pass * cpp;
     const uint32_t pt0 = w.t0 + pass * w.P, n = min(w.P, w.t1 - pt0);
+    if (TP) {
+        const uint32_t sf = w.parts(p.split, n);
+        /* the chunk's G consecutive groups fall to min(G, sf) parts */
+        return Chunk{w.base + shift + ((size_t)j * w.T + pt0) * w.piece(), n * w.piece(),
+                     n * (w.TR / 8) * (sf > 1 ? min(w.G, sf) : 1u), false};
+    }
     return Chunk{w.base + shift + ((size_t)j * w.T + pt0) * w.piece(), n * w.piece(), n * (w.TR / 8), false};
 }
-__device__ __forceinline__ Chunk narrow_chunk(const Narrow &w, size_t shift, uint32_t j) {
+template <bool TP>
+__device__ __forceinline__ Chunk narrow_chunk(const DecodeParams &p, const Narrow &w, size_t shift, uint32_t j) {
     const uint32_t n = w.r1 - w.r0;
+    if (TP) {
+        const uint32_t NG = p.ng_narrow;
+        return Chunk{w.base + shift + w.off_ng(NG, j, w.r0), n * w.groups_ng(NG, j) * 128u, n, false};
+    }
     return Chunk{w.base + shift + w.off(j, w.r0), n * w.groups(j) * 128u, n, false};
 }
 /* Chunk c of the schedule, advancing c; false past the end. */
+template <bool TP>
 __device__ __forceinline__ bool sched_next(const DecodeParams &p, const Sched &s, Cursor &c, Chunk &out) {
     while (c.l <= p.L) {
         const size_t shift = (size_t)c.l * p.layer_stride;
         uint32_t count;
         if (c.l == p.L) {
             count = wide_count(s.lm);
-            if (c.k < count) { out = wide_chunk(s.lm, 0, c.k++); return true; }
+            if (c.k < count) { out = wide_chunk<TP>(p, s.lm, 0, c.k++); return true; }
         } else {
             switch (c.seg) {
-            case 0: count = wide_count(s.qkvg); if (c.k < count) { out = wide_chunk(s.qkvg, shift, c.k++); return true; } break;
+            case 0: count = wide_count(s.qkvg); if (c.k < count) { out = wide_chunk<TP>(p, s.qkvg, shift, c.k++); return true; } break;
             case 1:
                 if (c.k == 0) {
                     ++c.k;
@@ -935,9 +982,9 @@ __device__ __forceinline__ bool sched_next(const DecodeParams &p, const Sched &s
                     return true;
                 }
                 break;
-            case 3: count = s.o.chunks(); if (c.k < count) { out = narrow_chunk(s.o, shift, c.k++); return true; } break;
-            case 4: count = wide_count(s.gu); if (c.k < count) { out = wide_chunk(s.gu, shift, c.k++); return true; } break;
-            default: count = s.down.chunks(); if (c.k < count) { out = narrow_chunk(s.down, shift, c.k++); return true; } break;
+            case 3: count = TP ? s.o.chunks_ng(p.ng_narrow) : s.o.chunks(); if (c.k < count) { out = narrow_chunk<TP>(p, s.o, shift, c.k++); return true; } break;
+            case 4: count = wide_count(s.gu); if (c.k < count) { out = wide_chunk<TP>(p, s.gu, shift, c.k++); return true; } break;
+            default: count = TP ? s.down.chunks_ng(p.ng_narrow) : s.down.chunks(); if (c.k < count) { out = narrow_chunk<TP>(p, s.down, shift, c.k++); return true; } break;
             }
         }
         c.k = 0;
@@ -959,7 +1006,7 @@ __device__ void producer(const DecodeParams &p, uint32_t cta, uint32_t ncta) {
     const Sched s = *sm_sched();
     Cursor d{0, 0, 0};
     Chunk ch;
-    for (uint32_t q = 0; sched_next(p, s, d, ch); ++q) {
+    for (uint32_t q = 0; sched_next<Mode<MODE>::kTp>(p, s, d, ch); ++q) {
         if (!claim_slot(p, q, ch.active, ch.bytes)) return;
         if (lane == 0)
             bulk_g2s(smem_u32(sm_slot(q % kSlots)), ch.src, ch.bytes, smem_u32(&sm_full()[q % kSlots]),
@@ -1002,8 +1049,80 @@ __device__ __forceinline__ float tree16_at(const uint8_t *wrow, uint32_t wsw, ui
 constexpr uint32_t kPair = 1;  /* chunks taken together by a warp (2 measured slower: fewer slots in flight) */
 constexpr uint32_t kMaxG = 4;   /* groups per chunk of a tiled projection, at most */
 
+/* A pass of a tiled projection split into sf parts (every consumer warp
+ * calls it): warp (unit u = warp % units, part k = warp / units) forms the
+ * tree16 values of the groups g % sf == k of unit u's rows into shared
+ * memory, then unit u's own warp (k == 0, the warp that owns the rows
+ * unsplit) adds them in group order -- the same chain as wide_chunks. */
 template <int KIND>
+__device__ __forceinline__ float wide_split(const DecodeParams &p, const Wide &w, uint32_t n, uint32_t q, uint32_t sf) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t wpt = w.TR / 8, units = n * wpt, unit = warp % units, part = warp / units;
+    const uint32_t tw = unit / wpt, rr = (unit % wpt) * 8u + (lane >> 2), b = lane & 3u;
+    const uint32_t ng = w.K / 64;
+    float *vals = sm_split(p) + unit * ng * 32u + lane;
+    named_sync(1, kConsumerThreads); /* the previous split's chain reads are done */
+    if (part < sf) {
+        const uint32_t cpp = w.chunks_per_pass();
+        for (uint32_t j = 0; j < cpp; ++j) {
+            const uint32_t ga = j * w.G, g1 = ga + w.G;
+            const uint32_t gf = ga + (part + sf - ga % sf) % sf; /* the part's first group of the chunk */
+            if (gf >= g1) continue;
+            if (!wait_full(p, q + j)) continue;
+            const uint8_t *tile = sm_slot((q + j) % kSlots) + tw * w.piece() + rr * 128u;
+            for (uint32_t g = gf; g < g1; g += sf) vals[g * 32u] = tree16_at<KIND>(tile + (g - ga) * w.TR * 128u, rr & 7u, g, b);
+            release(q + j);
+        }
+    }
+    named_sync(1, kConsumerThreads);
+    float acc = 0.0f;
+    if (warp < units) {
+#pragma unroll 8
+        for (uint32_t g = 0; g < ng; ++g) acc = __fadd_rn(acc, vals[g * 32u]);
+    }
+    const float t = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+    return __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 2));
+}
+
+/* The same for the tensor-parallel images: any G, in blocks of kMaxG groups
+ * (the chain in group order). */
+template <int KIND>
+__device__ __forceinline__ float wide_chunks_any(const DecodeParams &p, const Wide &w, uint32_t n, uint32_t q) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t wpt = w.TR / 8;
+    const uint32_t tw = (uint32_t)warp / wpt;
+    const uint32_t rr = ((uint32_t)warp % wpt) * 8u + ((uint32_t)lane >> 2), b = (uint32_t)lane & 3u;
+    float acc = 0.0f;
+    if (tw < n) {
+        const uint32_t cpp = w.chunks_per_pass();
+        for (uint32_t j = 0; j < cpp; ++j, ++q) {
+            if (!wait_full(p, q)) continue;
+            const uint8_t *tile = sm_slot(q % kSlots) + tw * w.piece() + rr * 128u;
+            for (uint32_t gb = 0; gb < w.G; gb += kMaxG) {
+                float t[kMaxG];
+#pragma unroll
+                for (uint32_t gi = 0; gi < kMaxG; ++gi)
+                    t[gi] = gb + gi < w.G ? tree16_at<KIND>(tile + (gb + gi) * w.TR * 128u, rr & 7u, j * w.G + gb + gi, b)
+                                          : 0.0f;
+#pragma unroll
+                for (uint32_t gi = 0; gi < kMaxG; ++gi)
+                    if (gb + gi < w.G) acc = __fadd_rn(acc, t[gi]);
+            }
+            release(q);
+        }
+    }
+    const float t = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));
+    return __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 2));
+}
+
+/* TP: a tensor-parallel launch (the image's geometry; split when the pass
+ * leaves warps idle). */
+template <int KIND, bool TP>
 __device__ __forceinline__ float wide_chunks(const DecodeParams &p, const Wide &w, uint32_t n, uint32_t q) {
+    if (TP) {
+        const uint32_t sf = w.parts(p.split, n);
+        return sf > 1 ? wide_split<KIND>(p, w, n, q, sf) : wide_chunks_any<KIND>(p, w, n, q);
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t wpt = w.TR / 8;
     const uint32_t tw = (uint32_t)warp / wpt;
@@ -1038,13 +1157,42 @@ __device__ __forceinline__ float wide_chunks(const DecodeParams &p, const Wide &
     return __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 2));
 }
 
+/* The same for the tensor-parallel images: chunks of any multiple of 8
+ * groups, in blocks of 8 (lane (b, s): group 8 m + s). */
+template <int KIND>
+__device__ __forceinline__ float narrow_chunks_any(const DecodeParams &p, const Narrow &w, uint32_t q) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t b = (uint32_t)lane >> 3, s = (uint32_t)lane & 7u;
+    float acc = 0.0f;
+    if ((uint32_t)warp < w.r1 - w.r0) {
+        const uint32_t NG = p.ng_narrow, nc = w.chunks_ng(NG);
+        for (uint32_t j = 0; j < nc; ++j, ++q) {
+            const uint32_t ng = w.groups_ng(NG, j);
+            if (!wait_full(p, q)) continue;
+            const uint8_t *row = sm_slot(q % kSlots) + warp * ng * 128u;
+            const uint32_t g0 = j * NG;
+            for (uint32_t gb = 0; gb < ng; gb += 8) {
+                const uint32_t g = g0 + gb + s;
+                const float t0 = tree16_at<KIND>(row + (gb + s) * 128u, g & 7u, g, b);
+                acc = __fadd_rn(acc, t0);
+#pragma unroll
+                for (int k = 1; k < 8; ++k) acc = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, t0, k));
+            }
+            release(q);
+        }
+    }
+    const float t = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8));
+    return __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 16));
+}
+
 /* A narrow projection: warp w owns row r0 + w; lane (b = lane / 8, s = lane
  * % 8) computes the tree16 of bank b of groups s and s + 8 of a chunk, and
  * lane (b, 0) adds a chunk's values in group order to the bank's chain
  * (gathered by warp shuffles). Returns (b0 + b1) + (b2 + b3) in lane 0 of
  * active warps. */
-template <int KIND>
+template <int KIND, bool TP>
 __device__ __forceinline__ float narrow_chunks(const DecodeParams &p, const Narrow &w, uint32_t q) {
+    if (TP) return narrow_chunks_any<KIND>(p, w, q);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t b = (uint32_t)lane >> 3, s = (uint32_t)lane & 7u;
     float acc = 0.0f;
@@ -1676,8 +1824,8 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                     w.base += (size_t)l * p.layer_stride;
                     const uint32_t q0 = q;
                     const float total = gemv_dispatch<MODE>(
-                        exact, [&, q0](auto K) { return narrow_chunks<decltype(K)::value>(p, w, q0); });
-                    q += w.chunks();
+                        exact, [&, q0](auto K) { return narrow_chunks<decltype(K)::value, Mode<MODE>::kTp>(p, w, q0); });
+                    q += Mode<MODE>::kTp ? w.chunks_ng(p.ng_narrow) : w.chunks();
                     if (!drop && lane == 0 && (uint32_t)warp < w.r1 - w.r0)
                         xput<MODE>(p, ph == PH_O ? p.y_o : p.y_down, w.r0 + warp, bnd<MODE>(total), tag_out);
                 } else {
@@ -1705,7 +1853,7 @@ __global__ void __launch_bounds__(kThreads, 1) gdn_decode_kernel(const __grid_co
                         }
                         const uint32_t q0 = q;
                         const float total = gemv_dispatch<MODE>(
-                            exact, [&, q0](auto K) { return wide_chunks<decltype(K)::value>(p, w, n, q0); });
+                            exact, [&, q0](auto K) { return wide_chunks<decltype(K)::value, Mode<MODE>::kTp>(p, w, n, q0); });
                         q += w.chunks_per_pass();
                         const float up = __shfl_down_sync(0xffffffffu, total, 4);
                         if (!active || !head || drop) continue;
@@ -1857,7 +2005,7 @@ static cudaError_t launch_mode(const DecodeParams &p, int grid, cudaStream_t str
  * (BF16 boundaries, exact products, FP32 state), c_impl (BF16 boundaries,
  * BF16-rounded products, BF16 state); tensor-parallel forms of each. */
 cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t stream) {
-    const size_t smem = decode_smem_bytes(p.H, p.I);
+    const size_t smem = decode_smem_bytes(p.H, p.I, p.tp_world > 1);
     const bool fp32 = !p.bf16_boundary && !p.native_product && !p.bf16_state;
     const bool engine = p.bf16_boundary && !p.native_product && !p.bf16_state;
     const bool cimpl = p.bf16_boundary && p.native_product && p.bf16_state;

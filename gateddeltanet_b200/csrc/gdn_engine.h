@@ -60,16 +60,22 @@ constexpr int kConsumerWarps = 15;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kProducerWarp = kConsumerWarps;      /* the last warp issues the ring's copies */
 constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kSlotBytes = 28672;
-constexpr int kSlots = 4;  /* 4 x 28 KB in flight per SM: more queues the latency-critical exchange traffic behind the weight stream (measured 6 slots 1.26, 5 1.23, 4 1.18, 3 1.23 ms/token) */
+/* 4 slots in flight per SM: more queues the latency-critical exchange
+ * traffic behind the weight stream (measured with 28 KB slots: 6 slots 1.26,
+ * 5 1.23, 4 1.18, 3 1.23 ms/token). The one-GPU image's chunks are 28 KB;
+ * 32 KB slots let a tensor-parallel CTA of four 8-row tiles take a whole
+ * QKVG phase in 4 chunks. */
+constexpr int kSlotBytes = 32768;
+constexpr int kSlots = 4;
 constexpr int kPhasesPerLayer = 5;
 constexpr int kTraceSlots = 8;
-constexpr int kNarrowGroups = 16;    /* 64-column groups per chunk of O / DOWN (the last may have fewer) */
+constexpr int kNarrowGroups = 16;    /* 64-column groups per chunk of O / DOWN in the one-GPU image (the last may have fewer) */
 constexpr int kMaxNarrowRows = kConsumerWarps;  /* O / DOWN rows per CTA: one per consumer warp */
 constexpr int kMaxStateCols = kConsumerWarps;   /* state columns per CTA: one per consumer warp */
 constexpr int kTileRowsQKVG = 8, kGroupsQKVG = 4;
 constexpr int kTileRowsGU = 16, kGroupsGU = 2;
 constexpr int kTileRowsLM = 16, kGroupsLM = 2;
+constexpr uint32_t kPassTiles = 7;   /* tiles of a tiled projection per pass (one warp per 8 rows of QKVG; 28 KB chunks in the one-GPU image) */
 constexpr int kMaxExcBf16 = 8;       /* BF16-valued entries of the exp exception list, copied into the parameters */
 
 /* error codes written to DecodeStatus.err */
@@ -129,6 +135,13 @@ struct DecodeParams {
      * finite). Phases whose input fails the test use the exact emulation. */
     float fast_x_min;
     int force_exact;           /* test hook: always use the exact emulation */
+    /* chunk geometry of the weight image (wimg, w_lm): 64-column groups per
+     * chunk of the QKVG, gate/up and LM-head tiles, and of the O / DOWN rows
+     * (a multiple of 8) */
+    uint32_t g_qkvg, g_gu, g_lm, ng_narrow;
+    /* 1: a tiled GEMV pass whose tiles leave at least half of the consumer
+     * warps idle spreads its groups over them (tensor-parallel launches) */
+    uint32_t split;
     /* stream state */
     void *S;
     float *tails;
@@ -184,7 +197,7 @@ cudaError_t launch_delta_rule(const DeltaRuleParams &p, cudaStream_t stream);
 /* Tags one launch consumes; the host advances DecodeParams.epoch by this. */
 inline uint32_t epoch_stride(int L) { return (uint32_t)(L * kPhasesPerLayer + 1); }
 
-size_t decode_smem_bytes(int H, int I);
+size_t decode_smem_bytes(int H, int I, bool tp);  /* tp: a tensor-parallel launch (adds the split GEMV values) */
 cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t stream);
 /* acc[0] += log_softmax(logits)[*target] (double), acc[1] += 1 (gdn_score.cu) */
 cudaError_t launch_score(const float *logits, uint32_t V, const int32_t *target, double *acc, cudaStream_t stream);

@@ -176,6 +176,15 @@ int engine_grid_ok(const GDNWeightHeader &c, int ncta, bool report = true) {
 
 /* ------------------------------------------------- device weight image */
 
+/* Chunk geometry of a weight image: 64-column groups per chunk of the tiled
+ * projections and of the O / DOWN rows (the defaults: the one-GPU image). */
+struct ImageGeom {
+    uint32_t g_qkvg = gdn::kGroupsQKVG, g_gu = gdn::kGroupsGU, g_lm = gdn::kGroupsLM, ng = gdn::kNarrowGroups;
+    bool operator==(const ImageGeom &o) const {
+        return g_qkvg == o.g_qkvg && g_gu == o.g_gu && g_lm == o.g_lm && ng == o.ng;
+    }
+};
+
 struct DeviceModel {
     int device = 0;
     int refs = 0;
@@ -194,6 +203,13 @@ struct DeviceModel {
     uint32_t exp_exc_bf16[gdn::kMaxExcBf16] = {};  /* the BF16-valued entries of exp_exc */
     uint32_t exp_exc_bf16_n = 0;
     bool model_alive = true;
+    /* the same weights in the chunk geometries of tensor-parallel grids
+     * (built from wimg / w_lm on first use, guarded by g_mu) */
+    struct Image {
+        ImageGeom g;
+        uint8_t *wimg, *w_lm;
+    };
+    std::vector<Image> images;
 };
 
 std::mutex g_mu;
@@ -206,7 +222,7 @@ inline uint16_t hi16(float v) { return (uint16_t)(f2u(v) >> 16); }
  * groups][TR rows][64]; row-major: element i of [K/512 column chunks][R
  * rows][8 groups][64]. In both, the 16-byte pieces of a 128-byte group are
  * permuted (by the row in tiles, by the group otherwise). */
-inline void tiled_src(size_t i, size_t TR, size_t G, size_t rows, size_t *row, size_t *col) {
+__host__ __device__ inline void tiled_src(size_t i, size_t TR, size_t G, size_t rows, size_t *row, size_t *col) {
     const size_t T = rows / TR, chunk = T * G * TR * 64;
     const size_t j = i / chunk, rem = i % chunk;
     const size_t t = rem / (G * TR * 64), rem2 = rem % (G * TR * 64);
@@ -214,13 +230,48 @@ inline void tiled_src(size_t i, size_t TR, size_t G, size_t rows, size_t *row, s
     *row = t * TR + r;
     *col = (j * G + gi) * 64 + (((c >> 3) ^ (r & 7)) << 3) + (c & 7);
 }
-inline void rowmajor_src(size_t i, size_t rows, size_t K, size_t *row, size_t *col) {
-    const size_t NG = gdn::kNarrowGroups, groups = K / 64;
+/* NG: groups per column chunk (gdn::kNarrowGroups in the one-GPU image) */
+__host__ __device__ inline void rowmajor_src(size_t i, size_t rows, size_t K, size_t NG, size_t *row, size_t *col) {
+    const size_t groups = K / 64;
     const size_t j = i / (rows * NG * 64), rem = i - j * rows * NG * 64;
-    const size_t ng = std::min(NG, groups - j * NG);
+    const size_t ng = groups - j * NG < NG ? groups - j * NG : NG;
     const size_t cc = rem % (ng * 64), g = j * NG + cc / 64, c = cc % 64;
     *row = rem / (ng * 64);
     *col = g * 64 + (((c >> 3) ^ (g & 7)) << 3) + (c & 7);
+}
+/* The inverses: image position of natural (row, col). */
+__host__ __device__ inline size_t tiled_pos(size_t row, size_t col, size_t TR, size_t G, size_t rows) {
+    const size_t T = rows / TR, t = row / TR, r = row % TR, gg = col / 64, j = gg / G, gi = gg % G, ci = col % 64;
+    const size_t c = (((ci >> 3) ^ (r & 7)) << 3) | (ci & 7);
+    return ((j * T + t) * G + gi) * TR * 64 + r * 64 + c;
+}
+__host__ __device__ inline size_t rowmajor_pos(size_t row, size_t col, size_t rows, size_t K, size_t NG) {
+    const size_t groups = K / 64, g = col / 64, j = g / NG, ci = col % 64;
+    const size_t ng = groups - j * NG < NG ? groups - j * NG : NG;
+    const size_t c = (((ci >> 3) ^ (g & 7)) << 3) | (ci & 7);
+    return j * rows * NG * 64 + row * ng * 64 + (g - j * NG) * 64 + c;
+}
+
+/* The geometry for `ncta` CTAs (all GPUs of a tensor-parallel launch): the
+ * fewest chunks per phase whose largest copy still fits a ring slot. A
+ * tiled projection of T tiles gives a CTA at most ceil(T / ncta) tiles (at
+ * most kPassTiles of them per pass), an O / DOWN row set ceil(H / ncta)
+ * rows. */
+ImageGeom image_geometry(const GDNWeightHeader &c, uint32_t ncta) {
+    const uint32_t H = c.hidden_size, I = c.intermediate_size;
+    auto wide = [&](uint32_t T, uint32_t TR) {
+        const uint32_t n = std::min(gdn::kPassTiles, (T + ncta - 1) / ncta);
+        uint32_t G = 1;
+        while ((H / 64) % (2 * G) == 0 && n * 2 * G * TR * 128 <= (uint32_t)gdn::kSlotBytes) G *= 2;
+        return G;
+    };
+    ImageGeom g;
+    g.g_qkvg = wide(4 * H / gdn::kTileRowsQKVG, gdn::kTileRowsQKVG);
+    g.g_gu = wide(2 * I / gdn::kTileRowsGU, gdn::kTileRowsGU);
+    g.g_lm = wide(c.vocab_size / gdn::kTileRowsLM, gdn::kTileRowsLM);
+    const uint32_t rows = (H + ncta - 1) / ncta;
+    g.ng = std::min<uint32_t>((uint32_t)gdn::kSlotBytes / (rows * 128) / 8 * 8, std::max(H, I) / 64);
+    return g;
 }
 
 /* The reference's scalar functions with the host C library
@@ -263,6 +314,10 @@ void free_device_model(DeviceModel *dm) {
     cudaSetDevice(dm->device);
     cudaFree(dm->wimg);
     cudaFree(dm->w_lm);
+    for (auto &im : dm->images) {
+        cudaFree(im.wimg);
+        cudaFree(im.w_lm);
+    }
     cudaFree(dm->emb);
     cudaFree(dm->aux);
     cudaFree(dm->exp_table);
@@ -368,13 +423,13 @@ DeviceModel *build_device_model(const GDNModel *model) {
                     r = j / H;
                     src = ((r & 1) ? w.b_proj : w.a_proj) + (r >> 1) * H + j % H;
                 } else if (i < dm->off_gu / 2) {
-                    rowmajor_src(i - dm->off_o / 2, H, H, &r, &col);
+                    rowmajor_src(i - dm->off_o / 2, H, H, gdn::kNarrowGroups, &r, &col);
                     src = w.o_proj + r * H + col;
                 } else if (i < dm->off_down / 2) {
                     tiled_src(i - dm->off_gu / 2, gdn::kTileRowsGU, gdn::kGroupsGU, 2 * I, &r, &col);
                     src = ((r & 1) ? w.mlp_up_proj : w.mlp_gate_proj) + (r >> 1) * H + col;
                 } else {
-                    rowmajor_src(i - dm->off_down / 2, H, I, &r, &col);
+                    rowmajor_src(i - dm->off_down / 2, H, I, gdn::kNarrowGroups, &r, &col);
                     src = w.mlp_down_proj + r * I + col;
                 }
                 st[so + (i - b)] = hi16(*src);
@@ -458,6 +513,77 @@ DeviceModel *build_device_model(const GDNModel *model) {
     return dm;
 }
 
+/* Piece i (8 BF16 values, consecutive columns in every geometry) of a
+ * projection in groups-per-chunk `gd`, gathered from its copy in `gs`;
+ * kind 0 tiled (TR-row tiles), 1 row-major O / DOWN rows. */
+__global__ void reimage_kernel(uint4 *dst, const uint4 *src, size_t pieces, int kind, uint32_t TR, uint32_t gs,
+                               uint32_t gd, size_t rows, size_t K) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < pieces; i += (size_t)gridDim.x * blockDim.x) {
+        size_t r, c, j;
+        if (kind == 0) {
+            tiled_src(i * 8, TR, gd, rows, &r, &c);
+            j = tiled_pos(r, c, TR, gs, rows);
+        } else {
+            rowmajor_src(i * 8, rows, K, gd, &r, &c);
+            j = rowmajor_pos(r, c, rows, K, gs);
+        }
+        dst[i] = src[j / 8];
+    }
+}
+
+/* The weight image (QKVG ... DOWN of every layer, and the LM head) in
+ * geometry g: the one-GPU image itself for the default geometry, else a copy
+ * re-laid on the device from it on first use and kept with the model. */
+int device_image(DeviceModel *dm, const ImageGeom &g, cudaStream_t st, uint8_t **wimg, uint8_t **w_lm) {
+    if (g == ImageGeom()) {
+        *wimg = dm->wimg;
+        *w_lm = dm->w_lm;
+        return 0;
+    }
+    std::lock_guard<std::mutex> lock(g_mu);
+    for (const auto &im : dm->images)
+        if (im.g == g) {
+            *wimg = im.wimg;
+            *w_lm = im.w_lm;
+            return 0;
+        }
+    const GDNWeightHeader &c = dm->cfg;
+    const size_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size, L = c.num_layers;
+    DeviceModel::Image im{g, nullptr, nullptr};
+    if (cudaMalloc(&im.wimg, dm->layer_stride * L) != cudaSuccess || cudaMalloc(&im.w_lm, V * H * 2) != cudaSuccess) {
+        cudaFree(im.wimg);
+        return fail("gdn_b200: tensor-parallel weight image allocation failed (%.2f GB)",
+                    (double)(dm->layer_stride * L + V * H * 2) / 1e9);
+    }
+    auto run = [&](uint8_t *dst, const uint8_t *src, size_t elems, int kind, uint32_t TR, uint32_t gs, uint32_t gd,
+                   size_t rows, size_t K) {
+        reimage_kernel<<<1184, 256, 0, st>>>(reinterpret_cast<uint4 *>(dst), reinterpret_cast<const uint4 *>(src),
+                                             elems / 8, kind, TR, gs, gd, rows, K);
+    };
+    for (size_t l = 0; l < L; ++l) {
+        uint8_t *d = im.wimg + l * dm->layer_stride;
+        const uint8_t *s0 = dm->wimg + l * dm->layer_stride;
+        run(d, s0, 4 * H * H, 0, gdn::kTileRowsQKVG, gdn::kGroupsQKVG, g.g_qkvg, 4 * H, H);
+        cudaMemcpyAsync(d + dm->off_ab, s0 + dm->off_ab, dm->off_o - dm->off_ab, cudaMemcpyDeviceToDevice, st);
+        run(d + dm->off_o, s0 + dm->off_o, H * H, 1, 0, gdn::kNarrowGroups, g.ng, H, H);
+        run(d + dm->off_gu, s0 + dm->off_gu, 2 * I * H, 0, gdn::kTileRowsGU, gdn::kGroupsGU, g.g_gu, 2 * I, H);
+        run(d + dm->off_down, s0 + dm->off_down, H * I, 1, 0, gdn::kNarrowGroups, g.ng, H, I);
+    }
+    run(im.w_lm, dm->w_lm, V * H, 0, gdn::kTileRowsLM, gdn::kGroupsLM, g.g_lm, V, H);
+    const cudaError_t e = cudaStreamSynchronize(st);
+    const cudaError_t e2 = cudaGetLastError();
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+        cudaFree(im.wimg);
+        cudaFree(im.w_lm);
+        return fail("gdn_b200: building the tensor-parallel weight image failed: %s",
+                    cudaGetErrorString(e != cudaSuccess ? e : e2));
+    }
+    dm->images.push_back(im);
+    *wimg = im.wimg;
+    *w_lm = im.w_lm;
+    return 0;
+}
+
 /* ------------------------------------------------------- decode streams */
 
 struct Stream {
@@ -497,6 +623,9 @@ struct Stream {
      * regions mapped into this process */
     int tp_world = 1, tp_rank = 0;
     int tp_grid = 0;      /* CTAs per GPU while attached: every phase must keep a unit for each CTA of all GPUs */
+    /* the weight image of the attached grid's chunk geometry */
+    ImageGeom tp_geom;
+    uint8_t *tp_wimg = nullptr, *tp_lm = nullptr;
     /* the state holds one rank's part since a tensor-parallel step (until a
      * full upload); part_* is the attachment that step ran under */
     bool tp_part = false;
@@ -618,13 +747,20 @@ gdn::DecodeParams make_params(const Stream &s) {
     p.bf16_boundary = s.bf16_boundary;
     p.native_product = s.native_product;
     p.bf16_state = s.bf16_state;
-    p.wimg = dm.wimg;
+    const bool tp = s.tp_world > 1;
+    p.wimg = tp ? s.tp_wimg : dm.wimg;
+    p.w_lm = tp ? s.tp_lm : dm.w_lm;
+    const ImageGeom geom = tp ? s.tp_geom : ImageGeom();
+    p.g_qkvg = geom.g_qkvg;
+    p.g_gu = geom.g_gu;
+    p.g_lm = geom.g_lm;
+    p.ng_narrow = geom.ng;
+    p.split = tp ? 1u : 0u;
     p.layer_stride = dm.layer_stride;
     p.off_ab = dm.off_ab;
     p.off_o = dm.off_o;
     p.off_gu = dm.off_gu;
     p.off_down = dm.off_down;
-    p.w_lm = dm.w_lm;
     p.emb = dm.emb;
     p.aux = dm.aux;
     p.aux_stride = dm.aux_stride;
@@ -1116,6 +1252,8 @@ static void tp_close(Stream &s) {
     }
     s.tp_world = 1;
     s.tp_rank = 0;
+    s.tp_geom = ImageGeom();
+    s.tp_wimg = s.tp_lm = nullptr;
 }
 
 static int tp_token_of(Stream &s, TpToken &t) {
@@ -1178,6 +1316,12 @@ int gdn_b200_tp_attach(GDNRunState *state, int rank, int world, const void *toke
         tp_close(*s);
         return fail("gdn_b200_tp_attach: no grid fits %d GPUs for this model", world);
     }
+    const ImageGeom geom = image_geometry(s->dm->cfg, (uint32_t)(world * g));
+    if (device_image(s->dm, geom, s->stream, &s->tp_wimg, &s->tp_lm) != 0) {
+        tp_close(*s);
+        return -1;
+    }
+    s->tp_geom = geom;
     s->tp_grid = g;
     s->tp_world = world;
     s->tp_rank = rank;
