@@ -499,6 +499,8 @@ def tp_record(model, teacher, args, world, rank, barrier):
     ms = max_over_ranks(ms, device="cuda")
     logits, _ = rs.outputs()
     rec, conv, grid, _, _ = rs.read_state_part()
+    # one traced step on every rank at once (after the checked values are read)
+    phases = phase_medians(rs.trace(toks[0]), dims["layers"])
     rs.tp_detach()
     barrier()
     rs.free()
@@ -529,9 +531,30 @@ def tp_record(model, teacher, args, world, rank, barrier):
                              "teacher-forced tokens",
                  "exchange": "row-split partitions over all GPUs' CTAs; every output stored into every GPU's "
                              "exchange region by peer stores over NVLink (no NCCL call on the data path)",
-                 "timing": "CUDA events on each rank's stream, max over ranks"}
+                 "timing": "CUDA events on each rank's stream, max over ranks",
+                 "phases_us": phases,
+                 "phases_note": "one traced step after the timed ones, %globaltimer stamps: medians over rank 0's "
+                                "CTAs and layers 1..L-2 of [arrive, input built, chunk work, total] per phase "
+                                "(A QKVG, B state, C O, D gate/up, E down; LM head)"}
     barrier()
     return rec_d
+
+
+def phase_medians(tr, layers: int) -> dict:
+    """Per-phase medians, us, of a gdn_b200_trace_step stamp array [cta,
+    phase, slot] over the CTAs that ran and layers 1..layers-2: slot 1 - 0
+    (inputs arrived), 2 - 1 (input built), 3 - 2 (chunk work), 3 - 0."""
+    import numpy as np
+    tr = tr.astype(np.int64)
+    tr = tr[tr[:, 0, 3] != 0]
+    out = {}
+
+    def med(t):
+        return [round(float(np.median(t[..., a] - t[..., b])) / 1e3, 2) for a, b in ((1, 0), (2, 1), (3, 2), (3, 0))]
+    for k, name in enumerate("ABCDE"):
+        out[name] = med(tr[:, [l * 5 + k for l in range(1, layers - 1)], :])
+    out["LM"] = med(tr[:, layers * 5, :])
+    return out
 
 
 def streams_record(model, args, world, rank, barrier, per_gpu: int = 64, steps: int = 32, warmup: int = 4):
