@@ -138,6 +138,8 @@ EXPORTS = [
     ("gdn_b200_test_drop_outputs", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int, ctypes.c_int]),
     ("gdn_b200_test_force_exact_products", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_int]),
     ("gdn_b200_test_set_epoch", ctypes.c_int, [ctypes.POINTER(GDNRunState), ctypes.c_uint32]),
+    ("gdn_b200_test_image_geometry", ctypes.c_int, [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                                     ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
     ("gdn_b200_grid_size", ctypes.c_int, []),
     ("gdn_b200_batch_create", ctypes.c_void_p, [ctypes.POINTER(GDNModel), ctypes.c_uint32]),
     ("gdn_b200_batch_free", None, [ctypes.c_void_p]),

@@ -1438,6 +1438,62 @@ int gdn_b200_test_set_epoch(GDNRunState *state, uint32_t epoch) {
     return 0;
 }
 
+namespace {
+/* Pieces (8 values) of a projection: the image map of piece i lands in range
+ * at a piece boundary and its inverse gives i back, so the map is a
+ * bijection of the projection's pieces. */
+bool tiled_map_ok(size_t TR, size_t G, size_t rows, size_t K) {
+    std::atomic<bool> ok{true};
+    parallel_for(rows * K / 8, [&](size_t b, size_t e) {
+        for (size_t i = b; i < e && ok.load(std::memory_order_relaxed); ++i) {
+            size_t r, c;
+            tiled_src(i * 8, TR, G, rows, &r, &c);
+            if (r >= rows || c >= K || c % 8 != 0 || tiled_pos(r, c, TR, G, rows) != i * 8) ok = false;
+        }
+    });
+    return ok;
+}
+bool rowmajor_map_ok(size_t rows, size_t K, size_t NG) {
+    std::atomic<bool> ok{true};
+    parallel_for(rows * K / 8, [&](size_t b, size_t e) {
+        for (size_t i = b; i < e && ok.load(std::memory_order_relaxed); ++i) {
+            size_t r, c;
+            rowmajor_src(i * 8, rows, K, NG, &r, &c);
+            if (r >= rows || c >= K || c % 8 != 0 || rowmajor_pos(r, c, rows, K, NG) != i * 8) ok = false;
+        }
+    });
+    return ok;
+}
+}  // namespace
+
+int gdn_b200_test_image_geometry(uint32_t hidden, uint32_t intermediate, uint32_t vocab, uint32_t ncta,
+                                 uint32_t *geom, int check_maps) {
+    if (geom == nullptr || ncta == 0) return fail("gdn_b200_test_image_geometry: null geometry or no CTAs");
+    if (hidden == 0 || intermediate == 0 || hidden % 512 || intermediate % 512 || vocab == 0 || vocab % 16)
+        return fail("gdn_b200_test_image_geometry: hidden and intermediate must be multiples of 512, vocab of 16");
+    GDNWeightHeader c;
+    memset(&c, 0, sizeof(c));
+    c.hidden_size = hidden;
+    c.intermediate_size = intermediate;
+    c.vocab_size = vocab;
+    const ImageGeom g = image_geometry(c, ncta);
+    geom[0] = g.g_qkvg;
+    geom[1] = g.g_gu;
+    geom[2] = g.g_lm;
+    geom[3] = g.ng;
+    if (check_maps) {
+        const size_t H = hidden, I = intermediate, V = vocab;
+        for (const ImageGeom &m : {g, ImageGeom()}) {
+            if (!tiled_map_ok(gdn::kTileRowsQKVG, m.g_qkvg, 4 * H, H) || !tiled_map_ok(gdn::kTileRowsGU, m.g_gu, 2 * I, H) ||
+                !tiled_map_ok(gdn::kTileRowsLM, m.g_lm, V, H) || !rowmajor_map_ok(H, H, m.ng) ||
+                !rowmajor_map_ok(H, I, m.ng))
+                return fail("gdn_b200_test_image_geometry: a layout map of geometry (%u, %u, %u, %u) is not a bijection",
+                            m.g_qkvg, m.g_gu, m.g_lm, m.ng);
+        }
+    }
+    return 0;
+}
+
 int gdn_b200_test_drop_outputs(GDNRunState *state, int cta, int phase) {
     Stream *s = find_stream(state);
     if (s == nullptr) return fail("gdn_b200: unknown run state");

@@ -61,6 +61,32 @@ def tp_grid(dims: dict, world: int, grid: int) -> int:
     return min(grid, min(phase_units(dims).values()) // world)
 
 
+SLOT_BYTES = 32768  # one slot of the decode kernel's 4-slot shared-memory ring
+PASS_TILES = 7      # tiles of a tiled projection per pass
+
+
+def image_geometry(dims: dict, ncta: int) -> tuple[int, int, int, int]:
+    """Chunk geometry of the weight image gdn_b200_tp_attach builds for
+    `ncta` CTAs over all GPUs: (groups of 64 columns per chunk of the QKVG,
+    gate/up and LM-head tiles, groups per chunk of the O / DOWN rows). Each
+    is the largest whose biggest copy -- a CTA's ceil(units / ncta) tiles
+    (at most PASS_TILES a pass) or rows -- still fits a ring slot; the tiled
+    counts are powers of two dividing hidden / 64, the row count a multiple
+    of 8. At one GPU's 148 CTAs this is the one-GPU image (4, 2, 2, 16)."""
+    H, I, V = dims["hidden"], dims["inter"], dims["vocab"]
+
+    def wide(tiles: int, tile_rows: int) -> int:
+        n = min(PASS_TILES, -(-tiles // ncta))
+        g = 1
+        while (H // 64) % (2 * g) == 0 and n * 2 * g * tile_rows * 128 <= SLOT_BYTES:
+            g *= 2
+        return g
+    rows = -(-H // ncta)
+    ng = min(SLOT_BYTES // (rows * 128) // 8 * 8, max(H, I) // 64)
+    return (wide(4 * H // QKVG_TILE_ROWS, QKVG_TILE_ROWS), wide(2 * I // GU_TILE_ROWS, GU_TILE_ROWS),
+            wide(V // LM_TILE_ROWS, LM_TILE_ROWS), ng)
+
+
 def owner_maps(dims: dict, grid: int, world: int):
     """(col_rank [heads][256], ch_rank [3][hidden]): the rank that updates
     recurrent-state column v of head h, and the conv-tail channel of row d of

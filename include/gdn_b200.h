@@ -149,6 +149,17 @@ int gdn_b200_test_force_exact_products(GDNRunState *state, int on);
  * that was never written since the exchange buffers were last refilled. */
 int gdn_b200_test_set_epoch(GDNRunState *state, uint32_t epoch);
 
+/* Test hook (no counterpart in the reference; host only, no GPU needed): the
+ * chunk geometry gdn_b200_tp_attach gives the weight image of a model of
+ * these sizes for `ncta` CTAs over all GPUs -- geom[0..3] = 64-column groups
+ * per chunk of the QKVG, gate/up and LM-head tiles and of the O / DOWN rows
+ * (4, 2, 2, 16 is the one-GPU image). With check_maps != 0 it also checks,
+ * for that geometry and the one-GPU one, that the image layout maps and
+ * their inverses are bijections onto every projection (the device re-layout
+ * gathers through them). 0, or -1 with gdn_last_error(). */
+int gdn_b200_test_image_geometry(uint32_t hidden, uint32_t intermediate, uint32_t vocab, uint32_t ncta,
+                                 uint32_t *geom, int check_maps);
+
 /* Reference-ABI compatibility for the run states created afterwards (also
  * GDN_B200_ABI_COMPAT=1 in the environment): gdn_run_state_init then builds
  * the reference's host images (32 packed shards with the BF16 state stripes,

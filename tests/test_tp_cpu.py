@@ -43,6 +43,54 @@ def test_owner_matches_the_kernel_partition(world):
         assert (np.diff(ranks) >= 0).all()
 
 
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_image_geometry_matches_the_library_and_its_maps_are_bijections(world):
+    """The tensor-parallel weight image's chunk geometry: the library's choice
+    (gdn_b200_test_image_geometry, host code only) equals the restatement in
+    tensor_parallel.image_geometry, every chunk fits a ring slot, and the
+    layout maps the device re-layout gathers through are bijections for that
+    geometry and the one-GPU one."""
+    import ctypes
+
+    import gateddeltanet_b200 as gdn
+    from gateddeltanet_b200 import build
+    build.build()
+    L = gdn.lib()
+    for dims in (FULL, SMALL):
+        grid = tp.tp_grid(dims, world, 148)
+        ncta = grid * world
+        geom = (ctypes.c_uint32 * 4)()
+        assert L.gdn_b200_test_image_geometry(dims["hidden"], dims["inter"], dims["vocab"], ncta, geom, 1) == 0, \
+            gdn.last_error()
+        got = tuple(geom)
+        assert got == tp.image_geometry(dims, ncta)
+        H = dims["hidden"]
+        g_qkvg, g_gu, g_lm, ng = got
+        for G in (g_qkvg, g_gu, g_lm):
+            assert (H // 64) % G == 0
+        assert ng % 8 == 0
+        for tiles, tile_rows, G in ((4 * H // 8, 8, g_qkvg), (2 * dims["inter"] // 16, 16, g_gu),
+                                    (dims["vocab"] // 16, 16, g_lm)):
+            assert min(tp.PASS_TILES, -(-tiles // ncta)) * G * tile_rows * 128 <= tp.SLOT_BYTES
+        assert -(-H // ncta) * min(ng, max(H, dims["inter"]) // 64) * 128 <= tp.SLOT_BYTES
+    # the one-GPU grid gives the one-GPU image; the measured tensor-parallel grids these
+    expect = {1: (4, 2, 2, 16), 2: (8, 4, 2, 32), 4: (16, 8, 4, 64), 8: (16, 16, 4, 80)}
+    assert tp.image_geometry(FULL, tp.tp_grid(FULL, world, 148) * world) == expect[world]
+
+
+def test_image_geometry_rejects_unsupported_sizes():
+    import ctypes
+
+    import gateddeltanet_b200 as gdn
+    from gateddeltanet_b200 import build
+    build.build()
+    L = gdn.lib()
+    geom = (ctypes.c_uint32 * 4)()
+    assert L.gdn_b200_test_image_geometry(2000, 5632, 32000, 296, geom, 0) == -1
+    assert "multiples of 512" in gdn.last_error()
+    assert L.gdn_b200_test_image_geometry(2048, 5632, 32000, 0, geom, 0) == -1
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_merge_state_takes_each_unit_from_its_owner(world):
     dims = SMALL
