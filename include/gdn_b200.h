@@ -196,7 +196,11 @@ int gdn_b200_grid_size(void);
  * does, gdn_b200_state_download, gdn_b200_state_save_file, gdn_b200_prefill
  * and (after gdn_b200_tp_detach) single-GPU decode return -1. The parts come
  * out through gdn_b200_tp_state_download_part; the Python layer's
- * tensor_parallel.merge_state joins them into the full state. */
+ * tensor_parallel.merge_state joins them into the full state.
+ * The first attach of a model for a given world * grid allocates, on this
+ * GPU, a copy of the weight image in that grid's chunk geometry (about the
+ * size of the weights; kept with the model, reused, freed with it); -1 if
+ * that allocation fails. */
 #define GDN_B200_TP_TOKEN_BYTES 128
 int gdn_b200_tp_token(GDNRunState *state, void *token);
 int gdn_b200_tp_attach(GDNRunState *state, int rank, int world, const void *tokens);
